@@ -1,0 +1,343 @@
+#!/usr/bin/env python3
+"""Benchmark of the decode hot path: batch-1 Llama-3.2-1B decode tok/s and % of the HBM roofline.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--dtype bf16|int8|int4]
+
+Workload (configs[1..2] are reported as extra precisions): seeded synthetic
+Llama-3.2-1B weights (cudallm_b200.synth), a 32-token random prompt, greedy decode, bf16 KV cache.
+A *step* is one decode token. After W untimed warm-up decode steps, the engine is reset, the prompt is
+stepped (untimed), and K decode steps (positions 32 .. 32+K-1) are timed with CUDA events on the
+engine's stream, bracketed by a barrier and a device synchronise. With N GPUs (torchrun, one process
+per GPU) every rank decodes its own sequence (replicas: the batch-1 path does not shard) and the value
+is N*K divided by the slowest rank's time.
+
+Reported (one JSON line on rank 0): value = tok/s with weights resident; e2e = tok/s through the C ABI
+when every step takes its token from the host and returns the next token to the host; roofline of the
+persistent decode-step kernel (algorithmic bytes = weight bytes + KV bytes read at the step's context,
+the reference's bytes-per-token count, cudallm_bench.cpp:82-87); cpu_baseline = the oracle's restatement
+of the reference's CPU model timed on a bounded sample. `--impl reference` times that CPU model alone.
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PROMPT_LEN = 32
+KV_BYTES_PER_TOKEN = 16 * 2 * 8 * 64 * 2  # layers * (K,V) * kv heads * head_dim * 2 bytes
+
+
+def log(msg: str) -> None:
+    print(msg, file=sys.stderr, flush=True)
+
+
+def dist_info() -> tuple[int, int, int]:
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def profiled_traffic(dtype: str) -> float | None:
+    """DRAM bytes per decode-step launch from the committed ncu summary, if one exists."""
+    p = ROOT / "profiles" / "decode_step_traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    v = d.get(dtype)
+    return float(v["dram_bytes_per_launch"]) if v else None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def __exit__(self, *exc):
+        self.out = ""
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                self.out, _ = self.proc.communicate()
+
+    def summary(self) -> dict:
+        rows = [r for r in csv.reader(io.StringIO(self.out or "")) if len(r) >= 9]
+        sm, smax, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for r in rows:
+            try:
+                sm.append(float(r[1]))
+                smax = max(smax, float(r[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, r[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": smax or None, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def time_decode(eng, prompt: list[int], steps: int, warmup: int, torch, barrier) -> dict:
+    """Device-timed decode steps on the engine's stream (weights resident, no host I/O per step)."""
+    stream = torch.cuda.ExternalStream(eng.stream_handle, device=torch.device("cuda", eng.device))
+    # Warm-up: a full prompt plus W decode steps, untimed.
+    eng.reset()
+    for t in prompt:
+        eng.step_async(t)
+    for _ in range(warmup):
+        eng.step_async(None)
+    eng.synchronize()
+    # Timed: reset, prompt (untimed), then K steps with per-launch events.
+    eng.reset()
+    for t in prompt:
+        eng.step_async(t)
+    eng.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    barrier()
+    torch.cuda.synchronize(eng.device)
+    for i in range(steps):
+        starts[i].record(stream)
+        eng.step_async(None)
+        ends[i].record(stream)
+    eng.synchronize()
+    torch.cuda.synchronize(eng.device)
+    barrier()
+    total_ms = starts[0].elapsed_time(ends[-1])
+    per = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    return {"total_ms": total_ms, "kernel_ms": per}
+
+
+def time_e2e(eng, prompt: list[int], steps: int, torch, barrier) -> dict:
+    """Same decode, each step through cudallm_step with the token from the host and the next token
+    read back to the host (synchronising call)."""
+    stream = torch.cuda.ExternalStream(eng.stream_handle, device=torch.device("cuda", eng.device))
+    eng.reset()
+    nxt = None
+    for t in prompt:
+        nxt, _ = eng.step(t)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize(eng.device)
+    t0 = time.perf_counter()
+    start.record(stream)
+    for _ in range(steps):
+        nxt, _ = eng.step(nxt)
+    end.record(stream)
+    torch.cuda.synchronize(eng.device)
+    wall = time.perf_counter() - t0
+    barrier()
+    return {"total_ms": start.elapsed_time(end), "wall_ms": wall * 1e3}
+
+
+def cpu_reference_tokps(path: Path, prompt: list[int], kv: str, n_prompt: int, n_decode: int,
+                        time_budget_s: float | None = None) -> dict:
+    """The oracle's restatement of the reference CPU model (per-call dequantisation, all host threads)."""
+    import torch
+    from oracle.refmodel import RefModel
+    ref = RefModel(path, kv_dtype=torch.float16 if kv == "fp16" else torch.bfloat16, cache_dense=False)
+    logits = None
+    for t in prompt[:n_prompt]:
+        logits, _ = ref.step(t)
+    t0 = time.perf_counter()
+    done = 0
+    for _ in range(n_decode):
+        logits, _ = ref.step(int(torch.argmax(logits)))
+        done += 1
+        if time_budget_s is not None and time.perf_counter() - t0 > time_budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"tok_s": done / dt, "steps": done, "seconds": dt, "threads": torch.get_num_threads()}
+
+
+def run_reference_arm(args) -> None:
+    rank, world, _ = dist_info()
+    if rank != 0:
+        return
+    from cudallm_b200 import synth
+    path, _ = synth.ensure_model(args.dtype, seed=0, max_seq_len=4096)
+    prompt = synth.prompt_ids(PROMPT_LEN, seed=0)
+    import torch
+    warm = cpu_reference_tokps(path, prompt, args.kv, n_prompt=4, n_decode=max(1, args.warmup))
+    del warm
+    r = cpu_reference_tokps(path, prompt, args.kv, n_prompt=8, n_decode=args.steps, time_budget_s=args.ref_budget_s)
+    cores = os.cpu_count()
+    line = {
+        "impl": "reference", "metric": metric_name(args.dtype), "value": r["tok_s"], "unit": "tok/s",
+        "n_gpus": world, "steps": r["steps"], "warmup": args.warmup, "ms_per_step": 1e3 / r["tok_s"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": args.dtype, "data": "synthetic",
+        "config": config_block(args),
+        "cpu_baseline": {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
+                         "sample": f"{r['steps']} greedy decode steps after an 8-token prefix of the prompt, "
+                                   f"{args.dtype} weights dequantised per call (reference.py:47-55), torch threads="
+                                   f"{r['threads']} of {cores} host cores"},
+        "e2e": {"value": r["tok_s"], "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    del torch
+    print(json.dumps(line), flush=True)
+
+
+def metric_name(dtype: str) -> str:
+    return f"bs1 decode tok/s ({dtype} weights), Llama-3.2-1B"
+
+
+def config_block(args) -> dict:
+    return {"workload": f"llama3.2-1b batch-1 greedy decode: prompt {PROMPT_LEN}, timed decode steps at positions "
+                        f"{PROMPT_LEN}..{PROMPT_LEN + args.steps - 1}, {args.dtype} weights, {args.kv} KV cache",
+            "model": "Llama-3.2-1B (seeded synthetic weights, N(0,0.02) bf16, seed 0)",
+            "global_batch": 1, "seq_len": PROMPT_LEN + args.steps, "parallelism": f"replicas x{dist_info()[1]}",
+            "l2": "inputs larger than L2: every step streams all weights (0.64-2.47 GB > 126 MB L2)",
+            "compute": f"{args.dtype} weights, fp32 activations and accumulation"}
+
+
+def run_ours(args) -> None:
+    rank, world, local_rank = dist_info()
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(minutes=10), device_id=torch.device("cuda", local_rank))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    from cudallm_b200 import synth
+    from cudallm_b200.engine import Engine
+    prompt = synth.prompt_ids(PROMPT_LEN, seed=0)
+    dtypes = [args.dtype] + ([d for d in ("int8", "int4") if d != args.dtype] if (world == 1 and not args.quick) else [])
+    results = {}
+    peaks = measured_peaks()
+    for dt in dtypes:
+        path, digest = synth.ensure_model(dt, seed=0, max_seq_len=4096)
+        barrier()
+        with Engine(path, kv_dtype=args.kv, device=local_rank) as eng:
+            assert eng.decode_path == "persistent"
+            weight_bytes = eng.config["weight_bytes"]
+            if dt == args.dtype:
+                with ClockSampler(local_rank) as clk:
+                    t = time_decode(eng, prompt, args.steps, args.warmup, torch, barrier)
+                clocks = clk.summary()
+                e = time_e2e(eng, prompt, args.steps, torch, barrier)
+            else:
+                t = time_decode(eng, prompt, args.steps, args.warmup, torch, barrier)
+                e, clocks = None, None
+        results[dt] = {"t": t, "e": e, "clocks": clocks, "weight_bytes": weight_bytes}
+
+    # Max over ranks of the timed-region durations.
+    def max_over_ranks(v: float) -> float:
+        if world == 1:
+            return v
+        x = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        return float(x.item())
+
+    head = results[args.dtype]
+    total_ms = max_over_ranks(head["t"]["total_ms"])
+    e2e_ms = max_over_ranks(head["e"]["total_ms"])
+    kernel_ms = head["t"]["kernel_ms"]
+    avg_kernel_ms = sum(kernel_ms) / len(kernel_ms)
+    avg_ctx = PROMPT_LEN + (args.steps + 1) / 2
+    bytes_per_step = head["weight_bytes"] + KV_BYTES_PER_TOKEN * avg_ctx
+    achieved = bytes_per_step / (avg_kernel_ms * 1e-3) / 1e9
+    extra = {}
+    for dt, r in results.items():
+        ms = r["t"]["total_ms"]
+        kms = sum(r["t"]["kernel_ms"]) / len(r["t"]["kernel_ms"])
+        b = r["weight_bytes"] + KV_BYTES_PER_TOKEN * avg_ctx
+        extra[dt] = {"tok_s": args.steps / (ms * 1e-3), "bytes_per_token": int(b),
+                     "roofline_frac": (b / (kms * 1e-3) / 1e9) / peaks["hbm_gbs"],
+                     "achieved_gbs": b / (kms * 1e-3) / 1e9, "ms_per_token": ms / args.steps}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        path, _ = synth.ensure_model(args.dtype, seed=0, max_seq_len=4096)
+        r = cpu_reference_tokps(path, prompt, args.kv, n_prompt=4, n_decode=8, time_budget_s=25.0)
+        cpu = {"value": r["tok_s"], "unit": "tok/s", "cores": r["threads"], "kind": "port",
+               "sample": f"{r['steps']} greedy decode steps after a 4-token prefix of the prompt, {args.dtype} "
+                         f"weights dequantised per call as reference.py:47-55 does, torch threads={r['threads']}"}
+
+    if world > 1:
+        dist.barrier()
+    if rank == 0:
+        value = world * args.steps / (total_ms * 1e-3)
+        line = {
+            "metric": metric_name(args.dtype), "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": total_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": args.dtype, "data": "synthetic", "config": config_block(args),
+            "e2e": {"value": world * args.steps / (e2e_ms * 1e-3), "unit": "tok/s", "h2d_bytes_per_step": 4,
+                    "d2h_bytes_per_step": 16},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved / peaks["hbm_gbs"], "traffic": profiled_traffic(args.dtype),
+                         "kernel": "decode_step_kernel (one persistent launch per token)",
+                         "peak_source": f"{peaks['source']} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)",
+                         "algorithmic_bytes_per_launch": int(bytes_per_step)},
+            "cpu_baseline": cpu,
+            "gpu_launches": args.steps,
+            "clocks": head["clocks"],
+            "precisions": extra,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=256)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--dtype", choices=("bf16", "int8", "int4"), default="bf16")
+    ap.add_argument("--kv", choices=("fp16", "bf16"), default="bf16")
+    ap.add_argument("--quick", action="store_true", help="headline precision only")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ref-budget-s", type=float, default=120.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if PROMPT_LEN + args.steps > 4096:
+        raise SystemExit("--steps too large for max_seq_len 4096")
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,86 @@
+// Persistent decode-step kernel: one cooperative launch computes a whole Llama-3.2-1B token step
+// (embedding -> 16 x [QKV, RoPE + KV write + split-K GQA attention, O proj + residual, RMSNorm +
+// gate/up + SwiGLU, down + residual] -> final RMSNorm + tied lm_head -> argmax) on one CTA per SM.
+// It replaces the 116-launch graph of wasiqnauman/cudallm src/engine/engine.cpp:181-237 for the
+// fused opt/opt path.
+//
+// Inside the kernel, warp 0 of every CTA streams that CTA's share of every weight matrix, in use
+// order, through a ring of shared-memory stages with bulk (TMA) copies, and prefetches the head of
+// the next operation into L2; it never waits for activations, so HBM keeps streaming while the 8
+// consumer warps wait on inter-CTA dependencies. Dependencies are monotonic per-step counters in
+// global memory (release add / acquire load), every wait is bounded by a wall-clock limit after
+// which the kernel records an error code and exits cleanly, and the last CTA to finish the lm_head
+// reduces the argmax, advances the device position and zeroes the counters for the next step.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "common/dtype.h"
+#include "kernels/kernels.h"
+
+namespace cudallm {
+
+struct StepLayer {
+    const float* attn_norm;
+    const void* wqkv;
+    const void* sqkv;
+    const void* wo;
+    const void* so;
+    const float* ffn_norm;
+    const void* wgu;
+    const void* sgu;
+    const void* wdown;
+    const void* sdown;
+};
+
+constexpr int kStepLayers = 16;
+
+// Device error word layout (err[0] = flags, err[1] = id of the first wait that gave up).
+constexpr unsigned kErrWaitTimeout = 1u;
+constexpr unsigned kErrAborted = 2u;
+
+// Counters the step uses (zeroed at creation, after an error and by the step itself at its end).
+constexpr int kSyncQkv = 0, kSyncAtt = 16, kSyncWo = 32, kSyncGu = 48, kSyncDown = 64, kSyncTicket = 80,
+              kSyncLm = 80 + 16 * 8, kSyncWords = 256;
+
+struct StepParams {
+    StepLayer layers[kStepLayers];
+    const void* emb_w;
+    const void* emb_s;
+    const float* final_norm;
+    const float* inv_freq;
+    float* x;       // [2048] residual stream
+    float* qkv;     // [3072]
+    float* att;     // [2048]
+    float* act;     // [8192]
+    float* logits;  // [128256]
+    void* k_cache;  // [16][8][max_seq][64]
+    void* v_cache;
+    float* part_o;   // [32][max_seq/64][64]
+    float* part_ml;  // [32][max_seq/64][2]
+    float* am_v;     // [grid]
+    int* am_i;       // [grid]
+    int* d_token;
+    int* d_pos;
+    unsigned* sync;  // [kSyncWords]
+    unsigned* err;   // [2]
+    float* debug_res;  // [(16+1)][2048] or null
+    int token_override;  // >= 0: feed this token instead of *d_token
+    int max_seq;
+    float eps;
+    int group_size;
+    unsigned long long wait_limit_ns;
+    TileGeom g_qkv, g_wo, g_gu, g_down, g_lm;
+};
+
+// Shared memory bytes of one CTA of the persistent kernel.
+int decode_step_smem_bytes();
+// Prepares (once per device) and launches one step on `stream` as a cooperative launch with one CTA
+// per SM. Throws if the device cannot hold the grid.
+void launch_decode_step(const StepParams& p, WeightType wt, KvType kv, cudaStream_t stream);
+// Grid size the launch uses (the number of SMs).
+int decode_step_grid();
+
+}  // namespace cudallm

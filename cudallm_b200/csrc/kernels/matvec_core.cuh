@@ -1,0 +1,246 @@
+// Device building blocks of every weight matvec (per-op stream kernel and persistent decode step).
+//
+// Work unit: a *tile* = up to R consecutive weight rows x one row segment, fetched by a single bulk
+// copy (two for SWIGLU: R gate rows then the R matching up rows) into one 16 KiB shared-memory stage.
+// One warp consumes a tile: lane l owns the 16-byte chunks l, l+32, l+64, ... of every row, so the
+// per-row accumulation order (and therefore every result bit) is independent of the tile shape, the
+// grid and the kernel that runs it.
+//
+// The input vector is staged once per operation into shared memory as "planes": float4 p of chunk c
+// is stored at plane p, slot c, so the 32 lanes of a warp read 32 consecutive float4 (no bank
+// conflicts) and each float4 lines up with the lanes' in-register weight unpacking:
+//   bf16: 8 cols/chunk, word k = cols (2k, 2k+1)            -> planes hold cols 0-3, 4-7
+//   int8: 16 cols/chunk, word k = cols 4k..4k+3             -> plane k = cols 4k..4k+3
+//   int4: 32 cols/chunk, word k byte b = cols 8k+2b (low nibble), 8k+2b+1 (high nibble)
+//         -> plane 2k = even cols 8k+{0,2,4,6}, plane 2k+1 = odd cols 8k+{1,3,5,7}
+// Dequantisation follows the reference formats (wasiqnauman/cudallm python/cudallm/quantize.py:5-29,
+// src/kernels/matvec_opt.cu:65-115) but not its arithmetic:
+//   int8: q = byte value, one fp32 scale per row applied after the row reduction.
+//   int4: a nibble n is placed in mantissa bits 16..19 of 0.5f by one PRMT, giving f = 0.5 + n/256;
+//         per 32-column chunk sum_i q_i x_i = 256 * sum_i f_i x_i - 136 * sum_i x_i (q = n - 8), where
+//         sum_i x_i of the chunk is precomputed while staging. Two instructions per weight.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <cstdint>
+
+#include "common/dtype.h"
+#include "kernels/kernels.h"
+
+namespace cudallm {
+
+template <WeightType WT>
+struct Chunk;
+template <>
+struct Chunk<WeightType::BF16> {
+    static constexpr int kCols = 8, kPlanes = 2;
+};
+template <>
+struct Chunk<WeightType::INT8> {
+    static constexpr int kCols = 16, kPlanes = 4;
+};
+template <>
+struct Chunk<WeightType::INT4> {
+    static constexpr int kCols = 32, kPlanes = 8;
+};
+
+// Float offset of column j inside the plane layout (nc = number of chunks of the vector).
+template <WeightType WT>
+__device__ __forceinline__ int plane_offset(int j, int nc) {
+    constexpr int C = Chunk<WT>::kCols;
+    const int c = j / C;
+    const int i = j % C;
+    int plane, comp;
+    if constexpr (WT == WeightType::INT4) {
+        const int k = i >> 3, e = i & 7;
+        plane = 2 * k + (e & 1);
+        comp = e >> 1;
+    } else {
+        plane = i >> 2;
+        comp = i & 3;
+    }
+    return (plane * nc + c) * 4 + comp;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); }
+
+// Stages `src(j)` (optionally RMS-normalised with gain norm_w) for j < K into planes `xp`, and for
+// int4 the per-chunk sums into `xc`. Runs on `nthr` threads with index tid (nthr == 256 in every
+// caller, which fixes the sum-of-squares order). `sync()` is a barrier over those threads;
+// `red` is 32 floats of scratch.
+template <WeightType WT, typename Src, typename Sync>
+__device__ __forceinline__ void stage_vector(Src src, int K, const float* __restrict__ norm_w, float eps, float* xp,
+                                             float* xc, float* red, int tid, int nthr, Sync sync) {
+    constexpr int C = Chunk<WT>::kCols;
+    const int nc = K / C;
+    float inv = 1.f;
+    if (norm_w != nullptr) {
+        float ss = 0.f;
+        for (int j = tid; j < K; j += nthr) {
+            const float v = src(j);
+            ss = fmaf(v, v, ss);
+        }
+        ss = warp_sum(ss);
+        if ((tid & 31) == 0) red[tid >> 5] = ss;
+        sync();
+        if (tid < 32) {
+            float t = (tid < nthr / 32) ? red[tid] : 0.f;
+            t = warp_sum(t);
+            if (tid == 0) red[0] = t;
+        }
+        sync();
+        inv = rsqrtf(red[0] / static_cast<float>(K) + eps);
+    }
+    for (int j = tid; j < K; j += nthr) {
+        float v = src(j);
+        if (norm_w != nullptr) v = v * inv * __ldg(norm_w + j);
+        xp[plane_offset<WT>(j, nc)] = v;
+    }
+    sync();
+    if constexpr (WT == WeightType::INT4) {
+        const float4* p4 = reinterpret_cast<const float4*>(xp);
+        for (int c = tid; c < nc; c += nthr) {
+            float s = 0.f;
+#pragma unroll
+            for (int p = 0; p < Chunk<WT>::kPlanes; ++p) {
+                const float4 v = p4[p * nc + c];
+                s += v.x + v.y + v.z + v.w;
+            }
+            xc[c] = s;
+        }
+        sync();
+    }
+}
+
+__device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// int8: biased byte (q + 128) in the mantissa of 2^23, minus 2^23 + 128 -> q (exact).
+__device__ __forceinline__ float i8val(uint32_t wb, uint32_t sel) {
+    return __uint_as_float(__byte_perm(wb, 0x4B000000u, sel)) - 8388736.f;
+}
+// int4: nibble n (already isolated in byte b) -> 0.5 + n/256.
+__device__ __forceinline__ float i4half(uint32_t v, uint32_t sel) { return __uint_as_float(__byte_perm(v, 0x3F000000u, sel)); }
+
+// Rows held by one stage: rows [0, nr) are r0.., rows [nr, 2nr) (SWIGLU only) are r0+up_off...
+struct StageRows {
+    int r0, nr, n, up_off;
+    __device__ __forceinline__ int global_row(int i) const { return i < nr ? r0 + i : r0 + (i - nr) + up_off; }
+};
+
+// Accumulates one tile (rows x one segment) into acc[0..n). MAXN bounds n at compile time so the
+// accumulators stay in registers.
+template <WeightType WT, int MAXN>
+__device__ __forceinline__ void tile_accumulate(const uint8_t* stage, const StageRows& sr, int seg_bytes, int seg_chunk0,
+                                                const float* xp, int nc, const float* xc, const void* scales, int K,
+                                                float (&acc)[MAXN], int lane) {
+    const float4* p4 = reinterpret_cast<const float4*>(xp);
+    const int cpl = seg_bytes >> 9;  // chunks per lane per row (segment bytes / (32 lanes * 16 B))
+    [[maybe_unused]] const int groups = K >> 7;
+    for (int j = 0; j < cpl; ++j) {
+        const int c = lane + 32 * j;
+        const int gc = seg_chunk0 + c;
+        if constexpr (WT == WeightType::BF16) {
+            const float4 x0 = p4[gc], x1 = p4[nc + gc];
+#pragma unroll
+            for (int i = 0; i < MAXN; ++i) {
+                if (i < sr.n) {
+                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                    float a = acc[i];
+                    a = fmaf(bf16lo(w.x), x0.x, a);
+                    a = fmaf(bf16hi(w.x), x0.y, a);
+                    a = fmaf(bf16lo(w.y), x0.z, a);
+                    a = fmaf(bf16hi(w.y), x0.w, a);
+                    a = fmaf(bf16lo(w.z), x1.x, a);
+                    a = fmaf(bf16hi(w.z), x1.y, a);
+                    a = fmaf(bf16lo(w.w), x1.z, a);
+                    a = fmaf(bf16hi(w.w), x1.w, a);
+                    acc[i] = a;
+                }
+            }
+        } else if constexpr (WT == WeightType::INT8) {
+            const float4 x0 = p4[gc], x1 = p4[nc + gc], x2 = p4[2 * nc + gc], x3 = p4[3 * nc + gc];
+#pragma unroll
+            for (int i = 0; i < MAXN; ++i) {
+                if (i < sr.n) {
+                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                    const uint32_t b0 = w.x ^ 0x80808080u, b1 = w.y ^ 0x80808080u, b2 = w.z ^ 0x80808080u,
+                                   b3 = w.w ^ 0x80808080u;
+                    float a = acc[i];
+                    a = fmaf(i8val(b0, 0x7540), x0.x, a);
+                    a = fmaf(i8val(b0, 0x7541), x0.y, a);
+                    a = fmaf(i8val(b0, 0x7542), x0.z, a);
+                    a = fmaf(i8val(b0, 0x7543), x0.w, a);
+                    a = fmaf(i8val(b1, 0x7540), x1.x, a);
+                    a = fmaf(i8val(b1, 0x7541), x1.y, a);
+                    a = fmaf(i8val(b1, 0x7542), x1.z, a);
+                    a = fmaf(i8val(b1, 0x7543), x1.w, a);
+                    a = fmaf(i8val(b2, 0x7540), x2.x, a);
+                    a = fmaf(i8val(b2, 0x7541), x2.y, a);
+                    a = fmaf(i8val(b2, 0x7542), x2.z, a);
+                    a = fmaf(i8val(b2, 0x7543), x2.w, a);
+                    a = fmaf(i8val(b3, 0x7540), x3.x, a);
+                    a = fmaf(i8val(b3, 0x7541), x3.y, a);
+                    a = fmaf(i8val(b3, 0x7542), x3.z, a);
+                    a = fmaf(i8val(b3, 0x7543), x3.w, a);
+                    acc[i] = a;
+                }
+            }
+        } else {
+            const float xsum = xc[gc];
+            const int g = gc >> 2;  // 128-column group of this chunk
+            const __half* sc = static_cast<const __half*>(scales);
+#pragma unroll
+            for (int i = 0; i < MAXN; ++i) {
+                if (i < sr.n) {
+                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                    const float s = __half2float(__ldg(sc + static_cast<size_t>(sr.global_row(i)) * groups + g));
+                    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+                    float p = 0.f;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const float4 xe = p4[(2 * k) * nc + gc];
+                        const float4 xo = p4[(2 * k + 1) * nc + gc];
+                        const uint32_t lo = words[k] & 0x0F0F0F0Fu;
+                        const uint32_t hi = (words[k] >> 4) & 0x0F0F0F0Fu;
+                        p = fmaf(i4half(lo, 0x7044), xe.x, p);
+                        p = fmaf(i4half(lo, 0x7144), xe.y, p);
+                        p = fmaf(i4half(lo, 0x7244), xe.z, p);
+                        p = fmaf(i4half(lo, 0x7344), xe.w, p);
+                        p = fmaf(i4half(hi, 0x7044), xo.x, p);
+                        p = fmaf(i4half(hi, 0x7144), xo.y, p);
+                        p = fmaf(i4half(hi, 0x7244), xo.z, p);
+                        p = fmaf(i4half(hi, 0x7344), xo.w, p);
+                    }
+                    acc[i] = fmaf(s, fmaf(256.f, p, -136.f * xsum), acc[i]);
+                }
+            }
+        }
+    }
+}
+
+// Row result after the warp reduction (all lanes hold it); int8 applies its per-row scale here.
+template <WeightType WT>
+__device__ __forceinline__ float finish_row(float reduced, const void* scales, int global_row) {
+    if constexpr (WT == WeightType::INT8) {
+        return reduced * __ldg(static_cast<const float*>(scales) + global_row);
+    } else {
+        return reduced;
+    }
+}
+
+}  // namespace cudallm

@@ -1,0 +1,134 @@
+/*
+ * cudallm.h: C ABI of the B200 (sm_100a) Llama-3.2-1B decode engine.
+ *
+ * Drop-in replacement for wasiqnauman/cudallm's include/cudallm/cudallm.h:1-62. Every symbol, struct
+ * layout, return code and ownership rule of that header is kept, so its ctypes wrapper
+ * (python/cudallm/engine.py:39-66) and its tests bind this library unchanged when CUDALLM_LIB points
+ * at it. Entry points after the "additive" marker are new and change none of the originals.
+ *
+ * Conventions (reference src/capi/cudallm_capi.cpp:24-44): every entry point returns a CUDALLM_*
+ * code (except destroy / default_options / pos / last_error); no C++ exception crosses the ABI;
+ * the message of the last failure on the calling thread is returned by cudallm_last_error().
+ * One engine per thread; engines own all device memory, callers own all host buffers.
+ */
+#ifndef CUDALLM_B200_CUDALLM_H
+#define CUDALLM_B200_CUDALLM_H
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Return codes: reference include/cudallm/cudallm.h:8-14. */
+#define CUDALLM_OK 0
+#define CUDALLM_ERR_INVALID_ARG 1
+#define CUDALLM_ERR_IO 2
+#define CUDALLM_ERR_FORMAT 3
+#define CUDALLM_ERR_CUDA 4
+#define CUDALLM_ERR_STATE 5
+#define CUDALLM_ERR_INTERNAL 6
+
+typedef struct cudallm_engine cudallm_engine;
+
+/* Engine options, 24 bytes: reference include/cudallm/cudallm.h:18-25.
+ * matvec_impl/attn_impl: 0 naive, 1 opt. fuse: 1 selects the fused decode path (the persistent
+ * decode-step kernel when matvec and attention are both opt). cuda_graph: replay the step as a CUDA
+ * graph. max_seq_len: 0 = the file header's value, else a positive multiple of 128 not above it.
+ * matvec_rpb: 0 = default, else 1, 2, 4 or 8 = the most weight rows a consumer warp takes per tile. */
+typedef struct {
+    int matvec_impl;
+    int attn_impl;
+    int fuse;
+    int cuda_graph;
+    int max_seq_len;
+    int matvec_rpb;
+} cudallm_options;
+
+/* Model description: reference include/cudallm/cudallm.h:27-32. weight_bytes = sum of the nbytes of
+ * every tensor in the file, each counted once (the bytes one decode step streams). */
+typedef struct {
+    int weight_dtype; /* 1 bf16, 3 int8, 4 int4 */
+    int hidden, inter, n_layers, n_heads, n_kv_heads, head_dim, vocab, max_seq_len, group_size;
+    float rms_eps;
+    unsigned long long weight_bytes;
+} cudallm_config_info;
+
+/* Replaces reference cudallm.h:34 (thread-local message of the last failure). */
+const char* cudallm_last_error(void);
+/* Replaces reference cudallm.h:35: fills opt, opt, fuse 1, graph 1, 0, 0. */
+void cudallm_default_options(cudallm_options* out);
+/* Replaces reference cudallm.h:36: loads a .cudallm file; *out = NULL on failure. */
+int cudallm_create(const char* path, const cudallm_options* opts, cudallm_engine** out);
+/* Replaces reference cudallm.h:37; NULL-safe. */
+void cudallm_destroy(cudallm_engine* e);
+/* Replaces reference cudallm.h:38. */
+int cudallm_get_config(cudallm_engine* e, cudallm_config_info* out);
+/* Replaces reference cudallm.h:39: position back to 0 (KV contents are overwritten as it advances). */
+int cudallm_reset(cudallm_engine* e);
+/* Replaces reference cudallm.h:40: host mirror of the position; -1 for a NULL engine. */
+int cudallm_pos(cudallm_engine* e);
+/* Replaces reference cudallm.h:41. token >= 0 is fed; -1 feeds the previous step's device argmax.
+ * logits_out: host [vocab] or NULL; next_token_out: host or NULL. With both NULL the call does not
+ * synchronise (steps queue asynchronously on the engine's stream). */
+int cudallm_step(cudallm_engine* e, int token, float* logits_out, int* next_token_out);
+/* Replaces reference cudallm.h:42. Never uses a CUDA graph; residuals_out: host [(n_layers+1)*hidden],
+ * the residual stream after the embedding and after each layer. */
+int cudallm_step_debug(cudallm_engine* e, int token, float* residuals_out, float* logits_out, int* next_token_out);
+
+/* ---- single-kernel test hooks: host pointers in/out; each call allocates, uploads, runs on the
+ * default stream, synchronises, downloads and frees (reference cudallm.h:44-56, cudallm_capi.cpp:179-316). */
+
+/* Replaces reference cudallm.h:45-48. impl 0 naive (bf16, STORE, no norm), 1 opt. weight_dtype 1/3/4;
+ * epilogue 0 STORE, 1 ADD (y += W x), 2 SWIGLU (y[r] = silu(g_r) u_r, rows/2 outputs). */
+int cudallm_kernel_matvec(int impl, int weight_dtype, int epilogue, int fuse_norm, int rpb,
+                          const void* w, unsigned long long w_bytes, const void* scales, unsigned long long scales_bytes,
+                          const float* x, const float* norm_w, float eps,
+                          float* y /* in/out (ADD reads it) */, int rows, int cols);
+/* Replaces reference cudallm.h:49. */
+int cudallm_kernel_rmsnorm(const float* x, const float* w, float eps, float* y, int n);
+/* Replaces reference cudallm.h:50-52. Caches are fp16 bits [nkv][max_seq][hd]. */
+int cudallm_kernel_rope_kv(int fused, float* qkv /* in/out */, const float* inv_freq, int pos,
+                           unsigned short* k_cache, unsigned short* v_cache, int nh, int nkv, int hd, int max_seq);
+/* Replaces reference cudallm.h:53-54. impl 1 requires max_seq % 128 == 0, nh == 4*nkv, hd == 64. */
+int cudallm_kernel_attention(int impl, const float* q, const unsigned short* k_cache, const unsigned short* v_cache,
+                             int ctx, float* out, int nh, int nkv, int hd, int max_seq);
+/* Replaces reference cudallm.h:55. */
+int cudallm_kernel_silu_mul(const float* gu, float* act, int inter);
+/* Replaces reference cudallm.h:56. Lowest index wins ties. */
+int cudallm_kernel_argmax(const float* logits, int n, int* out_idx);
+
+/* ================================ additive (no counterpart in the reference ABI) ================ */
+
+#define CUDALLM_KV_FP16 0
+#define CUDALLM_KV_BF16 1
+
+#define CUDALLM_PATH_AUTO 0       /* persistent decode-step kernel when fuse=1 and both impls are opt */
+#define CUDALLM_PATH_PERSISTENT 1 /* force the persistent decode-step kernel (needs fuse=1, opt/opt) */
+#define CUDALLM_PATH_PER_OP 2     /* one kernel per operation, as the reference sequences them */
+
+/* Extended creation options. struct_size must be sizeof(cudallm_options_ex). */
+typedef struct {
+    int struct_size;
+    int kv_dtype; /* CUDALLM_KV_FP16 (reference default, engine.cpp:51-52) or CUDALLM_KV_BF16 */
+    int device;   /* CUDA device ordinal; -1 = the calling thread's current device */
+    int path;     /* CUDALLM_PATH_* */
+    int reserved[4];
+} cudallm_options_ex;
+
+/* Fills kv fp16, device -1, path auto. */
+void cudallm_default_options_ex(cudallm_options_ex* out);
+/* cudallm_create with extended options (ex may be NULL = defaults). */
+int cudallm_create_ex(const char* path, const cudallm_options* opts, const cudallm_options_ex* ex, cudallm_engine** out);
+/* Waits for every queued step; reports a device-side failure (e.g. a timed-out inter-block wait). */
+int cudallm_synchronize(cudallm_engine* e);
+/* Which decode path the engine runs: CUDALLM_PATH_PERSISTENT or CUDALLM_PATH_PER_OP. */
+int cudallm_engine_path(cudallm_engine* e);
+/* The engine's CUDA stream (a cudaStream_t) and device, so callers can order or time work against the
+ * steps it enqueues; NULL / -1 for a NULL engine. */
+void* cudallm_engine_stream(cudallm_engine* e);
+int cudallm_engine_device(cudallm_engine* e);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUDALLM_B200_CUDALLM_H */
