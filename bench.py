@@ -211,6 +211,25 @@ def run_reference_arm(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def max_over_ranks(v: float) -> float:
+    """Largest value over all ranks (device tensor under NCCL, host tensor under gloo)."""
+    import torch
+    import torch.distributed as dist
+    if not dist.is_initialized() or dist.get_world_size() == 1:
+        return v
+    dev = "cuda" if dist.get_backend() == "nccl" else "cpu"
+    x = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(x, op=dist.ReduceOp.MAX)
+    return float(x.item())
+
+
+def aggregate_tok_s(per_rank_ms: float, steps: int) -> float:
+    """Whole-job tok/s: every rank decodes `steps` tokens; the job takes as long as the slowest rank."""
+    import torch.distributed as dist
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    return world * steps / (max_over_ranks(per_rank_ms) * 1e-3)
+
+
 def metric_name(dtype: str) -> str:
     return f"bs1 decode tok/s ({dtype} weights), Llama-3.2-1B"
 
@@ -258,14 +277,6 @@ def run_ours(args) -> None:
                 t = time_decode(eng, prompt, args.steps, args.warmup, torch, barrier)
                 e, clocks = None, None
         results[dt] = {"t": t, "e": e, "clocks": clocks, "weight_bytes": weight_bytes}
-
-    # Max over ranks of the timed-region durations.
-    def max_over_ranks(v: float) -> float:
-        if world == 1:
-            return v
-        x = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(x, op=dist.ReduceOp.MAX)
-        return float(x.item())
 
     head = results[args.dtype]
     total_ms = max_over_ranks(head["t"]["total_ms"])
