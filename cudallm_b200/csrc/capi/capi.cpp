@@ -238,6 +238,23 @@ int cudallm_engine_device(cudallm_engine* e) {
     return e->impl->device();
 }
 
+int cudallm_debug_trace(cudallm_engine* e, int enable) {
+    return guarded([&] {
+        require(e && e->impl, "cudallm_debug_trace: null engine");
+        e->impl->set_trace(enable != 0);
+    });
+}
+
+int cudallm_debug_read_trace(cudallm_engine* e, unsigned long long* out, unsigned long long count, int* grid_out,
+                             int* slots_out) {
+    return guarded([&] {
+        require(e && e->impl && out, "cudallm_debug_read_trace: null argument");
+        e->impl->read_trace(out, static_cast<size_t>(count));
+        if (grid_out) *grid_out = e->impl->trace_grid();
+        if (slots_out) *slots_out = cudallm::kTraceSlots;
+    });
+}
+
 int cudallm_kernel_matvec(int impl, int weight_dtype, int epilogue, int fuse_norm, int rpb, const void* w,
                           unsigned long long w_bytes, const void* scales, unsigned long long scales_bytes, const float* x,
                           const float* norm_w, float eps, float* y, int rows, int cols) {

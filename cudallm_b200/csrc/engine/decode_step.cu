@@ -19,10 +19,13 @@ namespace {
 
 constexpr int kCw = 8;             // consumer warps
 constexpr int kCt = 32 * kCw;      // consumer threads
-constexpr int kThreads = 32 + kCt; // + one producer warp
-constexpr int kStages = 11;
+constexpr int kThreads = 64 + kCt; // + copy-producer warp + L2-prefetch warp
+constexpr int kStages = 12;
+// Producer lanes: lane j of warp 0 issues the tiles t with t % kProducers == j, i.e. it owns the stages
+// s with s % kProducers == j, so four issue loops (each ~0.2-0.5 us per copy) run concurrently.
+constexpr int kProducers = 4;
+static_assert(kStages % kProducers == 0, "each stage must belong to one producer lane");
 constexpr int kMaxK = 8192;
-constexpr int kPrefetchBytes = 192 * 1024;
 constexpr int kOpsPerLayer = 4;
 constexpr int kWeightOps = kStepLayers * kOpsPerLayer + 1;  // + tied lm_head
 constexpr int kH = 2048, kNh = 32, kNkv = 8;
@@ -33,11 +36,12 @@ struct Flags {
     int abort;
     int ok;
     int role;
-    int pad;
+    int issued;  // tiles the copy producer has issued (read by the prefetch warp)
 };
 
 // Shared-memory layout (byte offsets).
 constexpr int kOffBars = 0;
+constexpr int kOffTiles = 2 * kStages * 8;  // int per stage: tile the producer last issued into it
 constexpr int kOffFlags = 256;
 constexpr int kOffRed = 384;
 constexpr int kOffCs = 512;
@@ -47,11 +51,34 @@ constexpr int kOffXc = 2048;
 constexpr int kOffXp = 3072;
 constexpr int kOffRing = kOffXp + kMaxK * 4;  // 35840
 constexpr int kSmemBytes = kOffRing + kStages * kStageBytes;
-static_assert(2 * kStages * 8 <= kOffFlags, "barriers overflow");
+static_assert(kOffTiles + kStages * 4 <= kOffFlags, "barriers overflow");
 static_assert(kOffAm + kCw * 8 <= kOffXc, "argmax scratch overflow");
 static_assert(kOffXc + (kMaxK / 32) * 4 <= kOffXp, "chunk sums overflow");
 static_assert(sizeof(AttSmem<__half>) <= kMaxK * 4, "attention scratch must fit in the vector area");
+static_assert(sizeof(HeadSmem<__half>) <= kMaxK * 4, "attention scratch must fit in the vector area");
+// Contexts up to this many 64-token tiles use the whole-head attention (one CTA per KV head).
+constexpr int kWholeHeadMaxTiles = 16;
 static_assert(kOffRing % 128 == 0, "ring alignment");
+
+// Stage rows of each operation's tile (rows per tile x halves); the host builds the persistent path's
+// geometry with the same rule (make_tile_geom with the default tile rows), checked at run time.
+template <WeightType WT>
+constexpr int weight_row_bytes(int k) {
+    return WT == WeightType::BF16 ? 2 * k : (WT == WeightType::INT8 ? k : k / 2);
+}
+// Chunks per lane of one row segment (the whole row: every Llama operation has n_seg == 1).
+template <WeightType WT, int KIND>
+constexpr int seg_chunks_per_lane() {
+    return weight_row_bytes<WT>(KIND == 3 ? 4 * 2048 : 2048) / 512;
+}
+
+template <WeightType WT, int KIND>
+constexpr int stage_rows() {
+    constexpr int halves = KIND == 2 ? 2 : 1;  // gate/up
+    constexpr int rb = weight_row_bytes<WT>(KIND == 3 ? 4 * 2048 : 2048);  // down has K = 8192
+    constexpr int fit = kStageBytes / halves / rb;
+    return (fit < kMaxTileRows ? fit : kMaxTileRows) * halves;
+}
 
 struct WOp {
     const uint8_t* w;
@@ -78,6 +105,22 @@ __device__ __forceinline__ void split_rows(int n, int& lo, int& hi) {
 __device__ __forceinline__ int op_tiles(const TileGeom& g, int lo, int hi) {
     const int R = g.rows_per_tile;
     return ((hi - lo + R - 1) / R) * g.n_seg;
+}
+
+__device__ __forceinline__ void trace_mark(const StepParams& p, int op, int slot) {
+    if (p.trace) p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + op * 4 + slot] = global_ns();
+}
+
+__device__ __forceinline__ void trace_tile(const StepParams& p, int o, int i, int slot) {
+    if (p.trace && blockIdx.x == 0 && o == kWeightOps - 1 && i < kTraceTiles) {
+        p.trace[static_cast<size_t>(gridDim.x) * kTraceSlots + i * kTraceTileStamps + slot] = global_ns();
+    }
+}
+
+__device__ __forceinline__ int trace_op_of_weight_op(int o) {
+    if (o == kWeightOps - 1) return 80;
+    const int l = o / kOpsPerLayer, k = o % kOpsPerLayer;
+    return l * 5 + (k == kQkv ? 0 : k + 1);
 }
 
 __device__ __forceinline__ void fail(const StepParams& p, volatile Flags* fl, unsigned code, unsigned id) {
@@ -109,12 +152,14 @@ __device__ bool spin_until(const StepParams& p, const unsigned* ctr, unsigned ta
     }
 }
 
-// Bounded wait on an mbarrier phase; also gives up when the CTA aborts (check_abort).
+// Bounded wait on an mbarrier phase; also gives up when the CTA aborts (check_abort). With
+// `tile_word`, first waits until the producer has published tile `tile` into the stage (a parity wait
+// only distinguishes the barrier's current and previous phase; a consumer warp can be further ahead).
 __device__ bool wait_bar(const StepParams& p, uint64_t* bar, uint32_t parity, volatile Flags* fl, bool check_abort,
-                         unsigned id) {
+                         unsigned id, const volatile int* tile_word = nullptr, int tile = 0) {
     uint64_t t0 = 0;
     for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if ((tile_word == nullptr || *tile_word == tile) && mbar_try_wait(bar, parity)) return true;
         if ((it & 63) == 0) {
             if (check_abort && fl->abort) return false;
             const uint64_t t = global_ns();
@@ -128,19 +173,23 @@ __device__ bool wait_bar(const StepParams& p, uint64_t* bar, uint32_t parity, vo
     }
 }
 
-__device__ void prefetch_head(const StepParams& p, int o) {
-    const WOp op = weight_op(p, o);
-    int lo, hi;
-    split_rows(op.g.out_rows, lo, hi);
-    const size_t slice = static_cast<size_t>(hi - lo) * op.g.row_bytes;
-    const size_t want = min(slice, static_cast<size_t>(kPrefetchBytes / op.g.halves));
-    for (int h = 0; h < op.g.halves; ++h) {
-        const uint8_t* base = op.w + (static_cast<size_t>(lo) + static_cast<size_t>(h) * op.g.out_rows) * op.g.row_bytes;
-        for (size_t off = 0; off < want; off += 32768) {
-            bulk_prefetch_l2(base + off, static_cast<uint32_t>(min(static_cast<size_t>(32768), want - off)));
+// Cursor over this CTA's tiles of the whole step (operation by operation).
+struct TileCursor {
+    int o = 0, i = 0, nt = 0, lo = 0, hi = 0;
+    WOp op;
+    __device__ void load(const StepParams& p) {
+        op = weight_op(p, o);
+        split_rows(op.g.out_rows, lo, hi);
+        nt = op_tiles(op.g, lo, hi);
+        i = 0;
+    }
+    __device__ bool valid() const { return o < kWeightOps; }
+    __device__ void next(const StepParams& p) {
+        if (++i >= nt) {
+            if (++o < kWeightOps) load(p);
         }
     }
-}
+};
 
 __device__ __forceinline__ void issue_tile(const WOp& op, int lo, int hi, int i, uint8_t* dst, uint64_t* bar, uint64_t pol) {
     const TileGeom& g = op.g;
@@ -151,41 +200,115 @@ __device__ __forceinline__ void issue_tile(const WOp& op, int lo, int hi, int i,
     for (int h = 0; h < g.halves; ++h) {
         const size_t row = static_cast<size_t>(r0) + static_cast<size_t>(h) * g.out_rows;
         if (g.n_seg == 1) {
-            bulk_load(dst + h * nr * g.seg_bytes, op.w + row * g.row_bytes, static_cast<uint32_t>(nr * g.row_bytes), bar, pol);
+            bulk_load(dst + h * g.rows_per_tile * g.seg_bytes, op.w + row * g.row_bytes, static_cast<uint32_t>(nr * g.row_bytes),
+                      bar, pol);
         } else {
             for (int r = 0; r < nr; ++r) {
-                bulk_load(dst + (h * nr + r) * g.seg_bytes, op.w + (row + r) * g.row_bytes + static_cast<size_t>(sg) * g.seg_bytes,
+                bulk_load(dst + (h * g.rows_per_tile + r) * g.seg_bytes,
+                          op.w + (row + r) * g.row_bytes + static_cast<size_t>(sg) * g.seg_bytes,
                           static_cast<uint32_t>(g.seg_bytes), bar, pol);
             }
         }
     }
 }
 
-// Warp 0, lane 0: streams every tile of the step in order.
-__device__ void run_producer(const StepParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty, volatile Flags* fl) {
+// Warp 0, lanes 0..kProducers-1: lane j streams tiles j, j+kProducers, ... of the step (in use
+// order) into the stages it owns. A copy is issued as soon as its stage is released.
+__device__ void run_producer(const StepParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty, volatile int* stage_tile,
+                             volatile Flags* fl, int lane) {
     const uint64_t pol = l2_policy_evict_first();
-    int t = 0;
-    bool stop = false;
-    prefetch_head(p, 0);
-    for (int o = 0; o < kWeightOps && !stop; ++o) {
-        if (o + 1 < kWeightOps) prefetch_head(p, o + 1);
-        const WOp op = weight_op(p, o);
-        int lo, hi;
-        split_rows(op.g.out_rows, lo, hi);
-        const int nt = op_tiles(op.g, lo, hi);
-        for (int i = 0; i < nt; ++i) {
-            const int s = t % kStages, k = t / kStages;
-            if (k > 0 && !wait_bar(p, &empty[s], (k - 1) & 1, fl, true, 1000u + o)) {
-                stop = true;
-                break;
+    TileCursor cur;
+    cur.load(p);
+    for (int q = 0; q < lane && cur.valid(); ++q) cur.next(p);
+    int t = lane, last = -1;
+    while (cur.valid()) {
+        if (cur.i == 0) trace_mark(p, trace_op_of_weight_op(cur.o), 3);
+        const int s = t % kStages, k = t / kStages;
+        if (k > 0 && !wait_bar(p, &empty[s], (k - 1) & 1, fl, true, 1000u + cur.o)) break;
+        stage_tile[s] = t;
+        trace_tile(p, cur.o, cur.i, 0);
+        issue_tile(cur.op, cur.lo, cur.hi, cur.i, ring + s * kStageBytes, &full[s], pol);
+        last = t;
+        if (lane == 0) fl->issued = t + 1;
+        t += kProducers;
+        for (int q = 0; q < kProducers && cur.valid(); ++q) cur.next(p);
+    }
+    if (lane == 0) fl->issued = 1 << 30;  // releases the prefetch warp
+    // Every copy this lane issued lands before the CTA may exit.
+    for (int u = last; u >= 0 && u > last - kStages; u -= kProducers) {
+        wait_bar(p, &full[u % kStages], (u / kStages) & 1, fl, false, 2000u);
+    }
+}
+
+// Warp 1: L2 prefetch of the weight stream with ordinary prefetch instructions (load/store units,
+// not the TMA engine the copies use), p.prefetch_tiles tiles ahead of the copy producer.
+__device__ void run_prefetcher(const StepParams& p, volatile Flags* fl) {
+    const int lane = threadIdx.x & 31;
+    TileCursor pf;
+    pf.load(p);
+    int pt = 0;
+    uint64_t t0 = 0;
+    while (pf.valid()) {
+        for (uint32_t it = 1; pt >= fl->issued + p.prefetch_tiles; ++it) {
+            if (fl->abort) return;
+            if ((it & 63) == 0) {
+                const uint64_t t = global_ns();
+                if (t0 == 0) t0 = t;
+                if (t - t0 > p.wait_limit_ns) return;  // the copy producer stopped; nothing to wait for
             }
-            issue_tile(op, lo, hi, i, ring + s * kStageBytes, &full[s], pol);
-            ++t;
+            __nanosleep(128);
+        }
+        t0 = 0;
+        const TileGeom& g = pf.op.g;
+        const int grp = pf.i / g.n_seg, sg = pf.i % g.n_seg;
+        const int r0 = pf.lo + grp * g.rows_per_tile;
+        const int nr = min(g.rows_per_tile, pf.hi - r0);
+        for (int h = 0; h < g.halves; ++h) {
+            const size_t row = static_cast<size_t>(r0) + static_cast<size_t>(h) * g.out_rows;
+            for (int r = 0; r < (g.n_seg == 1 ? 1 : nr); ++r) {
+                const uint8_t* a = pf.op.w + (row + r) * g.row_bytes + static_cast<size_t>(sg) * g.seg_bytes;
+                const int bytes = g.n_seg == 1 ? nr * g.row_bytes : g.seg_bytes;
+                for (int off = lane * 128; off < bytes; off += 32 * 128) {
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(a + off) : "memory");
+                }
+            }
+        }
+        pf.next(p);
+        ++pt;
+    }
+}
+
+// Columns 4q..4q+3 of embedding row `tok`, dequantised (one 8/4/2-byte load).
+template <WeightType WT>
+struct EmbVec4 {
+    const StepParams* p;
+    int tok;
+    __device__ __forceinline__ float4 operator()(int q) const {
+        if constexpr (WT == WeightType::BF16) {
+            const uint2 w = __ldg(reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(p->emb_w) +
+                                                                 static_cast<size_t>(tok) * kH) + q);
+            return make_float4(__uint_as_float(w.x << 16), __uint_as_float(w.x & 0xffff0000u), __uint_as_float(w.y << 16),
+                               __uint_as_float(w.y & 0xffff0000u));
+        } else if constexpr (WT == WeightType::INT8) {
+            const uint32_t w = __ldg(reinterpret_cast<const uint32_t*>(static_cast<const int8_t*>(p->emb_w) +
+                                                                      static_cast<size_t>(tok) * kH) + q);
+            const float s = __ldg(static_cast<const float*>(p->emb_s) + tok);
+            return make_float4(static_cast<float>(static_cast<int8_t>(w & 0xff)) * s,
+                               static_cast<float>(static_cast<int8_t>((w >> 8) & 0xff)) * s,
+                               static_cast<float>(static_cast<int8_t>((w >> 16) & 0xff)) * s,
+                               static_cast<float>(static_cast<int8_t>(w >> 24)) * s);
+        } else {
+            const uint16_t w = __ldg(reinterpret_cast<const uint16_t*>(static_cast<const uint8_t*>(p->emb_w) +
+                                                                      static_cast<size_t>(tok) * (kH / 2)) + q);
+            const float s = __half2float(__ldg(static_cast<const __half*>(p->emb_s) +
+                                               static_cast<size_t>(tok) * (kH / p->group_size) + (4 * q) / p->group_size));
+            return make_float4(static_cast<float>(static_cast<int>(w & 0xF) - 8) * s,
+                               static_cast<float>(static_cast<int>((w >> 4) & 0xF) - 8) * s,
+                               static_cast<float>(static_cast<int>((w >> 8) & 0xF) - 8) * s,
+                               static_cast<float>(static_cast<int>((w >> 12) & 0xF) - 8) * s);
         }
     }
-    // Every issued copy lands before the CTA may exit.
-    for (int u = max(0, t - kStages); u < t; ++u) wait_bar(p, &full[u % kStages], (u / kStages) & 1, fl, false, 2000u);
-}
+};
 
 template <WeightType WT>
 __device__ __forceinline__ float emb_value(const StepParams& p, int tok, int j) {
@@ -223,6 +346,7 @@ struct ConsumerCtx {
     uint8_t* ring;
     uint64_t* full;
     uint64_t* empty;
+    volatile int* stage_tile;
     volatile Flags* fl;
     float* xp;
     float* xc;
@@ -234,82 +358,103 @@ struct ConsumerCtx {
 
 __device__ __forceinline__ void csync() { named_barrier(1, kCt); }
 
-// Waits (thread 0) for a dependency; all consumer threads learn the outcome.
-__device__ __forceinline__ bool dep_wait(ConsumerCtx& c, const unsigned* ctr, unsigned target, unsigned id) {
-    if (c.tid == 0) c.fl->ok = c.fl->abort ? 0 : (spin_until(*c.p, ctr, target, c.fl, id) ? 1 : 0);
+// Waits (thread 0) for a dependency; all consumer threads learn the outcome. `top` = trace op index.
+__device__ __forceinline__ bool dep_wait(ConsumerCtx& c, const unsigned* ctr, unsigned target, unsigned id, int top) {
+    if (c.tid == 0) {
+        trace_mark(*c.p, top, 0);
+        c.fl->ok = c.fl->abort ? 0 : (spin_until(*c.p, ctr, target, c.fl, id) ? 1 : 0);
+        trace_mark(*c.p, top, 1);
+    }
     csync();
     const bool ok = c.fl->ok != 0;
     csync();
     return ok;
 }
 
-__device__ __forceinline__ void signal(ConsumerCtx& c, unsigned* ctr) {
+__device__ __forceinline__ void signal(ConsumerCtx& c, unsigned* ctr, int top = -1) {
     csync();
     if (c.tid == 0) {
+        if (top >= 0) trace_mark(*c.p, top, 2);
         __threadfence();
         red_release_gpu_add(ctr, 1u);
     }
 }
 
-// Consumes this CTA's tiles of weight operation `o`; applies the epilogue of `kind`.
+// Waits for, accumulates and releases the n_seg tiles of one row group (first global tile `t0`),
+// reduces the N stage rows across the warp and leaves row i's value in my[i]. Not inlined: one copy
+// per (type, N) serves every operation with that tile shape.
+template <WeightType WT, int N, int CPL>
+__device__ __forceinline__ bool group_dot(const ConsumerCtx& c, int t0, int r0, const WOp& op, float* my, int trace_o,
+                                          int trace_t0) {
+    const StepParams& p = *c.p;
+    const TileGeom& g = op.g;
+    const TileRows tr{r0, g.rows_per_tile, g.halves == 2 ? g.out_rows : 0, g.out_rows * g.halves - 1};
+    const int nc = g.cols / Chunk<WT>::kCols;
+    float acc[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) acc[i] = 0.f;
+    for (int sg = 0; sg < g.n_seg; ++sg) {
+        const int t = t0 + sg;
+        const int s = t % kStages;
+        if (!wait_bar(p, &c.full[s], (t / kStages) & 1, c.fl, true, 3000u, &c.stage_tile[s], t)) return false;
+        if (c.lane == 0 && sg == 0) trace_tile(p, trace_o, t0 - trace_t0, 2);
+        tile_dot<WT, N, CPL>(c.ring + s * kStageBytes, tr, g.seg_bytes, sg * (g.seg_bytes / 16), c.xp, nc, c.xc, op.s, g.cols,
+                             acc, c.lane);
+        __syncwarp();
+        if (c.lane == 0) mbar_arrive(&c.empty[s]);
+    }
+#pragma unroll
+    for (int i = 0; i < N; ++i) {
+        const float v = warp_sum(acc[i]);
+        if (c.lane == 0) my[i] = finish_row<WT>(v, op.s, tr.global_row(i));
+    }
+    __syncwarp();
+    return true;
+}
+
+// Consumes this CTA's tiles of weight operation `o`; applies the epilogue of KIND.
 // LM tracks the best (value, index) per lane in bv/bi. Returns false if the CTA aborted.
-template <WeightType WT, int KIND>
-__device__ bool run_tiles(ConsumerCtx& c, int o, float& bv, int& bi, int layer) {
+// Consumes this CTA's tiles of weight operation `o` (tile shape N x CPL) and applies the epilogue of
+// `kind` (runtime: one copy of the tile loop serves every operation with this shape). LM tracks the
+// best (value, index) per lane in bv/bi. Returns false if the CTA aborted.
+template <WeightType WT, int N, int CPL>
+__device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, int layer) {
     const StepParams& p = *c.p;
     const WOp op = weight_op(p, o);
     const TileGeom& g = op.g;
-    constexpr int MAXN = (KIND == kGu ? 2 : 1) * kMaxTileRows;
     int lo, hi;
     split_rows(g.out_rows, lo, hi);
     const int R = g.rows_per_tile;
     const int ng = (hi - lo + R - 1) / R;
-    const int nc = g.cols / Chunk<WT>::kCols;
-    const int seg_chunks = g.seg_bytes / 16;
     float* my = c.scratch + c.cw * 32;
+    if (R * g.halves != N || g.n_seg != 1 || g.seg_bytes != CPL * 512) {
+        if (c.tid == 0) fail(p, c.fl, kErrWaitTimeout, 4000u + o);  // geometry mismatch: never expected
+        csync();
+        return false;
+    }
     bool ok = true;
     for (int grp = c.cw; grp < ng && ok; grp += kCw) {
         const int r0 = lo + grp * R;
         const int nr = min(R, hi - r0);
-        const StageRows sr{r0, nr, nr * g.halves, g.out_rows};
-        float acc[MAXN];
-#pragma unroll
-        for (int i = 0; i < MAXN; ++i) acc[i] = 0.f;
-        for (int sg = 0; sg < g.n_seg; ++sg) {
-            const int t = c.t_base + grp * g.n_seg + sg;
-            const int s = t % kStages;
-            if (!wait_bar(p, &c.full[s], (t / kStages) & 1, c.fl, true, 3000u + o)) {
-                ok = false;
-                break;
-            }
-            tile_accumulate<WT, MAXN>(c.ring + s * kStageBytes, sr, g.seg_bytes, sg * seg_chunks, c.xp, nc, c.xc, op.s, g.cols,
-                                      acc, c.lane);
-            __syncwarp();
-            if (c.lane == 0) mbar_arrive(&c.empty[s]);
-        }
+        if (c.lane == 0) trace_tile(p, o, grp, 1);
+        ok = group_dot<WT, N, CPL>(c, c.t_base + grp * g.n_seg, r0, op, my, o, c.t_base);
         if (!ok) break;
-#pragma unroll
-        for (int i = 0; i < MAXN; ++i) {
-            if (i < sr.n) {
-                const float v = warp_sum(acc[i]);
-                if (c.lane == 0) my[i] = finish_row<WT>(v, op.s, sr.global_row(i));
-            }
-        }
-        __syncwarp();
+        if (c.lane == 0) trace_tile(p, o, grp, 3);
         if (c.lane < nr) {
             const int r = r0 + c.lane;
-            if constexpr (KIND == kQkv) {
-                __stcg(p.qkv + r, my[c.lane]);
-            } else if constexpr (KIND == kWo || KIND == kDown) {
-                const float v = __ldcg(p.x + r) + my[c.lane];
+            const float d = my[c.lane];
+            if (kind == kQkv) {
+                __stcg(p.qkv + r, d);
+            } else if (kind == kWo || kind == kDown) {
+                const float v = __ldcg(p.x + r) + d;
                 __stcg(p.x + r, v);
-                if (KIND == kDown && p.debug_res) p.debug_res[static_cast<size_t>(layer + 1) * kH + r] = v;
-            } else if constexpr (KIND == kGu) {
-                __stcg(p.act + r, silu_f(my[c.lane]) * my[nr + c.lane]);
+                if (kind == kDown && p.debug_res) p.debug_res[static_cast<size_t>(layer + 1) * kH + r] = v;
+            } else if (kind == kGu) {
+                __stcg(p.act + r, silu_f(d) * my[R + c.lane]);
             } else {
-                const float v = my[c.lane];
-                __stcg(p.logits + r, v);
-                if (better(v, r, bv, bi)) {
-                    bv = v;
+                __stcg(p.logits + r, d);
+                if (better(d, r, bv, bi)) {
+                    bv = d;
                     bi = r;
                 }
             }
@@ -322,10 +467,16 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, float& bv, int& bi, int layer) 
     return c.fl->abort == 0;
 }
 
-template <WeightType WT, typename Src>
-__device__ __forceinline__ void stage(ConsumerCtx& c, Src src, int K, const float* norm_w) {
-    stage_vector<WT>(src, K, norm_w, c.p->eps, c.xp, c.xc, c.red, c.tid, kCt, [] { csync(); });
-}
+// Staging source: a global fp32 vector read through L2, or (vec == null) the embedding row `tok`.
+template <WeightType WT>
+struct StageSrc {
+    const StepParams* p;
+    const float* vec;
+    int tok;
+    __device__ __forceinline__ float4 operator()(int q) const {
+        return vec ? __ldcg(reinterpret_cast<const float4*>(vec) + q) : EmbVec4<WT>{p, tok}(q);
+    }
+};
 
 template <WeightType WT, typename KV>
 __device__ void run_consumers(ConsumerCtx& c, float* cs) {
@@ -336,7 +487,13 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
     const int tok = p.token_override >= 0 ? p.token_override : *p.d_token;
     const int n_tiles = (ctx + kAttnTile - 1) / kAttnTile;
     const int n_slots = p.max_seq / kAttnTile;
+    const bool whole_head = n_tiles <= kWholeHeadMaxTiles;
+    const int head_stride = G / kNkv;
     rope_table(p.inv_freq, pos, cs, c.tid);
+    if (c.tid == 0) {
+        trace_mark(p, 0, 0);
+        trace_mark(p, 0, 1);
+    }
     {
         // Residual rows this CTA owns in the O/down projections start as the embedding.
         int lo, hi;
@@ -347,64 +504,93 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
             if (p.debug_res) p.debug_res[r] = v;
         }
     }
+    constexpr int kN = stage_rows<WT, kQkv>(), kCpl = seg_chunks_per_lane<WT, kQkv>();
+    constexpr int kNd = stage_rows<WT, kDown>(), kCpld = seg_chunks_per_lane<WT, kDown>();
+    static_assert(stage_rows<WT, kWo>() == kN && stage_rows<WT, kGu>() == kN, "shared tile shape");
+    static_assert(seg_chunks_per_lane<WT, kWo>() == kCpl && seg_chunks_per_lane<WT, kGu>() == kCpl, "shared tile shape");
     float bv = -INFINITY;
     int bi = INT_MAX;
-    for (int l = 0; l < kStepLayers; ++l) {
-        const StepLayer& L = p.layers[l];
-        const size_t layer_off = static_cast<size_t>(l) * kNkv * p.max_seq * kHd;
-        KV* kc = static_cast<KV*>(p.k_cache) + layer_off;
-        KV* vc = static_cast<KV*>(p.v_cache) + layer_off;
-        // ---- QKV projection (fused RMSNorm) -------------------------------------------------
-        if (l == 0) {
-            stage<WT>(c, [&](int j) { return emb_value<WT>(p, tok, j); }, kH, L.attn_norm);
-        } else {
-            if (!dep_wait(c, p.sync + kSyncDown + l - 1, G, 10u + l)) return;
-            stage<WT>(c, [&](int j) { return __ldcg(p.x + j); }, kH, L.attn_norm);
-        }
-        if (!run_tiles<WT, kQkv>(c, l * kOpsPerLayer + kQkv, bv, bi, l)) return;
-        signal(c, p.sync + kSyncQkv + l);
-        // ---- RoPE + KV write + split-K attention ---------------------------------------------
-        if (!dep_wait(c, p.sync + kSyncQkv + l, G, 30u + l)) return;
-        {
-            AttSmem<KV>& sm = *reinterpret_cast<AttSmem<KV>*>(c.xp);
-            for (int i = blockIdx.x; i < kNkv * n_tiles; i += G) {
+    for (int o = 0; o < kWeightOps; ++o) {
+        const bool lm = o == kWeightOps - 1;
+        const int l = lm ? kStepLayers : o / kOpsPerLayer;
+        const int kind = lm ? kLm : o % kOpsPerLayer;
+        const float* svec = p.x;
+        const float* snorm = nullptr;
+        int sK = kH;
+        if (kind == kQkv) {
+            const size_t layer_bytes = static_cast<size_t>(l) * kNkv * p.max_seq * kHd * sizeof(KV);
+            // The cached K/V rows this CTA's attention will read do not depend on this step: pull them
+            // into L2 now, before the QKV dependency (the same assignment as the attention below).
+            for (int q = c.tid; q < 2 * kNkv * n_tiles; q += kCt) {
+                const int i = q >> 1;
                 const int h = i / n_tiles, tile = i % n_tiles;
-                attend_tile<KV, true>(p.qkv, kNh, kNkv, cs, kc, vc, p.max_seq, h, tile, ctx, n_slots, p.part_o, p.part_ml, sm,
-                                      c.tid, [] { csync(); });
-                if (c.tid == 0) {
-                    __threadfence();
-                    const unsigned old = atom_acq_rel_gpu_add(p.sync + kSyncTicket + l * kNkv + h, 1u);
-                    c.fl->role = (old == static_cast<unsigned>(n_tiles - 1)) ? 1 : 0;
-                }
-                csync();
-                const bool combiner = c.fl->role != 0;
-                csync();
-                if (combiner) {
-                    combine_head(p.part_o, p.part_ml, h, n_tiles, n_slots, p.att, c.tid);
+                const bool mine = whole_head ? (blockIdx.x == h * head_stride) : (i % G == static_cast<int>(blockIdx.x));
+                if (!mine) continue;
+                const int n = min(kAttnTile, ctx - tile * kAttnTile);
+                const size_t off = (static_cast<size_t>(h) * p.max_seq + tile * kAttnTile) * kHd * sizeof(KV);
+                const uint8_t* base = static_cast<const uint8_t*>((q & 1) ? p.v_cache : p.k_cache);
+                bulk_prefetch_l2(base + layer_bytes + off, static_cast<uint32_t>(n * kHd * sizeof(KV)));
+            }
+            if (l > 0 && !dep_wait(c, p.sync + kSyncDown + l - 1, G, 10u + l, l * 5 + 0)) return;
+            svec = l == 0 ? nullptr : p.x;
+            snorm = p.layers[l].attn_norm;
+        } else if (kind == kWo) {
+            // RoPE + KV write + attention, then the O projection's input.
+            if (!dep_wait(c, p.sync + kSyncQkv + l, G, 30u + l, l * 5 + 1)) return;
+            const size_t layer_off = static_cast<size_t>(l) * kNkv * p.max_seq * kHd;
+            KV* kc = static_cast<KV*>(p.k_cache) + layer_off;
+            KV* vc = static_cast<KV*>(p.v_cache) + layer_off;
+            if (whole_head) {
+                if (blockIdx.x % head_stride == 0 && blockIdx.x / head_stride < kNkv) {
+                    HeadSmem<KV>& sm = *reinterpret_cast<HeadSmem<KV>*>(c.xp);
+                    attend_head<KV>(p.qkv, kNh, kNkv, cs, kc, vc, p.max_seq, blockIdx.x / head_stride, ctx, p.att, sm, c.tid,
+                                    [] { csync(); });
                     signal(c, p.sync + kSyncAtt + l);
                 }
+            } else {
+                AttSmem<KV>& sm = *reinterpret_cast<AttSmem<KV>*>(c.xp);
+                for (int i = blockIdx.x; i < kNkv * n_tiles; i += G) {
+                    const int h = i / n_tiles, tile = i % n_tiles;
+                    attend_tile<KV, true>(p.qkv, kNh, kNkv, cs, kc, vc, p.max_seq, h, tile, ctx, n_slots, p.part_o, p.part_ml,
+                                          sm, c.tid, [] { csync(); });
+                    if (c.tid == 0) {
+                        __threadfence();
+                        const unsigned old = atom_acq_rel_gpu_add(p.sync + kSyncTicket + l * kNkv + h, 1u);
+                        c.fl->role = (old == static_cast<unsigned>(n_tiles - 1)) ? 1 : 0;
+                    }
+                    csync();
+                    const bool combiner = c.fl->role != 0;
+                    csync();
+                    if (combiner) {
+                        combine_head(p.part_o, p.part_ml, h, n_tiles, n_slots, p.att, c.tid);
+                        signal(c, p.sync + kSyncAtt + l);
+                    }
+                }
             }
+            if (c.tid == 0) trace_mark(p, l * 5 + 1, 2);
+            if (!dep_wait(c, p.sync + kSyncAtt + l, kNkv, 50u + l, l * 5 + 2)) return;
+            svec = p.att;
+        } else if (kind == kGu) {
+            if (!dep_wait(c, p.sync + kSyncWo + l, G, 70u + l, l * 5 + 3)) return;
+            snorm = p.layers[l].ffn_norm;
+        } else if (kind == kDown) {
+            if (!dep_wait(c, p.sync + kSyncGu + l, G, 90u + l, l * 5 + 4)) return;
+            svec = p.act;
+            sK = 4 * kH;
+        } else {
+            if (!dep_wait(c, p.sync + kSyncDown + kStepLayers - 1, G, 110u, 80)) return;
+            snorm = p.final_norm;
         }
-        // ---- O projection + residual ------------------------------------------------------
-        if (!dep_wait(c, p.sync + kSyncAtt + l, kNkv, 50u + l)) return;
-        stage<WT>(c, [&](int j) { return __ldcg(p.att + j); }, kH, nullptr);
-        if (!run_tiles<WT, kWo>(c, l * kOpsPerLayer + kWo, bv, bi, l)) return;
-        signal(c, p.sync + kSyncWo + l);
-        // ---- RMSNorm + gate/up + SwiGLU ---------------------------------------------------
-        if (!dep_wait(c, p.sync + kSyncWo + l, G, 70u + l)) return;
-        stage<WT>(c, [&](int j) { return __ldcg(p.x + j); }, kH, L.ffn_norm);
-        if (!run_tiles<WT, kGu>(c, l * kOpsPerLayer + kGu, bv, bi, l)) return;
-        signal(c, p.sync + kSyncGu + l);
-        // ---- down projection + residual ---------------------------------------------------
-        if (!dep_wait(c, p.sync + kSyncGu + l, G, 90u + l)) return;
-        stage<WT>(c, [&](int j) { return __ldcg(p.act + j); }, 4 * kH, nullptr);
-        if (!run_tiles<WT, kDown>(c, l * kOpsPerLayer + kDown, bv, bi, l)) return;
-        signal(c, p.sync + kSyncDown + l);
+        stage_vector<WT>(StageSrc<WT>{&p, svec, tok}, sK, snorm, p.eps, c.xp, c.xc, c.red, c.tid, kCt, [] { csync(); });
+        const bool ok = kind == kDown ? run_tiles<WT, kNd, kCpld>(c, o, kind, bv, bi, l)
+                                      : run_tiles<WT, kN, kCpl>(c, o, kind, bv, bi, l);
+        if (!ok) return;
+        if (kind != kLm) {
+            const int counter = kind == kQkv ? kSyncQkv : (kind == kWo ? kSyncWo : (kind == kGu ? kSyncGu : kSyncDown));
+            signal(c, p.sync + counter + l, l * 5 + (kind == kQkv ? 0 : kind + 1));
+        }
     }
-    // ---- final RMSNorm + tied lm_head + argmax ---------------------------------------------
-    if (!dep_wait(c, p.sync + kSyncDown + kStepLayers - 1, G, 110u)) return;
-    stage<WT>(c, [&](int j) { return __ldcg(p.x + j); }, kH, p.final_norm);
-    if (!run_tiles<WT, kLm>(c, kWeightOps - 1, bv, bi, kStepLayers)) return;
+    // ---- lm_head done: CTA argmax, then the last CTA commits the token ----------------------
     float* am_v = reinterpret_cast<float*>(c.scratch);  // scratch is free again after run_tiles
     int* am_i = reinterpret_cast<int*>(c.scratch + kCw);
     warp_argmax(bv, bi);
@@ -429,6 +615,10 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
         c.fl->role = (old == static_cast<unsigned>(G - 1)) ? 1 : 0;
     }
     csync();
+    if (c.tid == 0) {
+        trace_mark(p, 80, 2);
+        trace_mark(p, 81, 2);
+    }
     if (c.fl->role == 0) return;
     // Last CTA: reduce the per-CTA winners, commit the token, advance the position, reset counters.
     float v = -INFINITY;
@@ -469,20 +659,27 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
     uint64_t* empty = full + kStages;
     volatile Flags* fl = reinterpret_cast<volatile Flags*>(smem + kOffFlags);
+    volatile int* stage_tile = reinterpret_cast<volatile int*>(smem + kOffTiles);
     uint8_t* ring = smem + kOffRing;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+            stage_tile[s] = -1;
         }
         fl->abort = 0;
         fl->ok = 0;
         fl->role = 0;
+        fl->issued = 0;
         fence_barrier_init();
     }
     __syncthreads();
     if (threadIdx.x < 32) {
-        if (threadIdx.x == 0) run_producer(p, ring, full, empty, fl);
+        if (threadIdx.x < kProducers) run_producer(p, ring, full, empty, stage_tile, fl, threadIdx.x);
+        return;
+    }
+    if (threadIdx.x < 64) {
+        if (p.prefetch_mode == 2) run_prefetcher(p, fl);
         return;
     }
     ConsumerCtx c;
@@ -490,12 +687,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     c.ring = ring;
     c.full = full;
     c.empty = empty;
+    c.stage_tile = stage_tile;
     c.fl = fl;
     c.xp = reinterpret_cast<float*>(smem + kOffXp);
     c.xc = reinterpret_cast<float*>(smem + kOffXc);
     c.red = reinterpret_cast<float*>(smem + kOffRed);
     c.scratch = reinterpret_cast<float*>(smem + kOffScratch);
-    c.tid = threadIdx.x - 32;
+    c.tid = threadIdx.x - 64;
     c.cw = c.tid >> 5;
     c.lane = c.tid & 31;
     c.t_base = 0;

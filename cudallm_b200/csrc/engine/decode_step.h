@@ -37,6 +37,19 @@ struct StepLayer {
 
 constexpr int kStepLayers = 16;
 
+// Trace layout per CTA: operation k (layer l: 5l + {0 qkv, 1 attention, 2 o-proj, 3 gate/up, 4 down};
+// 80 lm_head; 81 step end) has 4 slots: dependency wait begins, wait ends, operation ends, producer
+// starts issuing its tiles (weight operations only).
+constexpr int kTraceOps = 82;
+constexpr int kTraceSlots = kTraceOps * 4;
+// After the per-CTA slots: CTA 0's first kTraceTiles lm_head tiles, 4 stamps each (producer issues the
+// copy, consumer starts waiting for it, the data is there, consumer is done with the tile).
+constexpr int kTraceTiles = 256;
+constexpr int kTraceTileStamps = 4;
+inline constexpr size_t trace_words(int grid) {
+    return static_cast<size_t>(grid) * kTraceSlots + kTraceTiles * kTraceTileStamps;
+}
+
 // Device error word layout (err[0] = flags, err[1] = id of the first wait that gave up).
 constexpr unsigned kErrWaitTimeout = 1u;
 constexpr unsigned kErrAborted = 2u;
@@ -67,11 +80,14 @@ struct StepParams {
     unsigned* sync;  // [kSyncWords]
     unsigned* err;   // [2]
     float* debug_res;  // [(16+1)][2048] or null
+    unsigned long long* trace;  // [grid][kTraceSlots] %globaltimer stamps, or null
     int token_override;  // >= 0: feed this token instead of *d_token
     int max_seq;
     float eps;
     int group_size;
     unsigned long long wait_limit_ns;
+    int prefetch_tiles;  // L2 prefetch distance of the weight stream, in tiles beyond the copies
+    int prefetch_mode;   // 0 none, 2 prefetch warp (load/store-unit prefetch instructions)
     TileGeom g_qkv, g_wo, g_gu, g_down, g_lm;
 };
 

@@ -3,7 +3,9 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <string>
 
 #include "common/check.h"
@@ -54,6 +56,8 @@ void alloc(T** p, size_t count) {
 }
 
 constexpr unsigned long long kStepWaitLimitNs = 1000000000ull;  // 1 s per inter-CTA wait
+// L2 prefetch distance (tiles of 16 KiB per SM) of the persistent step; CUDALLM_PREFETCH_TILES overrides it.
+constexpr int kDefaultPrefetchTiles = 16;
 
 }  // namespace
 
@@ -132,12 +136,19 @@ Engine::Engine(const std::string& path, const EngineOptions& opts) : opts_(opts)
             p.sync = sync_;
             p.err = state_->err;
             p.debug_res = nullptr;
+            p.trace = nullptr;
             p.token_override = -1;
             p.max_seq = max_seq_;
             p.eps = c.rms_eps;
             p.group_size = c.group_size;
             p.wait_limit_ns = kStepWaitLimitNs;
-            const int rpb = opts_.matvec_rpb;
+            p.prefetch_tiles = kDefaultPrefetchTiles;
+            if (const char* env = std::getenv("CUDALLM_PREFETCH_TILES")) p.prefetch_tiles = std::max(0, std::atoi(env));
+            p.prefetch_mode = 2;
+            if (const char* env = std::getenv("CUDALLM_PREFETCH_MODE")) p.prefetch_mode = std::atoi(env);
+            // The persistent kernel is compiled for the default tile shape (matvec_rpb selects the tile rows of
+            // the per-op kernels only; results do not depend on it).
+            const int rpb = 0;
             p.g_qkv = make_tile_geom(c.wtype, Epilogue::STORE, (c.n_heads + 2 * c.n_kv_heads) * c.head_dim, c.hidden, rpb);
             p.g_wo = make_tile_geom(c.wtype, Epilogue::ADD, c.hidden, c.hidden, rpb);
             p.g_gu = make_tile_geom(c.wtype, Epilogue::SWIGLU, 2 * c.inter, c.hidden, rpb);
@@ -158,14 +169,15 @@ void Engine::free_all() noexcept {
     if (graph_) report(cudaGraphDestroy(graph_), "cudaGraphDestroy");
     graph_exec_ = nullptr;
     graph_ = nullptr;
-    void* bufs[] = {x_,      xb_,      qkv_,  att_,  tmp_,   gu_,   act_,  logits_, k_cache_,
-                    v_cache_, part_o_, part_ml_, am_v_, am_i_, state_, sync_, debug_res_};
+    void* bufs[] = {x_,      xb_,      qkv_,  att_,  tmp_,   gu_,   act_,       logits_, k_cache_,
+                    v_cache_, part_o_, part_ml_, am_v_, am_i_, state_, sync_, debug_res_, trace_};
     for (void* b : bufs) {
         if (b) report(cudaFree(b), "cudaFree");
     }
     x_ = xb_ = qkv_ = att_ = tmp_ = gu_ = act_ = logits_ = part_o_ = part_ml_ = am_v_ = debug_res_ = nullptr;
     k_cache_ = v_cache_ = nullptr;
     am_i_ = nullptr;
+    trace_ = nullptr;
     state_ = nullptr;
     sync_ = nullptr;
     if (stream_) report(cudaStreamDestroy(stream_), "cudaStreamDestroy");
@@ -222,10 +234,33 @@ void Engine::finish_sync(float* logits_out, int* next_token_out) {
     if (next_token_out) *next_token_out = st.token;
 }
 
+void Engine::set_trace(bool enable) {
+    if (!persistent_) throw ArgError("tracing needs the persistent decode path");
+    DeviceGuard guard(device_);
+    if (enable && !trace_) {
+        const size_t n = trace_words(decode_step_grid());
+        CLLM_CUDA(cudaMalloc(&trace_, n * sizeof(unsigned long long)));
+        CLLM_CUDA(cudaMemset(trace_, 0, n * sizeof(unsigned long long)));
+    }
+    trace_on_ = enable;
+}
+
+int Engine::trace_grid() const { return decode_step_grid(); }
+
+void Engine::read_trace(unsigned long long* out, size_t count) {
+    if (!trace_) throw StateError("tracing was never enabled");
+    const size_t n = trace_words(decode_step_grid());
+    if (count < n) throw ArgError("read_trace: output buffer too small");
+    synchronize();
+    DeviceGuard guard(device_);
+    CLLM_CUDA(cudaMemcpy(out, trace_, n * sizeof(unsigned long long), cudaMemcpyDeviceToHost));
+}
+
 void Engine::enqueue_persistent(int token, float* debug_res) {
     StepParams p = step_params_;
     p.token_override = token;
     p.debug_res = debug_res;
+    p.trace = trace_on_ ? trace_ : nullptr;
     launch_decode_step(p, config().wtype, opts_.kv, stream_);
 }
 

@@ -60,6 +60,10 @@ public:
     void step_debug(int token, float* residuals_out, float* logits_out, int* next_token_out);
     // Waits for queued work and reports a device-side failure.
     void synchronize();
+    // Per-CTA timestamps of the persistent step (see decode_step.h kTraceSlots).
+    void set_trace(bool enable);
+    int trace_grid() const;
+    void read_trace(unsigned long long* out, size_t count);
 
 private:
     struct DevState {
@@ -104,6 +108,8 @@ private:
     DevState* state_ = nullptr;  // token, pos, error words
     unsigned* sync_ = nullptr;
     float* debug_res_ = nullptr;
+    unsigned long long* trace_ = nullptr;
+    bool trace_on_ = false;
 };
 
 }  // namespace cudallm

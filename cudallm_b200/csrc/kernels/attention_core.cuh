@@ -178,23 +178,194 @@ __device__ __forceinline__ void attend_tile(const float* qkv, int nh, int nkv, c
     sync();
 }
 
-// Merges the n_tiles partials of the 4 query heads of KV head h in tile order and writes
-// out[hq*64 + d]. Thread (g, d) = (tid/64, tid%64) of a 256-thread group.
+// Merges the n_tiles partials of the 4 query heads of KV head h in tile order (one pass with a
+// running maximum) and writes out[hq*64 + d]. Thread (g, d) = (tid/64, tid%64) of a 256-thread group.
 __device__ __forceinline__ void combine_head(const float* part_o, const float* part_ml, int h, int n_tiles, int n_slots,
                                              float* out, int tid) {
     const int g = tid >> 6, d = tid & 63;
     const int hq = h * kGqa + g;
-    const float* ml = part_ml + static_cast<size_t>(hq) * n_slots * 2;
+    const float2* ml = reinterpret_cast<const float2*>(part_ml + static_cast<size_t>(hq) * n_slots * 2);
     const float* po = part_o + static_cast<size_t>(hq) * n_slots * kHd;
-    float M = -INFINITY;
-    for (int c = 0; c < n_tiles; ++c) M = fmaxf(M, __ldcg(ml + 2 * c));
-    float L = 0.f, acc = 0.f;
+    float M = -INFINITY, L = 0.f, acc = 0.f;
+#pragma unroll 4
     for (int c = 0; c < n_tiles; ++c) {
-        const float e = expf(__ldcg(ml + 2 * c) - M);
-        L = fmaf(__ldcg(ml + 2 * c + 1), e, L);
-        acc = fmaf(__ldcg(po + static_cast<size_t>(c) * kHd + d), e, acc);
+        const float2 mlc = __ldcg(ml + c);
+        const float o = __ldcg(po + static_cast<size_t>(c) * kHd + d);
+        const float mn = fmaxf(M, mlc.x);
+        const float a = expf(M - mn), b = expf(mlc.x - mn);
+        L = L * a + mlc.y * b;
+        acc = acc * a + o * b;
+        M = mn;
     }
     __stcg(out + hq * kHd + d, acc / L);
+}
+
+// ---- whole-head attention (short contexts) -------------------------------------------------------
+// One 256-thread group computes all 4 query heads of KV head h over the whole context: warp w takes
+// tiles w, w+8, ... (64 tokens each) straight from the cache (through L2), keeps a running softmax
+// (max, sum, p.V) per head, and the 8 warp states are merged in warp order. No partials leave the
+// CTA, so there is no second pass. Lane j scores tokens t0+j and t0+j+32; for p.V, lane group
+// g = lane/8 takes tokens t0 + 4i + g and lane sub = lane%8 owns dims 8*sub .. 8*sub+7.
+template <typename KV>
+struct HeadSmem {
+    float qs[kGqa][kHd];
+    alignas(16) KV kn[kHd];
+    alignas(16) KV vn[kHd];
+    float ps[8][kGqa][kAttnTile];
+    float wm[8][kGqa];
+    float wl[8][kGqa];
+    float wo[8][kGqa][kHd];
+};
+
+template <typename KV>
+__device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
+    using KV2 = typename Kv2<KV>::T;
+    const KV2* h2 = reinterpret_cast<const KV2*>(&u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const float2 f = kv2_to_float2(h2[e]);
+        v[2 * e] = f.x;
+        v[2 * e + 1] = f.y;
+    }
+}
+
+template <typename KV, typename Sync>
+__device__ __forceinline__ void attend_head(const float* qkv, int nh, int nkv, const float* cs, KV* k_cache, KV* v_cache,
+                                            int max_seq, int h, int ctx, float* out, HeadSmem<KV>& sm, int tid, Sync sync) {
+    const int pos = ctx - 1;
+    const int w = tid >> 5, lane = tid & 31;
+    // Rotated query heads, and the new token's k (rotated) and v, rounded to the cache type.
+    if (tid < kGqa * kHd / 2) {
+        const int g = tid >> 5, i = tid & 31;
+        const float* q = qkv + (h * kGqa + g) * kHd;
+        const float x0 = __ldcg(q + i), x1 = __ldcg(q + i + kHd / 2);
+        const float c = cs[i], s = cs[kHd / 2 + i];
+        sm.qs[g][i] = x0 * c - x1 * s;
+        sm.qs[g][i + kHd / 2] = x1 * c + x0 * s;
+    } else if (tid < kGqa * kHd / 2 + kHd / 2) {
+        const int i = tid - kGqa * kHd / 2;
+        const float* k = qkv + (nh + h) * kHd;
+        const float x0 = __ldcg(k + i), x1 = __ldcg(k + i + kHd / 2);
+        const float c = cs[i], s = cs[kHd / 2 + i];
+        const KV k0 = to_kv<KV>(x0 * c - x1 * s), k1 = to_kv<KV>(x1 * c + x0 * s);
+        sm.kn[i] = k0;
+        sm.kn[i + kHd / 2] = k1;
+        KV* kdst = k_cache + (static_cast<size_t>(h) * max_seq + pos) * kHd;
+        kdst[i] = k0;
+        kdst[i + kHd / 2] = k1;
+    } else if (tid < kGqa * kHd / 2 + kHd / 2 + kHd) {
+        const int d = tid - kGqa * kHd / 2 - kHd / 2;
+        const KV v = to_kv<KV>(__ldcg(qkv + (nh + nkv + h) * kHd + d));
+        sm.vn[d] = v;
+        v_cache[(static_cast<size_t>(h) * max_seq + pos) * kHd + d] = v;
+    }
+    sync();
+    const KV* Kh = k_cache + static_cast<size_t>(h) * max_seq * kHd;
+    const KV* Vh = v_cache + static_cast<size_t>(h) * max_seq * kHd;
+    const int n_tiles = (ctx + kAttnTile - 1) / kAttnTile;
+    const int g = lane >> 3, sub = lane & 7;
+    float m_run[kGqa], l_run[kGqa], o_run[kGqa][8];
+#pragma unroll
+    for (int hq = 0; hq < kGqa; ++hq) {
+        m_run[hq] = -INFINITY;
+        l_run[hq] = 0.f;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o_run[hq][e] = 0.f;
+    }
+    for (int tl = w; tl < n_tiles; tl += 8) {
+        const int t0 = tl * kAttnTile;
+        // Scores for tokens t0 + lane (half 0) and t0 + lane + 32 (half 1), one key row at a time.
+        float sc[2][kGqa];
+#pragma unroll 1
+        for (int half = 0; half < 2; ++half) {
+            const int j = t0 + lane + 32 * half;
+            const uint4* src = (j < ctx && j != pos) ? reinterpret_cast<const uint4*>(Kh + static_cast<size_t>(j) * kHd)
+                                                     : reinterpret_cast<const uint4*>(sm.kn);
+            uint4 kr[8];
+#pragma unroll
+            for (int c = 0; c < 8; ++c) kr[c] = (j < ctx && j != pos) ? __ldcg(src + c) : src[c];
+            float dot[kGqa] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+                float kf[8];
+                unpack8<KV>(kr[c], kf);
+#pragma unroll
+                for (int hq = 0; hq < kGqa; ++hq) {
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) dot[hq] = fmaf(kf[e], sm.qs[hq][8 * c + e], dot[hq]);
+                }
+            }
+#pragma unroll
+            for (int hq = 0; hq < kGqa; ++hq) sc[half][hq] = j < ctx ? 0.125f * dot[hq] : -INFINITY;
+        }
+        // Running softmax: rescale the state to the new maximum, weight this tile's p by it directly.
+#pragma unroll
+        for (int hq = 0; hq < kGqa; ++hq) {
+            const float mn = fmaxf(m_run[hq], warp_max(fmaxf(sc[0][hq], sc[1][hq])));
+            const float a = expf(m_run[hq] - mn);
+            const float pa = expf(sc[0][hq] - mn), pb = expf(sc[1][hq] - mn);
+            sm.ps[w][hq][lane] = pa;
+            sm.ps[w][hq][lane + 32] = pb;
+            l_run[hq] = l_run[hq] * a + warp_sum(pa + pb);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o_run[hq][e] *= a;
+            m_run[hq] = mn;
+        }
+        __syncwarp();
+#pragma unroll 1
+        for (int batch = 0; batch < 2; ++batch) {
+            uint4 vr[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int j = t0 + 4 * (8 * batch + i) + g;
+                vr[i] = (j < ctx && j != pos) ? __ldcg(reinterpret_cast<const uint4*>(Vh + static_cast<size_t>(j) * kHd) + sub)
+                                              : reinterpret_cast<const uint4*>(sm.vn)[sub];
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int jt = 4 * (8 * batch + i) + g;  // token within the tile; p is 0 past the context
+                float vf[8];
+                unpack8<KV>(vr[i], vf);
+#pragma unroll
+                for (int hq = 0; hq < kGqa; ++hq) {
+                    const float pv = sm.ps[w][hq][jt];
+#pragma unroll
+                    for (int e = 0; e < 8; ++e) o_run[hq][e] = fmaf(pv, vf[e], o_run[hq][e]);
+                }
+            }
+        }
+        __syncwarp();
+    }
+#pragma unroll
+    for (int hq = 0; hq < kGqa; ++hq) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            float v = o_run[hq][e];
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            if (g == 0) sm.wo[w][hq][8 * sub + e] = v;
+        }
+        if (lane == 0) {
+            sm.wm[w][hq] = m_run[hq];
+            sm.wl[w][hq] = l_run[hq];
+        }
+    }
+    sync();
+    {
+        const int hq = tid >> 6, d = tid & 63;
+        float M = -INFINITY;
+#pragma unroll
+        for (int ww = 0; ww < 8; ++ww) M = fmaxf(M, sm.wm[ww][hq]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < 8; ++ww) {
+            const float e = expf(sm.wm[ww][hq] - M);
+            L = fmaf(sm.wl[ww][hq], e, L);
+            O = fmaf(sm.wo[ww][hq][d], e, O);
+        }
+        __stcg(out + (h * kGqa + hq) * kHd + d, O / L);
+    }
+    sync();
 }
 
 }  // namespace cudallm

@@ -78,21 +78,41 @@ __device__ __forceinline__ float warp_max(float v) {
 
 __device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); }
 
-// Stages `src(j)` (optionally RMS-normalised with gain norm_w) for j < K into planes `xp`, and for
-// int4 the per-chunk sums into `xc`. Runs on `nthr` threads with index tid (nthr == 256 in every
-// caller, which fixes the sum-of-squares order). `sync()` is a barrier over those threads;
-// `red` is 32 floats of scratch.
-template <WeightType WT, typename Src, typename Sync>
-__device__ __forceinline__ void stage_vector(Src src, int K, const float* __restrict__ norm_w, float eps, float* xp,
+// Stages the vector (optionally RMS-normalised with gain norm_w) into planes `xp`, and for int4 the
+// per-chunk sums into `xc`. `src4(q)` returns columns 4q..4q+3 as a float4. Runs on `nthr` == 256
+// threads with index tid (which fixes the sum-of-squares order); every thread issues all of its loads
+// (K/1024 float4) before using any, so staging costs one memory round trip, not K/256 of them.
+// `sync()` is a barrier over those threads; `red` is 32 floats of scratch.
+constexpr int kMaxStageK = 8192;
+template <WeightType WT, typename Src4, typename Sync>
+__device__ __forceinline__ void stage_vector(Src4 src4, int K, const float* __restrict__ norm_w, float eps, float* xp,
                                              float* xc, float* red, int tid, int nthr, Sync sync) {
     constexpr int C = Chunk<WT>::kCols;
+    constexpr int kMaxPer = kMaxStageK / 4 / 256;
     const int nc = K / C;
-    float inv = 1.f;
+    const int n4 = K / 4;
+    float4 v[kMaxPer];
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+        const int q = tid + i * nthr;
+        if (q < n4) v[i] = src4(q);
+    }
     if (norm_w != nullptr) {
         float ss = 0.f;
-        for (int j = tid; j < K; j += nthr) {
-            const float v = src(j);
-            ss = fmaf(v, v, ss);
+#pragma unroll
+        for (int i = 0; i < kMaxPer; ++i) {
+            if (tid + i * nthr < n4) {
+                ss = fmaf(v[i].x, v[i].x, ss);
+                ss = fmaf(v[i].y, v[i].y, ss);
+                ss = fmaf(v[i].z, v[i].z, ss);
+                ss = fmaf(v[i].w, v[i].w, ss);
+            }
+        }
+        float4 g[kMaxPer];
+#pragma unroll
+        for (int i = 0; i < kMaxPer; ++i) {
+            const int q = tid + i * nthr;
+            if (q < n4) g[i] = __ldg(reinterpret_cast<const float4*>(norm_w) + q);
         }
         ss = warp_sum(ss);
         if ((tid & 31) == 0) red[tid >> 5] = ss;
@@ -103,28 +123,51 @@ __device__ __forceinline__ void stage_vector(Src src, int K, const float* __rest
             if (tid == 0) red[0] = t;
         }
         sync();
-        inv = rsqrtf(red[0] / static_cast<float>(K) + eps);
+        const float inv = rsqrtf(red[0] / static_cast<float>(K) + eps);
+#pragma unroll
+        for (int i = 0; i < kMaxPer; ++i) {
+            v[i].x = v[i].x * inv * g[i].x;
+            v[i].y = v[i].y * inv * g[i].y;
+            v[i].z = v[i].z * inv * g[i].z;
+            v[i].w = v[i].w * inv * g[i].w;
+        }
     }
-    for (int j = tid; j < K; j += nthr) {
-        float v = src(j);
-        if (norm_w != nullptr) v = v * inv * __ldg(norm_w + j);
-        xp[plane_offset<WT>(j, nc)] = v;
+    float4* p4 = reinterpret_cast<float4*>(xp);
+#pragma unroll
+    for (int i = 0; i < kMaxPer; ++i) {
+        const int q = tid + i * nthr;
+        if (q >= n4) continue;
+        const int c = (4 * q) / C, i0 = (4 * q) % C;
+        if constexpr (WT == WeightType::INT4) {
+            const int k = i0 >> 3, e = (i0 & 7) >> 1;  // e = 0 or 2: component of the pair
+            float2* even = reinterpret_cast<float2*>(xp + ((2 * k) * nc + c) * 4 + e);
+            float2* odd = reinterpret_cast<float2*>(xp + ((2 * k + 1) * nc + c) * 4 + e);
+            *even = make_float2(v[i].x, v[i].z);
+            *odd = make_float2(v[i].y, v[i].w);
+        } else {
+            p4[(i0 >> 2) * nc + c] = v[i];
+        }
     }
     sync();
     if constexpr (WT == WeightType::INT4) {
-        const float4* p4 = reinterpret_cast<const float4*>(xp);
         for (int c = tid; c < nc; c += nthr) {
             float s = 0.f;
 #pragma unroll
-            for (int p = 0; p < Chunk<WT>::kPlanes; ++p) {
-                const float4 v = p4[p * nc + c];
-                s += v.x + v.y + v.z + v.w;
+            for (int pl = 0; pl < Chunk<WT>::kPlanes; ++pl) {
+                const float4 t = p4[pl * nc + c];
+                s += t.x + t.y + t.z + t.w;
             }
             xc[c] = s;
         }
         sync();
     }
 }
+
+// float4 source over a global fp32 vector, read through L2 (data written by other CTAs).
+struct GlobalVec4 {
+    const float* p;
+    __device__ __forceinline__ float4 operator()(int q) const { return __ldcg(reinterpret_cast<const float4*>(p) + q); }
+};
 
 __device__ __forceinline__ float bf16lo(uint32_t w) { return __uint_as_float(w << 16); }
 __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
@@ -136,101 +179,112 @@ __device__ __forceinline__ float i8val(uint32_t wb, uint32_t sel) {
 // int4: nibble n (already isolated in byte b) -> 0.5 + n/256.
 __device__ __forceinline__ float i4half(uint32_t v, uint32_t sel) { return __uint_as_float(__byte_perm(v, 0x3F000000u, sel)); }
 
-// Rows held by one stage: rows [0, nr) are r0.., rows [nr, 2nr) (SWIGLU only) are r0+up_off...
-struct StageRows {
-    int r0, nr, n, up_off;
-    __device__ __forceinline__ int global_row(int i) const { return i < nr ? r0 + i : r0 + (i - nr) + up_off; }
+// Rows of one stage. Stage layout is fixed whatever the number of valid rows: stage row i sits at
+// byte i * seg_bytes; for SWIGLU the R gate rows come first and the R matching up rows start at stage
+// row R. Rows past the end of the matrix are computed on stale shared memory and discarded, so the
+// accumulation loop has no per-row branches.
+struct TileRows {
+    int r0;      // first output row of the tile
+    int R;       // rows per half
+    int up_off;  // global row offset of the up half (SWIGLU), else 0
+    int last;    // last row of the weight matrix (scale loads are clamped to it)
+    __device__ __forceinline__ int global_row(int i) const {
+        const int r = i < R ? r0 + i : r0 + (i - R) + up_off;
+        return r < last ? r : last;
+    }
 };
 
-// Accumulates one tile (rows x one segment) into acc[0..n). MAXN bounds n at compile time so the
-// accumulators stay in registers.
-template <WeightType WT, int MAXN>
-__device__ __forceinline__ void tile_accumulate(const uint8_t* stage, const StageRows& sr, int seg_bytes, int seg_chunk0,
-                                                const float* xp, int nc, const float* xc, const void* scales, int K,
-                                                float (&acc)[MAXN], int lane) {
+// Accumulates one tile (N stage rows x one row segment) into acc[0..N). Two independent FMA chains
+// per row keep the dependency latency hidden. CPL > 0 fixes the chunks per lane (segment bytes / 512)
+// at compile time so the chunk loop unrolls completely; CPL == 0 reads it from seg_bytes.
+template <WeightType WT, int N, int CPL = 0>
+__device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& tr, int seg_bytes, int seg_chunk0,
+                                         const float* xp, int nc, const float* xc, const void* scales, int K,
+                                         float (&acc)[N], int lane) {
     const float4* p4 = reinterpret_cast<const float4*>(xp);
-    const int cpl = seg_bytes >> 9;  // chunks per lane per row (segment bytes / (32 lanes * 16 B))
+    const int cpl = CPL > 0 ? CPL : (seg_bytes >> 9);  // chunks per lane per row
+    if constexpr (CPL > 0) seg_bytes = CPL * 512;
+    float a0[N], a1[N];
+#pragma unroll
+    for (int i = 0; i < N; ++i) a0[i] = a1[i] = 0.f;
     [[maybe_unused]] const int groups = K >> 7;
+#pragma unroll(CPL > 0 ? CPL : 2)
     for (int j = 0; j < cpl; ++j) {
         const int c = lane + 32 * j;
         const int gc = seg_chunk0 + c;
         if constexpr (WT == WeightType::BF16) {
             const float4 x0 = p4[gc], x1 = p4[nc + gc];
 #pragma unroll
-            for (int i = 0; i < MAXN; ++i) {
-                if (i < sr.n) {
-                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
-                    float a = acc[i];
-                    a = fmaf(bf16lo(w.x), x0.x, a);
-                    a = fmaf(bf16hi(w.x), x0.y, a);
-                    a = fmaf(bf16lo(w.y), x0.z, a);
-                    a = fmaf(bf16hi(w.y), x0.w, a);
-                    a = fmaf(bf16lo(w.z), x1.x, a);
-                    a = fmaf(bf16hi(w.z), x1.y, a);
-                    a = fmaf(bf16lo(w.w), x1.z, a);
-                    a = fmaf(bf16hi(w.w), x1.w, a);
-                    acc[i] = a;
-                }
+            for (int i = 0; i < N; ++i) {
+                const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                a0[i] = fmaf(bf16lo(w.x), x0.x, a0[i]);
+                a1[i] = fmaf(bf16lo(w.z), x1.x, a1[i]);
+                a0[i] = fmaf(bf16hi(w.x), x0.y, a0[i]);
+                a1[i] = fmaf(bf16hi(w.z), x1.y, a1[i]);
+                a0[i] = fmaf(bf16lo(w.y), x0.z, a0[i]);
+                a1[i] = fmaf(bf16lo(w.w), x1.z, a1[i]);
+                a0[i] = fmaf(bf16hi(w.y), x0.w, a0[i]);
+                a1[i] = fmaf(bf16hi(w.w), x1.w, a1[i]);
             }
         } else if constexpr (WT == WeightType::INT8) {
             const float4 x0 = p4[gc], x1 = p4[nc + gc], x2 = p4[2 * nc + gc], x3 = p4[3 * nc + gc];
 #pragma unroll
-            for (int i = 0; i < MAXN; ++i) {
-                if (i < sr.n) {
-                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
-                    const uint32_t b0 = w.x ^ 0x80808080u, b1 = w.y ^ 0x80808080u, b2 = w.z ^ 0x80808080u,
-                                   b3 = w.w ^ 0x80808080u;
-                    float a = acc[i];
-                    a = fmaf(i8val(b0, 0x7540), x0.x, a);
-                    a = fmaf(i8val(b0, 0x7541), x0.y, a);
-                    a = fmaf(i8val(b0, 0x7542), x0.z, a);
-                    a = fmaf(i8val(b0, 0x7543), x0.w, a);
-                    a = fmaf(i8val(b1, 0x7540), x1.x, a);
-                    a = fmaf(i8val(b1, 0x7541), x1.y, a);
-                    a = fmaf(i8val(b1, 0x7542), x1.z, a);
-                    a = fmaf(i8val(b1, 0x7543), x1.w, a);
-                    a = fmaf(i8val(b2, 0x7540), x2.x, a);
-                    a = fmaf(i8val(b2, 0x7541), x2.y, a);
-                    a = fmaf(i8val(b2, 0x7542), x2.z, a);
-                    a = fmaf(i8val(b2, 0x7543), x2.w, a);
-                    a = fmaf(i8val(b3, 0x7540), x3.x, a);
-                    a = fmaf(i8val(b3, 0x7541), x3.y, a);
-                    a = fmaf(i8val(b3, 0x7542), x3.z, a);
-                    a = fmaf(i8val(b3, 0x7543), x3.w, a);
-                    acc[i] = a;
-                }
+            for (int i = 0; i < N; ++i) {
+                const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                const uint32_t b0 = w.x ^ 0x80808080u, b1 = w.y ^ 0x80808080u, b2 = w.z ^ 0x80808080u,
+                               b3 = w.w ^ 0x80808080u;
+                a0[i] = fmaf(i8val(b0, 0x7540), x0.x, a0[i]);
+                a1[i] = fmaf(i8val(b2, 0x7540), x2.x, a1[i]);
+                a0[i] = fmaf(i8val(b0, 0x7541), x0.y, a0[i]);
+                a1[i] = fmaf(i8val(b2, 0x7541), x2.y, a1[i]);
+                a0[i] = fmaf(i8val(b0, 0x7542), x0.z, a0[i]);
+                a1[i] = fmaf(i8val(b2, 0x7542), x2.z, a1[i]);
+                a0[i] = fmaf(i8val(b0, 0x7543), x0.w, a0[i]);
+                a1[i] = fmaf(i8val(b2, 0x7543), x2.w, a1[i]);
+                a0[i] = fmaf(i8val(b1, 0x7540), x1.x, a0[i]);
+                a1[i] = fmaf(i8val(b3, 0x7540), x3.x, a1[i]);
+                a0[i] = fmaf(i8val(b1, 0x7541), x1.y, a0[i]);
+                a1[i] = fmaf(i8val(b3, 0x7541), x3.y, a1[i]);
+                a0[i] = fmaf(i8val(b1, 0x7542), x1.z, a0[i]);
+                a1[i] = fmaf(i8val(b3, 0x7542), x3.z, a1[i]);
+                a0[i] = fmaf(i8val(b1, 0x7543), x1.w, a0[i]);
+                a1[i] = fmaf(i8val(b3, 0x7543), x3.w, a1[i]);
             }
         } else {
             const float xsum = xc[gc];
             const int g = gc >> 2;  // 128-column group of this chunk
             const __half* sc = static_cast<const __half*>(scales);
+            float4 xe[4], xo[4];
 #pragma unroll
-            for (int i = 0; i < MAXN; ++i) {
-                if (i < sr.n) {
-                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
-                    const float s = __half2float(__ldg(sc + static_cast<size_t>(sr.global_row(i)) * groups + g));
-                    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-                    float p = 0.f;
+            for (int k = 0; k < 4; ++k) {
+                xe[k] = p4[(2 * k) * nc + gc];
+                xo[k] = p4[(2 * k + 1) * nc + gc];
+            }
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        const float4 xe = p4[(2 * k) * nc + gc];
-                        const float4 xo = p4[(2 * k + 1) * nc + gc];
-                        const uint32_t lo = words[k] & 0x0F0F0F0Fu;
-                        const uint32_t hi = (words[k] >> 4) & 0x0F0F0F0Fu;
-                        p = fmaf(i4half(lo, 0x7044), xe.x, p);
-                        p = fmaf(i4half(lo, 0x7144), xe.y, p);
-                        p = fmaf(i4half(lo, 0x7244), xe.z, p);
-                        p = fmaf(i4half(lo, 0x7344), xe.w, p);
-                        p = fmaf(i4half(hi, 0x7044), xo.x, p);
-                        p = fmaf(i4half(hi, 0x7144), xo.y, p);
-                        p = fmaf(i4half(hi, 0x7244), xo.z, p);
-                        p = fmaf(i4half(hi, 0x7344), xo.w, p);
-                    }
-                    acc[i] = fmaf(s, fmaf(256.f, p, -136.f * xsum), acc[i]);
+            for (int i = 0; i < N; ++i) {
+                const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                const float s = __half2float(__ldg(sc + static_cast<size_t>(tr.global_row(i)) * groups + g));
+                const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+                float p0 = 0.f, p1 = 0.f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const uint32_t lo = words[k] & 0x0F0F0F0Fu;
+                    const uint32_t hi = (words[k] >> 4) & 0x0F0F0F0Fu;
+                    p0 = fmaf(i4half(lo, 0x7044), xe[k].x, p0);
+                    p1 = fmaf(i4half(hi, 0x7044), xo[k].x, p1);
+                    p0 = fmaf(i4half(lo, 0x7144), xe[k].y, p0);
+                    p1 = fmaf(i4half(hi, 0x7144), xo[k].y, p1);
+                    p0 = fmaf(i4half(lo, 0x7244), xe[k].z, p0);
+                    p1 = fmaf(i4half(hi, 0x7244), xo[k].z, p1);
+                    p0 = fmaf(i4half(lo, 0x7344), xe[k].w, p0);
+                    p1 = fmaf(i4half(hi, 0x7344), xo[k].w, p1);
                 }
+                a0[i] = fmaf(s, fmaf(256.f, p0 + p1, -136.f * xsum), a0[i]);
             }
         }
     }
+#pragma unroll
+    for (int i = 0; i < N; ++i) acc[i] += a0[i] + a1[i];
 }
 
 // Row result after the warp reduction (all lanes hold it); int8 applies its per-row scale here.

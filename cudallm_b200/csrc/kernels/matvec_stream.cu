@@ -26,13 +26,14 @@ constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s: far above any legitima
 __host__ __device__ constexpr int align128(int v) { return (v + 127) & ~127; }
 
 struct StreamLayout {
-    int bars, red, xp, xc, scratch, ring, total;
+    int bars, tiles, red, xp, xc, scratch, ring, total;
 };
 
 __host__ __device__ inline StreamLayout stream_layout(int cols, int stages) {
     StreamLayout L;
     L.bars = 0;
-    L.red = align128(2 * stages * 8);
+    L.tiles = 2 * stages * 8;
+    L.red = align128(L.tiles + stages * 4);
     L.xp = L.red + 128;
     L.xc = align128(L.xp + cols * 4);
     L.scratch = align128(L.xc + (cols / 32) * 4);
@@ -42,10 +43,14 @@ __host__ __device__ inline StreamLayout stream_layout(int cols, int stages) {
 }
 
 // Bounded wait on an mbarrier phase. Returns false (after recording *err) if it did not complete.
-__device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, unsigned* err) {
+// With `tile_word`, first waits until the producer has published tile `tile` into that stage: a
+// parity wait is only meaningful for the barrier's current or previous phase, and a consumer warp
+// can be more than one phase ahead of a stage it does not consume every round.
+__device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, unsigned* err,
+                                           const volatile int* tile_word = nullptr, int tile = 0) {
     uint64_t t0 = 0;
     for (uint32_t it = 1;; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if ((tile_word == nullptr || *tile_word == tile) && mbar_try_wait(bar, parity)) return true;
         if ((it & 255) == 0) {
             const uint64_t t = global_ns();
             if (t0 == 0) {
@@ -58,13 +63,60 @@ __device__ __forceinline__ bool wait_phase(uint64_t* bar, uint32_t parity, unsig
     }
 }
 
+// Consumer warp loop: row groups cw, cw+8, ... of this CTA's range, N = rows_per_tile * halves stage rows.
+template <WeightType WT, Epilogue EP, int N>
+__device__ __forceinline__ void consume_groups(const MatvecArgs& a, const TileGeom& g, int lo, int hi, const uint8_t* ring,
+                                               uint64_t* full, uint64_t* empty, const volatile int* stage_tile,
+                                               const float* xp, const float* xc, float* scratch, unsigned* err) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int cw = warp - 1;
+    const int R = g.rows_per_tile;
+    const int n_groups = (hi - lo + R - 1) / R;
+    const int nc = g.cols / Chunk<WT>::kCols;
+    const int seg_chunks = g.seg_bytes / 16;
+    float* my = scratch + cw * 32;
+    for (int grp = cw; grp < n_groups; grp += kConsumerWarps) {
+        const int r0 = lo + grp * R;
+        const int nr = min(R, hi - r0);
+        const TileRows tr{r0, R, g.halves == 2 ? g.out_rows : 0, g.out_rows * g.halves - 1};
+        float acc[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) acc[i] = 0.f;
+        for (int sg = 0; sg < g.n_seg; ++sg) {
+            const int t = grp * g.n_seg + sg;
+            const int s = t % kStreamStages;
+            if (!wait_phase(&full[s], (t / kStreamStages) & 1, err, &stage_tile[s], t)) return;
+            tile_dot<WT, N>(ring + s * kStageBytes, tr, g.seg_bytes, sg * seg_chunks, xp, nc, xc, a.scales, g.cols, acc, lane);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            const float v = warp_sum(acc[i]);
+            if (lane == 0) my[i] = finish_row<WT>(v, a.scales, tr.global_row(i));
+        }
+        __syncwarp();
+        if (lane < nr) {
+            const int r = r0 + lane;
+            if constexpr (EP == Epilogue::SWIGLU) {
+                a.y[r] = silu_f(my[lane]) * my[R + lane];
+            } else if constexpr (EP == Epilogue::ADD) {
+                a.y[r] += my[lane];
+            } else {
+                a.y[r] = my[lane];
+            }
+        }
+        __syncwarp();
+    }
+}
+
 template <WeightType WT, Epilogue EP, bool NORM>
 __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const MatvecArgs a, const TileGeom g, unsigned* err) {
     extern __shared__ __align__(128) uint8_t smem[];
-    constexpr int MAXN = (EP == Epilogue::SWIGLU ? 2 : 1) * kMaxTileRows;
     const StreamLayout L = stream_layout(g.cols, kStreamStages);
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
     uint64_t* empty = full + kStreamStages;
+    volatile int* stage_tile = reinterpret_cast<volatile int*>(smem + L.tiles);
     float* red = reinterpret_cast<float*>(smem + L.red);
     float* xp = reinterpret_cast<float*>(smem + L.xp);
     float* xc = reinterpret_cast<float*>(smem + L.xc);
@@ -82,6 +134,7 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const Mat
         for (int s = 0; s < kStreamStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
+            stage_tile[s] = -1;
         }
         fence_barrier_init();
     }
@@ -100,16 +153,17 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const Mat
                 const int grp = t / g.n_seg, sg = t % g.n_seg;
                 const int r0 = lo + grp * R;
                 const int nr = min(R, hi - r0);
+                stage_tile[s] = t;
                 mbar_arrive_expect_tx(&full[s], static_cast<uint32_t>(nr * g.seg_bytes * g.halves));
                 uint8_t* dst = ring + s * kStageBytes;
                 for (int h = 0; h < g.halves; ++h) {
                     const size_t row = static_cast<size_t>(r0) + static_cast<size_t>(h) * g.out_rows;
                     if (g.n_seg == 1) {
-                        bulk_load(dst + h * nr * g.seg_bytes, w + row * g.row_bytes, static_cast<uint32_t>(nr * g.row_bytes),
+                        bulk_load(dst + h * R * g.seg_bytes, w + row * g.row_bytes, static_cast<uint32_t>(nr * g.row_bytes),
                                   &full[s], pol);
                     } else {
                         for (int i = 0; i < nr; ++i) {
-                            bulk_load(dst + (h * nr + i) * g.seg_bytes,
+                            bulk_load(dst + (h * R + i) * g.seg_bytes,
                                       w + (row + i) * g.row_bytes + static_cast<size_t>(sg) * g.seg_bytes,
                                       static_cast<uint32_t>(g.seg_bytes), &full[s], pol);
                         }
@@ -125,53 +179,16 @@ __global__ void __launch_bounds__(kStreamThreads) matvec_stream_kernel(const Mat
     }
 
     const int tid = threadIdx.x - 32;
-    const int cw = warp - 1;
-    stage_vector<WT>([&](int j) { return __ldg(a.x + j); }, g.cols, NORM ? a.norm_w : nullptr, a.eps, xp, xc, red, tid,
+    stage_vector<WT>(GlobalVec4{a.x}, g.cols, NORM ? a.norm_w : nullptr, a.eps, xp, xc, red, tid,
                      kConsumerThreads, [] { named_barrier(1, kConsumerThreads); });
 
-    const int nc = g.cols / Chunk<WT>::kCols;
-    const int seg_chunks = g.seg_bytes / 16;
-    float* my_scratch = scratch + cw * 32;
-    for (int grp = cw; grp < n_groups; grp += kConsumerWarps) {
-        const int r0 = lo + grp * R;
-        const int nr = min(R, hi - r0);
-        const StageRows sr{r0, nr, nr * g.halves, g.out_rows};
-        float acc[MAXN];
-#pragma unroll
-        for (int i = 0; i < MAXN; ++i) acc[i] = 0.f;
-        bool ok = true;
-        for (int sg = 0; sg < g.n_seg; ++sg) {
-            const int t = grp * g.n_seg + sg;
-            const int s = t % kStreamStages;
-            if (!wait_phase(&full[s], (t / kStreamStages) & 1, err)) {
-                ok = false;
-                break;
-            }
-            tile_accumulate<WT, MAXN>(ring + s * kStageBytes, sr, g.seg_bytes, sg * seg_chunks, xp, nc, xc, a.scales, g.cols,
-                                      acc, lane);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-        }
-        if (!ok) return;
-#pragma unroll
-        for (int i = 0; i < MAXN; ++i) {
-            if (i < sr.n) {
-                const float v = warp_sum(acc[i]);
-                if (lane == 0) my_scratch[i] = finish_row<WT>(v, a.scales, sr.global_row(i));
-            }
-        }
-        __syncwarp();
-        if (lane < nr) {
-            const int r = r0 + lane;
-            if constexpr (EP == Epilogue::SWIGLU) {
-                a.y[r] = silu_f(my_scratch[lane]) * my_scratch[nr + lane];
-            } else if constexpr (EP == Epilogue::ADD) {
-                a.y[r] += my_scratch[lane];
-            } else {
-                a.y[r] = my_scratch[lane];
-            }
-        }
-        __syncwarp();
+    switch (R * g.halves) {
+        case 1: consume_groups<WT, EP, 1>(a, g, lo, hi, ring, full, empty, stage_tile, xp, xc, scratch, err); break;
+        case 2: consume_groups<WT, EP, 2>(a, g, lo, hi, ring, full, empty, stage_tile, xp, xc, scratch, err); break;
+        case 4: consume_groups<WT, EP, 4>(a, g, lo, hi, ring, full, empty, stage_tile, xp, xc, scratch, err); break;
+        case 8: consume_groups<WT, EP, 8>(a, g, lo, hi, ring, full, empty, stage_tile, xp, xc, scratch, err); break;
+        case 16: consume_groups<WT, EP, 16>(a, g, lo, hi, ring, full, empty, stage_tile, xp, xc, scratch, err); break;
+        default: consume_groups<WT, EP, 32>(a, g, lo, hi, ring, full, empty, stage_tile, xp, xc, scratch, err); break;
     }
 }
 

@@ -11,7 +11,8 @@ Procedure (fixed here; the reference does not define one):
     quantiser restated, block by block.
   * Prompts: `np.random.default_rng(seed).integers(0, 128256, n)` (batched: seed [seed, sequence]).
 Blocks are generated in parallel worker processes (spawn start method, safe after CUDA is in use)
-and written straight into a pre-sized file; a content digest (sha256 over per-block sha256s, in file
+and written straight into a pre-sized file. Because spawned workers re-import the caller's main
+module, a script that calls ensure_model/write_model must do so under `if __name__ == "__main__":`; a content digest (sha256 over per-block sha256s, in file
 order) identifies the result and is kept in a side file next to the model.
 """
 from __future__ import annotations

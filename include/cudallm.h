@@ -126,6 +126,14 @@ int cudallm_engine_path(cudallm_engine* e);
  * steps it enqueues; NULL / -1 for a NULL engine. */
 void* cudallm_engine_stream(cudallm_engine* e);
 int cudallm_engine_device(cudallm_engine* e);
+/* Step tracing (persistent path only): enable = 1 makes every following step record, per CTA, the
+ * %globaltimer value (ns) at each operation's dependency-wait begin / end, its end, and when the
+ * producer warp starts streaming its weights; 0 turns it off. */
+int cudallm_debug_trace(cudallm_engine* e, int enable);
+/* Copies the last traced step: grid x slots per-CTA values followed by 256 x 4 lm_head tile stamps of
+ * CTA 0 (count >= grid*slots + 1024); *grid_out, *slots_out get the shape. Waits for queued work first. */
+int cudallm_debug_read_trace(cudallm_engine* e, unsigned long long* out, unsigned long long count, int* grid_out,
+                             int* slots_out);
 
 #ifdef __cplusplus
 }

@@ -3,9 +3,15 @@ seeded Llama-3.2-1B files (golden_full_*.npz, made with the reference imported i
 
 Checks per engine configuration (reference tests/test_engine_vs_reference.py:10-94 and
 tests/test_generation.py, re-targeted at seeded weights and a random 32-token prompt):
-  * greedy token ids equal the reference's for all 64 generated tokens;
+  * greedy token ids equal the reference's for all 64 generated tokens (fp16 KV cache, the reference's
+    default). With a bf16 KV cache the reference itself meets a near tie (top-2 margin 6e-4 at generated
+    token 9) and a one-ulp bf16 rounding flip of a cached value moves logits by more than that, so there
+    ids must match up to the first step whose reference margin is below BF16_KV_MARGIN, and a
+    teacher-forced run (reference ids fed back) must pick the reference's argmax at every step whose
+    margin is at least BF16_KV_MARGIN;
   * logits at the last prompt step within max |delta| < 2e-2 and the same argmax;
-  * per-layer residuals (step_debug configurations) at steps 0 and 31 within rel-L2 < 1e-3;
+  * per-layer residuals (step_debug configurations) at steps 0 and 31 within rel-L2 < 1e-3 (fp16 KV, the
+    reference's tolerance) or < 3e-3 (bf16 KV: 8-bit mantissa, 8x coarser rounding of the cache);
   * the returned next token is the argmax of the returned logits;
   * reset then re-run of the first 4 steps gives bit-identical logits (CUDA-graph replay included).
 """
@@ -37,6 +43,8 @@ CONFIGS = [
     ("bf16", "opt", "opt", 1, 0, "bf16", "auto"),
 ]
 N_DET = 4
+BF16_KV_MARGIN = 2e-3
+RES_TOL = {"fp16": 1e-3, "bf16": 3e-3}
 
 
 def _cfg_id(cfg) -> str:
@@ -81,6 +89,10 @@ def runs(model_path, golden):
                 else:
                     rerun.append(eng.step_debug(t)[1])
             out["rerun"] = rerun
+            if kv == "bf16":
+                eng.reset()
+                forced = list(prompt) + [int(t) for t in g["ids"][:-1]]
+                out["forced_top1"] = [int(np.argmax(eng.step(t, want_logits=True)[1])) for t in forced]
         cache[cfg] = out
         return out
     return get
@@ -89,8 +101,17 @@ def runs(model_path, golden):
 @pytest.mark.parametrize("cfg", CONFIGS, ids=_cfg_id)
 def test_greedy_ids_match_reference(cfg, runs, golden):
     r = runs(cfg)
-    ref = golden(f"full_{cfg[0]}_{cfg[5]}")["ids"].tolist()
-    assert r["ids"] == ref
+    g = golden(f"full_{cfg[0]}_{cfg[5]}")
+    ref = g["ids"].tolist()
+    if cfg[5] == "fp16":
+        assert r["ids"] == ref
+        return
+    gen_margin = g["margin"][31:]  # margin of the step that chose generated token i
+    first_tie = next((i for i, m in enumerate(gen_margin) if m < BF16_KV_MARGIN), len(ref))
+    assert first_tie > 0 and r["ids"][:first_tie] == ref[:first_tie]
+    top1_ref = g["top8_i"][:, 0].tolist()
+    bad = [i for i, (a, b) in enumerate(zip(r["forced_top1"], top1_ref)) if a != b and g["margin"][i] >= BF16_KV_MARGIN]
+    assert not bad, f"teacher-forced argmax differs at steps {bad}"
 
 
 @pytest.mark.parametrize("cfg", CONFIGS, ids=_cfg_id)
@@ -115,7 +136,7 @@ def test_residuals_match_reference(cfg, runs, golden):
         assert eng.shape == ref.shape == (17, 2048)
         for k in range(17):
             rel = np.linalg.norm(eng[k] - ref[k]) / np.linalg.norm(ref[k])
-            assert rel < 1e-3, f"step {step}, residual {k}: relative error {rel:.3e}"
+            assert rel < RES_TOL[cfg[5]], f"step {step}, residual {k}: relative error {rel:.3e}"
 
 
 @pytest.mark.parametrize("cfg", CONFIGS, ids=_cfg_id)
@@ -161,3 +182,23 @@ def test_sequence_full_and_bad_token(model_path):
         assert eng.pos == 0
         nxt, _ = eng.step(1)
         assert 0 <= nxt < 128256
+
+
+@pytest.mark.parametrize("kv", ["fp16", "bf16"])
+def test_long_context_persistent_matches_per_op(model_path, kv):
+    """Past 1024 tokens the persistent kernel switches from whole-head attention to split-K across CTAs
+    with an ordered merge; it must agree with the per-op path (split-K kernels + separate RoPE/KV write,
+    themselves checked against float64 by the kernel tests) on the same token stream."""
+    path, _ = model_path("int4")
+    rng = np.random.default_rng(3)
+    toks = [int(t) for t in rng.integers(0, 128256, 1200)]
+    out = {}
+    for kind in ("persistent", "per_op"):
+        with Engine(path, kv_dtype=kv, path_kind=kind, max_seq_len=2048) as eng:
+            assert eng.decode_path == kind
+            for t in toks[:-4]:
+                eng.step_async(t)
+            out[kind] = [eng.step(t, want_logits=True)[1] for t in toks[-4:]]
+    for a, b in zip(out["persistent"], out["per_op"]):
+        assert np.max(np.abs(a - b)) < 2e-2
+        assert int(np.argmax(a)) == int(np.argmax(b))
