@@ -107,6 +107,14 @@ cudallm::EngineOptions to_options(const cudallm_options* opts, const cudallm_opt
 
 }  // namespace
 
+namespace cudallm {
+// Records ex for cudallm_last_error and returns its code; for entry points in other source files.
+int capi_report(const std::exception& ex) {
+    set_error(ex.what());
+    return error_code(ex);
+}
+}  // namespace cudallm
+
 extern "C" {
 
 const char* cudallm_last_error(void) { return g_last_error.c_str(); }

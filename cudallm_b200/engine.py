@@ -81,6 +81,9 @@ SIGNATURES = {
     "cudallm_engine_device": ([c_void_p], c_int),
     "cudallm_debug_trace": ([c_void_p, c_int], c_int),
     "cudallm_debug_read_trace": ([c_void_p, POINTER(c_ulonglong), c_ulonglong, _INT_P, _INT_P], c_int),
+    # device pointers: q, k_cache, v_cache, ctx, out, nh, nkv, hd, max_seq, stream
+    "cudallm_attention_noalloc": ([c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
+                                  c_int),
 }
 
 

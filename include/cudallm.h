@@ -135,6 +135,21 @@ int cudallm_debug_trace(cudallm_engine* e, int enable);
 int cudallm_debug_read_trace(cudallm_engine* e, unsigned long long* out, unsigned long long count, int* grid_out,
                              int* slots_out);
 
+/* No counterpart in the reference. Split-K decode attention (the kernels behind
+ * cudallm_kernel_attention impl 1) for callers that cannot allocate device memory: code whose device
+ * memory is owned by another runtime's pool, or loops that must not enter the driver's allocator.
+ * Every argument is caller-owned DEVICE memory: q [nh*hd] fp32, k_cache / v_cache [nkv][max_seq][hd]
+ * fp16 bits (16-byte aligned), out [nh*hd] fp32; ctx in [1, max_seq]; stream a cudaStream_t (NULL = the
+ * legacy default stream). The call only enqueues work on stream; it allocates nothing. The split-K
+ * partials live in one fixed device array of 1.03 MiB that every GPU loading the library holds until
+ * exit, so nh <= 32 and max_seq <= 8192 (and nh == 4*nkv, hd == 64, max_seq % 128 == 0); larger sizes
+ * return CUDALLM_ERR_INVALID_ARG. All calls share that array and it keeps the last call's contents, so
+ * calls whose GPU work overlaps (other streams or threads, same device) race: order them on one stream.
+ * The first call on each device, with that device current, looks up the array's device address
+ * (cudaGetSymbolAddress); make that first call before any stream capture that includes this function. */
+int cudallm_attention_noalloc(const float* q, const unsigned short* k_cache, const unsigned short* v_cache, int ctx,
+                              float* out, int nh, int nkv, int hd, int max_seq, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
