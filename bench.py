@@ -54,12 +54,14 @@ def measured_peaks() -> dict:
 
 def profiled_traffic(dtype: str) -> float | None:
     """DRAM bytes per decode-step launch from the committed ncu summary, if one exists."""
-    p = ROOT / "profiles" / "decode_step_traffic.json"
+    p = ROOT / "profiles" / "decode_step_traffic.txt"
     if not p.exists():
         return None
-    d = json.loads(p.read_text())
-    v = d.get(dtype)
-    return float(v["dram_bytes_per_launch"]) if v else None
+    for line in p.read_text().splitlines():
+        f = line.split()
+        if f and not f[0].startswith("#") and f[0] == dtype:
+            return float(f[1])
+    return None
 
 
 class ClockSampler:

@@ -112,7 +112,7 @@ __device__ __forceinline__ void trace_mark(const StepParams& p, int op, int slot
 }
 
 __device__ __forceinline__ void trace_tile(const StepParams& p, int o, int i, int slot) {
-    if (p.trace && blockIdx.x == 0 && o == kWeightOps - 1 && i < kTraceTiles) {
+    if (p.trace && blockIdx.x == 0 && o == p.trace_tile_op && i < kTraceTiles) {
         p.trace[static_cast<size_t>(gridDim.x) * kTraceSlots + i * kTraceTileStamps + slot] = global_ns();
     }
 }
@@ -493,6 +493,11 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
     if (c.tid == 0) {
         trace_mark(p, 0, 0);
         trace_mark(p, 0, 1);
+        if (p.trace) {  // the SM this CTA runs on (slot 3 of the step-end entry is otherwise unused)
+            unsigned smid;
+            asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+            p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + 81 * 4 + 3] = smid;
+        }
     }
     {
         // Residual rows this CTA owns in the O/down projections start as the embedding.

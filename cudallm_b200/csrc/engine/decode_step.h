@@ -39,10 +39,11 @@ constexpr int kStepLayers = 16;
 
 // Trace layout per CTA: operation k (layer l: 5l + {0 qkv, 1 attention, 2 o-proj, 3 gate/up, 4 down};
 // 80 lm_head; 81 step end) has 4 slots: dependency wait begins, wait ends, operation ends, producer
-// starts issuing its tiles (weight operations only).
+// starts issuing its tiles (weight operations only); slot 3 of entry 81 holds the CTA's SM id.
 constexpr int kTraceOps = 82;
 constexpr int kTraceSlots = kTraceOps * 4;
-// After the per-CTA slots: CTA 0's first kTraceTiles lm_head tiles, 4 stamps each (producer issues the
+// After the per-CTA slots: CTA 0's first kTraceTiles tiles of one weight operation (StepParams::trace_tile_op,
+// lm_head by default), 4 stamps each (producer issues the
 // copy, consumer starts waiting for it, the data is there, consumer is done with the tile).
 constexpr int kTraceTiles = 256;
 constexpr int kTraceTileStamps = 4;
@@ -88,6 +89,7 @@ struct StepParams {
     unsigned long long wait_limit_ns;
     int prefetch_tiles;  // L2 prefetch distance of the weight stream, in tiles beyond the copies
     int prefetch_mode;   // 0 none, 2 prefetch warp (load/store-unit prefetch instructions)
+    int trace_tile_op;   // weight operation (layer*4 + qkv/wo/gu/down, 64 = lm_head) whose tiles CTA 0 stamps
     TileGeom g_qkv, g_wo, g_gu, g_down, g_lm;
 };
 

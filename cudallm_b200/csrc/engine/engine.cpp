@@ -146,6 +146,8 @@ Engine::Engine(const std::string& path, const EngineOptions& opts) : opts_(opts)
             if (const char* env = std::getenv("CUDALLM_PREFETCH_TILES")) p.prefetch_tiles = std::max(0, std::atoi(env));
             p.prefetch_mode = 2;
             if (const char* env = std::getenv("CUDALLM_PREFETCH_MODE")) p.prefetch_mode = std::atoi(env);
+            p.trace_tile_op = 64;  // lm_head; CUDALLM_TRACE_TILE_OP picks another operation's tiles to stamp
+            if (const char* env = std::getenv("CUDALLM_TRACE_TILE_OP")) p.trace_tile_op = std::atoi(env);
             // The persistent kernel is compiled for the default tile shape (matvec_rpb selects the tile rows of
             // the per-op kernels only; results do not depend on it).
             const int rpb = 0;

@@ -1,0 +1,105 @@
+"""Timeline of one persistent decode step, read from the kernel's own %globaltimer stamps.
+
+    python -m cudallm_b200.timeline [--dtype bf16|int8|int4] [--kv bf16|fp16] [--prompt 32] [--tile-op N]
+
+Runs a seeded prompt through the engine, traces the next step (cudallm_debug_trace) and prints:
+  * per operation (layers 0, 1, 15 and the lm_head): when the dependency wait begins and ends, when the
+    operation ends (median and slowest CTA) and when the copy producer started streaming its weights;
+  * per layer, averaged over the 16 layers: the critical duration of each operation (slowest CTA's end
+    minus the slowest CTA's wait end) and the median dependency wait;
+  * the tiles of one weight operation on CTA 0 (--tile-op: layer*4 + {0 qkv, 1 o-proj, 2 gate/up,
+    3 down}, 64 = lm_head): copy issued, consumer starts waiting, data ready, consumer done;
+  * for gate/up and down of layer 1, the per-CTA durations (straggler spread) and the slowest SMs.
+Times are microseconds from the start of the step. Stamp layout: csrc/engine/decode_step.h.
+"""
+from __future__ import annotations
+
+import argparse
+import os
+
+import numpy as np
+
+LAYERS = 16
+
+
+def op_names() -> list[str]:
+    names = []
+    for layer in range(LAYERS):
+        names += [f"L{layer}.qkv", f"L{layer}.att", f"L{layer}.wo", f"L{layer}.gu", f"L{layer}.down"]
+    return names + ["lm", "end"]
+
+
+def capture(dtype: str, kv: str, prompt: int, tile_op: int | None) -> tuple[np.ndarray, np.ndarray]:
+    if tile_op is not None:
+        os.environ["CUDALLM_TRACE_TILE_OP"] = str(tile_op)  # read when the engine is created
+    from . import synth
+    from .engine import Engine
+    path, _ = synth.ensure_model(dtype)
+    with Engine(path, kv_dtype=kv) as eng:
+        for t in synth.prompt_ids(prompt):
+            eng.step_async(t)
+        for _ in range(4):
+            eng.step_async(None)
+        eng.synchronize()
+        eng.trace(True)
+        eng.step_async(None)
+        tr, tt = eng.read_trace()
+    return tr.astype(np.int64), tt.astype(np.int64)
+
+
+def report(tr: np.ndarray, tt: np.ndarray, tile_op: int) -> None:
+    names = op_names()
+    t0 = tr[:, 0, 0].min()
+    us = lambda a: a / 1e3  # noqa: E731
+    print("op        wait_begin  wait_end_max  wait_med  wait_max  end_max  end_med  producer_start_med")
+    for k, name in enumerate(names[:-1]):
+        if not name.startswith(("L0.", "L1.", "L15.", "lm")):
+            continue
+        wb, we, oe, pr = (tr[:, k, i] - t0 for i in range(4))
+        prod = us(np.median(pr)) if (tr[:, k, 3] > 0).any() and not name.endswith(".att") else float("nan")
+        print(f"{name:9s} {us(np.median(wb)):10.1f} {us(we.max()):13.1f} {us(np.median(we - wb)):9.1f} "
+              f"{us((we - wb).max()):9.1f} {us(oe.max()):8.1f} {us(np.median(oe)):8.1f} {prod:18.1f}")
+    span = us((tr[:, 80, 2] - t0).max())
+    waits = us(np.sum([tr[:, k, 1] - tr[:, k, 0] for k in range(81)], axis=0))
+    print(f"step span {span:.1f} us; per-CTA total dependency wait: median {np.median(waits):.1f} us, "
+          f"max {waits.max():.1f} us")
+    print("per layer (mean over 16 layers): critical duration / median wait, us")
+    for kind in ("qkv", "att", "wo", "gu", "down"):
+        ks = [i for i, n in enumerate(names) if n.endswith("." + kind)]
+        dur = np.mean([us((tr[:, k, 2] - t0).max() - (tr[:, k, 1] - t0).max()) for k in ks])
+        wt = np.mean([us(np.median(tr[:, k, 1] - tr[:, k, 0])) for k in ks])
+        print(f"  {kind:5s} {dur:6.2f} / {wt:5.2f}")
+    n = int((tt[:, 0] > 0).sum())
+    if n:
+        tt = us(tt[:n] - tt[0, 0])
+        issue, wstart, ready, done = (tt[:, k] for k in range(4))
+        print(f"tiles of weight operation {tile_op} on CTA 0 ({n}): issue / wait start / ready / done, us")
+        for i in range(min(n, 48)):
+            print(f"  {i:3d} {issue[i]:8.2f} {wstart[i]:8.2f} {ready[i]:8.2f} {done[i]:8.2f}   "
+                  f"issue->ready {ready[i] - issue[i]:6.2f}  wait {ready[i] - wstart[i]:5.2f}  "
+                  f"compute {done[i] - ready[i]:5.2f}")
+        print(f"  median issue->ready {np.median(ready - issue):.2f}, data wait {np.median(ready - wstart):.2f}, "
+              f"compute {np.median(done - ready):.2f} us")
+    sm = tr[:, 81, 3]
+    for name in ("L1.gu", "L1.down"):
+        k = names.index(name)
+        dur = us(tr[:, k, 2] - tr[:, k, 1])
+        slow = np.argsort(-dur)[:6]
+        print(f"{name}: per-CTA duration median {np.median(dur):.2f} max {dur.max():.2f} us; slowest (SM, us): "
+              + ", ".join(f"({int(sm[i])}, {dur[i]:.1f})" for i in slow))
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--dtype", choices=("bf16", "int8", "int4"), default="bf16")
+    ap.add_argument("--kv", choices=("bf16", "fp16"), default="bf16")
+    ap.add_argument("--prompt", type=int, default=32)
+    ap.add_argument("--tile-op", type=int, default=None)
+    args = ap.parse_args(argv)
+    tr, tt = capture(args.dtype, args.kv, args.prompt, args.tile_op)
+    report(tr, tt, 64 if args.tile_op is None else args.tile_op)
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
