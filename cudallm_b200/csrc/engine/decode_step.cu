@@ -17,9 +17,18 @@ namespace cudallm {
 
 namespace {
 
-constexpr int kCw = 8;             // consumer warps
+constexpr int kCw = 8;             // consumer warps (warpgroups 1 and 2)
 constexpr int kCt = 32 * kCw;      // consumer threads
-constexpr int kThreads = 64 + kCt; // + copy-producer warp + L2-prefetch warp
+// Warpgroup 0: the copy-producer warp, the L2-prefetch warp and two idle warps. Warpgroups exchange
+// registers at start (setmaxnreg): the block is launched with kLaunchRegs per thread; warpgroup 0 drops
+// to kProducerRegs and the consumers rise to kConsumerRegs. The two shares add up to exactly the launch
+// allocation (the host checks the kernel's register count before the first launch), so the increase
+// never waits for registers that are not there.
+constexpr int kThreads = 128 + kCt;
+constexpr int kLaunchRegs = 168;  // 65536 / 384 rounded down to a multiple of 8
+constexpr int kProducerRegs = 72;
+constexpr int kConsumerRegs = 216;
+static_assert(kProducerRegs * 128 + kConsumerRegs * kCt == kLaunchRegs * kThreads, "register split must use the launch pool");
 constexpr int kStages = 12;
 // Producer lanes: lane j of warp 0 issues the tiles t with t % kProducers == j, i.e. it owns the stages
 // s with s % kProducers == j, so four issue loops (each ~0.2-0.5 us per copy) run concurrently.
@@ -55,9 +64,7 @@ static_assert(kOffTiles + kStages * 4 <= kOffFlags, "barriers overflow");
 static_assert(kOffAm + kCw * 8 <= kOffXc, "argmax scratch overflow");
 static_assert(kOffXc + (kMaxK / 32) * 4 <= kOffXp, "chunk sums overflow");
 static_assert(sizeof(AttSmem<__half>) <= kMaxK * 4, "attention scratch must fit in the vector area");
-static_assert(sizeof(HeadSmem<__half>) <= kMaxK * 4, "attention scratch must fit in the vector area");
-// Contexts up to this many 64-token tiles use the whole-head attention (one CTA per KV head).
-constexpr int kWholeHeadMaxTiles = 16;
+static_assert(sizeof(HeadPassSmem<__half>) <= kMaxK * 4, "attention scratch must fit in the vector area");
 static_assert(kOffRing % 128 == 0, "ring alignment");
 
 // Stage rows of each operation's tile (rows per tile x halves); the host builds the persistent path's
@@ -268,8 +275,14 @@ __device__ void run_prefetcher(const StepParams& p, volatile Flags* fl) {
             for (int r = 0; r < (g.n_seg == 1 ? 1 : nr); ++r) {
                 const uint8_t* a = pf.op.w + (row + r) * g.row_bytes + static_cast<size_t>(sg) * g.seg_bytes;
                 const int bytes = g.n_seg == 1 ? nr * g.row_bytes : g.seg_bytes;
-                for (int off = lane * 128; off < bytes; off += 32 * 128) {
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(a + off) : "memory");
+                if (p.prefetch_mode == 3) {
+                    for (int off = lane * 128; off < bytes; off += 32 * 128) {
+                        asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(a + off) : "memory");
+                    }
+                } else {
+                    for (int off = lane * 128; off < bytes; off += 32 * 128) {
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(a + off) : "memory");
+                    }
                 }
             }
         }
@@ -487,7 +500,7 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
     const int tok = p.token_override >= 0 ? p.token_override : *p.d_token;
     const int n_tiles = (ctx + kAttnTile - 1) / kAttnTile;
     const int n_slots = p.max_seq / kAttnTile;
-    const bool whole_head = n_tiles <= kWholeHeadMaxTiles;
+    const bool whole_head = n_tiles <= p.whole_head_max_tiles;
     const int head_stride = G / kNkv;
     rope_table(p.inv_freq, pos, cs, c.tid);
     if (c.tid == 0) {
@@ -541,15 +554,15 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
             snorm = p.layers[l].attn_norm;
         } else if (kind == kWo) {
             // RoPE + KV write + attention, then the O projection's input.
-            if (!dep_wait(c, p.sync + kSyncQkv + l, G, 30u + l, l * 5 + 1)) return;
             const size_t layer_off = static_cast<size_t>(l) * kNkv * p.max_seq * kHd;
             KV* kc = static_cast<KV*>(p.k_cache) + layer_off;
             KV* vc = static_cast<KV*>(p.v_cache) + layer_off;
+            if (!dep_wait(c, p.sync + kSyncQkv + l, G, 30u + l, l * 5 + 1)) return;
             if (whole_head) {
                 if (blockIdx.x % head_stride == 0 && blockIdx.x / head_stride < kNkv) {
-                    HeadSmem<KV>& sm = *reinterpret_cast<HeadSmem<KV>*>(c.xp);
-                    attend_head<KV>(p.qkv, kNh, kNkv, cs, kc, vc, p.max_seq, blockIdx.x / head_stride, ctx, p.att, sm, c.tid,
-                                    [] { csync(); });
+                    HeadPassSmem<KV>& sm = *reinterpret_cast<HeadPassSmem<KV>*>(c.xp);
+                    attend_head_pass<KV>(p.qkv, kNh, kNkv, cs, kc, vc, p.max_seq, blockIdx.x / head_stride, ctx, p.att, sm,
+                                         c.tid, [] { csync(); });
                     signal(c, p.sync + kSyncAtt + l);
                 }
             } else {
@@ -679,14 +692,16 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         fence_barrier_init();
     }
     __syncthreads();
-    if (threadIdx.x < 32) {
-        if (threadIdx.x < kProducers) run_producer(p, ring, full, empty, stage_tile, fl, threadIdx.x);
+    if (threadIdx.x < 128) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
+        if (threadIdx.x < kProducers) {
+            run_producer(p, ring, full, empty, stage_tile, fl, threadIdx.x);
+        } else if (threadIdx.x >= 32 && threadIdx.x < 64 && p.prefetch_mode >= 2) {
+            run_prefetcher(p, fl);
+        }
         return;
     }
-    if (threadIdx.x < 64) {
-        if (p.prefetch_mode == 2) run_prefetcher(p, fl);
-        return;
-    }
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kConsumerRegs));
     ConsumerCtx c;
     c.p = &p;
     c.ring = ring;
@@ -698,7 +713,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     c.xc = reinterpret_cast<float*>(smem + kOffXc);
     c.red = reinterpret_cast<float*>(smem + kOffRed);
     c.scratch = reinterpret_cast<float*>(smem + kOffScratch);
-    c.tid = threadIdx.x - 64;
+    c.tid = threadIdx.x - 128;
     c.cw = c.tid >> 5;
     c.lane = c.tid & 31;
     c.t_base = 0;
@@ -717,6 +732,9 @@ void launch_typed(const StepParams& p, cudaStream_t stream) {
         int blocks = 0;
         CLLM_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kThreads, kSmemBytes));
         CLLM_CHECK(blocks >= 1, "decode step: the persistent kernel does not fit on an SM");
+        cudaFuncAttributes fa{};
+        CLLM_CUDA(cudaFuncGetAttributes(&fa, kernel));
+        CLLM_CHECK(fa.numRegs == kLaunchRegs, "decode step: unexpected register count; the warpgroup register split assumes 168");
         configured[dev] = true;
     }
     void* args[] = {const_cast<StepParams*>(&p)};

@@ -88,7 +88,8 @@ struct StepParams {
     int group_size;
     unsigned long long wait_limit_ns;
     int prefetch_tiles;  // L2 prefetch distance of the weight stream, in tiles beyond the copies
-    int prefetch_mode;   // 0 none, 2 prefetch warp (load/store-unit prefetch instructions)
+    int prefetch_mode;   // 0 none, 2 prefetch warp (load/store-unit prefetch instructions), 3 same with evict_last
+    int whole_head_max_tiles;  // contexts up to this many 64-token tiles use one CTA per KV head for attention
     int trace_tile_op;   // weight operation (layer*4 + qkv/wo/gu/down, 64 = lm_head) whose tiles CTA 0 stamps
     TileGeom g_qkv, g_wo, g_gu, g_down, g_lm;
 };

@@ -56,8 +56,11 @@ void alloc(T** p, size_t count) {
 }
 
 constexpr unsigned long long kStepWaitLimitNs = 1000000000ull;  // 1 s per inter-CTA wait
+// Contexts up to this many 64-token tiles use the whole-head attention (one CTA per KV head); longer ones
+// spread (head, tile) items over all CTAs. CUDALLM_WHOLE_HEAD_MAX_TILES overrides it.
+constexpr int kDefaultWholeHeadMaxTiles = 2;
 // L2 prefetch distance (tiles of 16 KiB per SM) of the persistent step; CUDALLM_PREFETCH_TILES overrides it.
-constexpr int kDefaultPrefetchTiles = 16;
+constexpr int kDefaultPrefetchTiles = 24;
 
 }  // namespace
 
@@ -146,6 +149,8 @@ Engine::Engine(const std::string& path, const EngineOptions& opts) : opts_(opts)
             if (const char* env = std::getenv("CUDALLM_PREFETCH_TILES")) p.prefetch_tiles = std::max(0, std::atoi(env));
             p.prefetch_mode = 2;
             if (const char* env = std::getenv("CUDALLM_PREFETCH_MODE")) p.prefetch_mode = std::atoi(env);
+            p.whole_head_max_tiles = kDefaultWholeHeadMaxTiles;
+            if (const char* env = std::getenv("CUDALLM_WHOLE_HEAD_MAX_TILES")) p.whole_head_max_tiles = std::atoi(env);
             p.trace_tile_op = 64;  // lm_head; CUDALLM_TRACE_TILE_OP picks another operation's tiles to stamp
             if (const char* env = std::getenv("CUDALLM_TRACE_TILE_OP")) p.trace_tile_op = std::atoi(env);
             // The persistent kernel is compiled for the default tile shape (matvec_rpb selects the tile rows of

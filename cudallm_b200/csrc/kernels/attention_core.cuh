@@ -207,17 +207,6 @@ __device__ __forceinline__ void combine_head(const float* part_o, const float* p
 // CTA, so there is no second pass. Lane j scores tokens t0+j and t0+j+32; for p.V, lane group
 // g = lane/8 takes tokens t0 + 4i + g and lane sub = lane%8 owns dims 8*sub .. 8*sub+7.
 template <typename KV>
-struct HeadSmem {
-    float qs[kGqa][kHd];
-    alignas(16) KV kn[kHd];
-    alignas(16) KV vn[kHd];
-    float ps[8][kGqa][kAttnTile];
-    float wm[8][kGqa];
-    float wl[8][kGqa];
-    float wo[8][kGqa][kHd];
-};
-
-template <typename KV>
 __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
     using KV2 = typename Kv2<KV>::T;
     const KV2* h2 = reinterpret_cast<const KV2*>(&u);
@@ -229,12 +218,62 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
     }
 }
 
+// ---- Whole-head attention (short contexts) -------------------------------------------------------
+// One 256-thread group computes all 4 query heads of KV head h over the whole context, in passes of
+// 128 tokens: warp w owns tokens p0 + 16w + i. For the scores, lane pair (2i, 2i+1) holds the key row of
+// token i (dims 0-31 and 32-63); for p.V, lane l holds V[token][2l .. 2l+1] of each of the 16 tokens.
+// A pass's key loads are issued together (in pass 0 together with the new token's q/k/v) and its value
+// loads right after the scores, so a pass costs about one L2 round trip. Each warp keeps a running softmax (max, sum, p.V) per query head; the 8 warp
+// states are merged in warp order.
+constexpr int kHeadWarpTokens = 16;
+constexpr int kHeadPassTokens = 8 * kHeadWarpTokens;
+
+template <typename KV>
+struct HeadPassSmem {
+    float qs[kGqa][kHd];
+    alignas(16) KV kn[kHd];
+    alignas(16) KV vn[kHd];
+    float4 ps[8][kHeadWarpTokens];  // p of the 4 query heads for each token of the warp
+    float wm[8][kGqa];
+    float wl[8][kGqa];
+    float wo[8][kGqa][kHd];
+};
+
+// Key loads (lane pair per token) and value loads (row by row) of pass `pass` for warp w: cached
+// tokens below pos only (the current token is inserted from shared memory); everything else is zero.
+template <typename KV>
+__device__ __forceinline__ void head_load_keys(const KV* k_cache, int max_seq, int h, int pos, int pass, int w, int lane,
+                                               uint4 (&k)[4]) {
+    const KV* Kh = k_cache + static_cast<size_t>(h) * max_seq * kHd;
+    const int j = pass * kHeadPassTokens + kHeadWarpTokens * w + (lane >> 1);
+    const uint4* krow = reinterpret_cast<const uint4*>(Kh + static_cast<size_t>(j) * kHd) + 4 * (lane & 1);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) k[c] = j < pos ? __ldcg(krow + c) : make_uint4(0, 0, 0, 0);
+}
+template <typename KV>
+__device__ __forceinline__ void head_load_values(const KV* v_cache, int max_seq, int h, int pos, int pass, int w, int lane,
+                                                 uint32_t (&v)[kHeadWarpTokens]) {
+    const KV* Vh = v_cache + static_cast<size_t>(h) * max_seq * kHd;
+    const int base = pass * kHeadPassTokens + kHeadWarpTokens * w;
+#pragma unroll
+    for (int i = 0; i < kHeadWarpTokens; ++i) {
+        v[i] = base + i < pos ? __ldcg(reinterpret_cast<const uint32_t*>(Vh + static_cast<size_t>(base + i) * kHd) + lane) : 0u;
+    }
+}
+
+// Attention of KV head h for context ctx (= pos + 1): rotates the 4 query heads and the new key
+// (cs = rope table of pos), rounds k and v to the cache type, writes them to the cache and uses the
+// rounded values. out receives [4][64] at query head 4h. `sync()` is a barrier over the 256
+// participating threads.
 template <typename KV, typename Sync>
-__device__ __forceinline__ void attend_head(const float* qkv, int nh, int nkv, const float* cs, KV* k_cache, KV* v_cache,
-                                            int max_seq, int h, int ctx, float* out, HeadSmem<KV>& sm, int tid, Sync sync) {
+__device__ __forceinline__ void attend_head_pass(const float* qkv, int nh, int nkv, const float* cs, KV* k_cache, KV* v_cache,
+                                                 int max_seq, int h, int ctx, float* out, HeadPassSmem<KV>& sm, int tid,
+                                                 Sync sync) {
+    using KV2 = typename Kv2<KV>::T;
     const int pos = ctx - 1;
     const int w = tid >> 5, lane = tid & 31;
-    // Rotated query heads, and the new token's k (rotated) and v, rounded to the cache type.
+    uint4 k[4];
+    if (kHeadWarpTokens * w < ctx) head_load_keys<KV>(k_cache, max_seq, h, pos, 0, w, lane, k);
     if (tid < kGqa * kHd / 2) {
         const int g = tid >> 5, i = tid & 31;
         const float* q = qkv + (h * kGqa + g) * kHd;
@@ -244,8 +283,8 @@ __device__ __forceinline__ void attend_head(const float* qkv, int nh, int nkv, c
         sm.qs[g][i + kHd / 2] = x1 * c + x0 * s;
     } else if (tid < kGqa * kHd / 2 + kHd / 2) {
         const int i = tid - kGqa * kHd / 2;
-        const float* k = qkv + (nh + h) * kHd;
-        const float x0 = __ldcg(k + i), x1 = __ldcg(k + i + kHd / 2);
+        const float* kp = qkv + (nh + h) * kHd;
+        const float x0 = __ldcg(kp + i), x1 = __ldcg(kp + i + kHd / 2);
         const float c = cs[i], s = cs[kHd / 2 + i];
         const KV k0 = to_kv<KV>(x0 * c - x1 * s), k1 = to_kv<KV>(x1 * c + x0 * s);
         sm.kn[i] = k0;
@@ -255,96 +294,81 @@ __device__ __forceinline__ void attend_head(const float* qkv, int nh, int nkv, c
         kdst[i + kHd / 2] = k1;
     } else if (tid < kGqa * kHd / 2 + kHd / 2 + kHd) {
         const int d = tid - kGqa * kHd / 2 - kHd / 2;
-        const KV v = to_kv<KV>(__ldcg(qkv + (nh + nkv + h) * kHd + d));
-        sm.vn[d] = v;
-        v_cache[(static_cast<size_t>(h) * max_seq + pos) * kHd + d] = v;
+        const KV vv = to_kv<KV>(__ldcg(qkv + (nh + nkv + h) * kHd + d));
+        sm.vn[d] = vv;
+        v_cache[(static_cast<size_t>(h) * max_seq + pos) * kHd + d] = vv;
     }
     sync();
-    const KV* Kh = k_cache + static_cast<size_t>(h) * max_seq * kHd;
-    const KV* Vh = v_cache + static_cast<size_t>(h) * max_seq * kHd;
-    const int n_tiles = (ctx + kAttnTile - 1) / kAttnTile;
-    const int g = lane >> 3, sub = lane & 7;
-    float m_run[kGqa], l_run[kGqa], o_run[kGqa][8];
+    float m_run[kGqa], l_run[kGqa], o[kGqa][2];
 #pragma unroll
     for (int hq = 0; hq < kGqa; ++hq) {
         m_run[hq] = -INFINITY;
         l_run[hq] = 0.f;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o_run[hq][e] = 0.f;
+        o[hq][0] = o[hq][1] = 0.f;
     }
-    for (int tl = w; tl < n_tiles; tl += 8) {
-        const int t0 = tl * kAttnTile;
-        // Scores for tokens t0 + lane (half 0) and t0 + lane + 32 (half 1), one key row at a time.
-        float sc[2][kGqa];
-#pragma unroll 1
-        for (int half = 0; half < 2; ++half) {
-            const int j = t0 + lane + 32 * half;
-            const uint4* src = (j < ctx && j != pos) ? reinterpret_cast<const uint4*>(Kh + static_cast<size_t>(j) * kHd)
-                                                     : reinterpret_cast<const uint4*>(sm.kn);
-            uint4 kr[8];
+    const int n_pass = (ctx + kHeadPassTokens - 1) / kHeadPassTokens;
+    for (int pass = 0; pass < n_pass; ++pass) {
+        const int base = pass * kHeadPassTokens + kHeadWarpTokens * w;
+        if (base >= ctx) break;  // warp-uniform: no token of this warp is in the context
+        if (pass > 0) head_load_keys<KV>(k_cache, max_seq, h, pos, pass, w, lane, k);
+        const int j = base + (lane >> 1), half = lane & 1;
+        if (j == pos) {
 #pragma unroll
-            for (int c = 0; c < 8; ++c) kr[c] = (j < ctx && j != pos) ? __ldcg(src + c) : src[c];
-            float dot[kGqa] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                float kf[8];
-                unpack8<KV>(kr[c], kf);
-#pragma unroll
-                for (int hq = 0; hq < kGqa; ++hq) {
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) dot[hq] = fmaf(kf[e], sm.qs[hq][8 * c + e], dot[hq]);
-                }
-            }
-#pragma unroll
-            for (int hq = 0; hq < kGqa; ++hq) sc[half][hq] = j < ctx ? 0.125f * dot[hq] : -INFINITY;
+            for (int c = 0; c < 4; ++c) k[c] = reinterpret_cast<const uint4*>(sm.kn)[4 * half + c];
         }
-        // Running softmax: rescale the state to the new maximum, weight this tile's p by it directly.
+        float dot[kGqa] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            float kf[8];
+            unpack8<KV>(k[c], kf);
+#pragma unroll
+            for (int hq = 0; hq < kGqa; ++hq) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) dot[hq] = fmaf(kf[e], sm.qs[hq][32 * half + 8 * c + e], dot[hq]);
+            }
+        }
+        // Values: loaded once the key registers are free; their latency overlaps the softmax.
+        uint32_t v[kHeadWarpTokens];
+        head_load_values<KV>(v_cache, max_seq, h, pos, pass, w, lane, v);
+        if (pos >= base && pos < base + kHeadWarpTokens) {
+#pragma unroll
+            for (int i = 0; i < kHeadWarpTokens; ++i) {
+                if (base + i == pos) v[i] = reinterpret_cast<const uint32_t*>(sm.vn)[lane];
+            }
+        }
+        float pj[kGqa];
 #pragma unroll
         for (int hq = 0; hq < kGqa; ++hq) {
-            const float mn = fmaxf(m_run[hq], warp_max(fmaxf(sc[0][hq], sc[1][hq])));
+            const float d = dot[hq] + __shfl_xor_sync(0xffffffffu, dot[hq], 1);  // both halves of the row
+            const float sc = j < ctx ? 0.125f * d : -INFINITY;
+            const float mn = fmaxf(m_run[hq], warp_max(sc));  // finite: the warp's first token is in the context
             const float a = expf(m_run[hq] - mn);
-            const float pa = expf(sc[0][hq] - mn), pb = expf(sc[1][hq] - mn);
-            sm.ps[w][hq][lane] = pa;
-            sm.ps[w][hq][lane + 32] = pb;
-            l_run[hq] = l_run[hq] * a + warp_sum(pa + pb);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) o_run[hq][e] *= a;
+            pj[hq] = expf(sc - mn);
+            l_run[hq] = l_run[hq] * a + 0.5f * warp_sum(pj[hq]);  // every token is counted by its two lanes
+            o[hq][0] *= a;
+            o[hq][1] *= a;
             m_run[hq] = mn;
         }
+        if (half == 0) sm.ps[w][lane >> 1] = make_float4(pj[0], pj[1], pj[2], pj[3]);
         __syncwarp();
-#pragma unroll 1
-        for (int batch = 0; batch < 2; ++batch) {
-            uint4 vr[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int j = t0 + 4 * (8 * batch + i) + g;
-                vr[i] = (j < ctx && j != pos) ? __ldcg(reinterpret_cast<const uint4*>(Vh + static_cast<size_t>(j) * kHd) + sub)
-                                              : reinterpret_cast<const uint4*>(sm.vn)[sub];
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int jt = 4 * (8 * batch + i) + g;  // token within the tile; p is 0 past the context
-                float vf[8];
-                unpack8<KV>(vr[i], vf);
-#pragma unroll
-                for (int hq = 0; hq < kGqa; ++hq) {
-                    const float pv = sm.ps[w][hq][jt];
-#pragma unroll
-                    for (int e = 0; e < 8; ++e) o_run[hq][e] = fmaf(pv, vf[e], o_run[hq][e]);
-                }
-            }
+        for (int i = 0; i < kHeadWarpTokens; ++i) {
+            const float4 p4 = sm.ps[w][i];
+            const float2 vf = kv2_to_float2(*reinterpret_cast<const KV2*>(&v[i]));
+            o[0][0] = fmaf(p4.x, vf.x, o[0][0]);
+            o[0][1] = fmaf(p4.x, vf.y, o[0][1]);
+            o[1][0] = fmaf(p4.y, vf.x, o[1][0]);
+            o[1][1] = fmaf(p4.y, vf.y, o[1][1]);
+            o[2][0] = fmaf(p4.z, vf.x, o[2][0]);
+            o[2][1] = fmaf(p4.z, vf.y, o[2][1]);
+            o[3][0] = fmaf(p4.w, vf.x, o[3][0]);
+            o[3][1] = fmaf(p4.w, vf.y, o[3][1]);
         }
         __syncwarp();
     }
 #pragma unroll
     for (int hq = 0; hq < kGqa; ++hq) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            float v = o_run[hq][e];
-            v += __shfl_xor_sync(0xffffffffu, v, 8);
-            v += __shfl_xor_sync(0xffffffffu, v, 16);
-            if (g == 0) sm.wo[w][hq][8 * sub + e] = v;
-        }
+        *reinterpret_cast<float2*>(&sm.wo[w][hq][2 * lane]) = make_float2(o[hq][0], o[hq][1]);
         if (lane == 0) {
             sm.wm[w][hq] = m_run[hq];
             sm.wl[w][hq] = l_run[hq];
@@ -359,13 +383,12 @@ __device__ __forceinline__ void attend_head(const float* qkv, int nh, int nkv, c
         float L = 0.f, O = 0.f;
 #pragma unroll
         for (int ww = 0; ww < 8; ++ww) {
-            const float e = expf(sm.wm[ww][hq] - M);
+            const float e = expf(sm.wm[ww][hq] - M);  // 0 for a warp that had no token
             L = fmaf(sm.wl[ww][hq], e, L);
             O = fmaf(sm.wo[ww][hq][d], e, O);
         }
         __stcg(out + (h * kGqa + hq) * kHd + d, O / L);
     }
-    sync();
 }
 
 }  // namespace cudallm
