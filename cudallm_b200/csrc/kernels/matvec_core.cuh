@@ -7,12 +7,13 @@
 // grid and the kernel that runs it.
 //
 // The input vector is staged once per operation into shared memory as "planes": float4 p of chunk c
-// is stored at plane p, slot c, so the 32 lanes of a warp read 32 consecutive float4 (no bank
-// conflicts) and each float4 lines up with the lanes' in-register weight unpacking:
-//   bf16: 8 cols/chunk, word k = cols (2k, 2k+1)            -> planes hold cols 0-3, 4-7
-//   int8: 16 cols/chunk, word k = cols 4k..4k+3             -> plane k = cols 4k..4k+3
+// (its columns 4p..4p+3) is stored at plane p, slot c, so the 32 lanes of a warp read 32 consecutive
+// float4 (no bank conflicts). Each float4 holds two (even, odd) column pairs, which are the operand
+// pairs of the packed FMAs: a lane keeps two accumulation chains per row, one over the even and one
+// over the odd columns of its chunks.
+//   bf16: 8 cols/chunk, word k = cols (2k, 2k+1)
+//   int8: 16 cols/chunk, word k = cols 4k..4k+3
 //   int4: 32 cols/chunk, word k byte b = cols 8k+2b (low nibble), 8k+2b+1 (high nibble)
-//         -> plane 2k = even cols 8k+{0,2,4,6}, plane 2k+1 = odd cols 8k+{1,3,5,7}
 // Dequantisation follows the reference formats (wasiqnauman/cudallm python/cudallm/quantize.py:5-29,
 // src/kernels/matvec_opt.cu:65-115) but not its arithmetic:
 //   int8: q = byte value, one fp32 scale per row applied after the row reduction.
@@ -52,16 +53,7 @@ __device__ __forceinline__ int plane_offset(int j, int nc) {
     constexpr int C = Chunk<WT>::kCols;
     const int c = j / C;
     const int i = j % C;
-    int plane, comp;
-    if constexpr (WT == WeightType::INT4) {
-        const int k = i >> 3, e = i & 7;
-        plane = 2 * k + (e & 1);
-        comp = e >> 1;
-    } else {
-        plane = i >> 2;
-        comp = i & 3;
-    }
-    return (plane * nc + c) * 4 + comp;
+    return ((i >> 2) * nc + c) * 4 + (i & 3);
 }
 
 __device__ __forceinline__ float warp_sum(float v) {
@@ -138,24 +130,18 @@ __device__ __forceinline__ void stage_vector(Src4 src4, int K, const float* __re
         const int q = tid + i * nthr;
         if (q >= n4) continue;
         const int c = (4 * q) / C, i0 = (4 * q) % C;
-        if constexpr (WT == WeightType::INT4) {
-            const int k = i0 >> 3, e = (i0 & 7) >> 1;  // e = 0 or 2: component of the pair
-            float2* even = reinterpret_cast<float2*>(xp + ((2 * k) * nc + c) * 4 + e);
-            float2* odd = reinterpret_cast<float2*>(xp + ((2 * k + 1) * nc + c) * 4 + e);
-            *even = make_float2(v[i].x, v[i].z);
-            *odd = make_float2(v[i].y, v[i].w);
-        } else {
-            p4[(i0 >> 2) * nc + c] = v[i];
-        }
+        p4[(i0 >> 2) * nc + c] = v[i];
     }
     sync();
     if constexpr (WT == WeightType::INT4) {
         for (int c = tid; c < nc; c += nthr) {
+            // Per word k: the even columns 8k, 8k+2, 8k+4, 8k+6, then the odd ones.
             float s = 0.f;
 #pragma unroll
-            for (int pl = 0; pl < Chunk<WT>::kPlanes; ++pl) {
-                const float4 t = p4[pl * nc + c];
-                s += t.x + t.y + t.z + t.w;
+            for (int k = 0; k < 4; ++k) {
+                const float4 a = p4[(2 * k) * nc + c], b = p4[(2 * k + 1) * nc + c];
+                s += a.x + a.z + b.x + b.z;
+                s += a.y + a.w + b.y + b.w;
             }
             xc[c] = s;
         }
@@ -176,6 +162,8 @@ __device__ __forceinline__ float bf16hi(uint32_t w) { return __uint_as_float(w &
 __device__ __forceinline__ float i8val(uint32_t wb, uint32_t sel) {
     return __uint_as_float(__byte_perm(wb, 0x4B000000u, sel)) - 8388736.f;
 }
+// The same before the subtraction (2^23 + q + 128), for packed subtraction of the bias.
+__device__ __forceinline__ float i8raw(uint32_t wb, uint32_t sel) { return __uint_as_float(__byte_perm(wb, 0x4B000000u, sel)); }
 // int4: nibble n (already isolated in byte b) -> 0.5 + n/256.
 __device__ __forceinline__ float i4half(uint32_t v, uint32_t sel) { return __uint_as_float(__byte_perm(v, 0x3F000000u, sel)); }
 
@@ -197,6 +185,11 @@ struct TileRows {
 // Accumulates one tile (N stage rows x one row segment) into acc[0..N). Two independent FMA chains
 // per row keep the dependency latency hidden. CPL > 0 fixes the chunks per lane (segment bytes / 512)
 // at compile time so the chunk loop unrolls completely; CPL == 0 reads it from seg_bytes.
+// Packed fp32 pair arithmetic (sm_100 FFMA2 / FADD2): each half is an ordinary round-to-nearest fp32
+// operation, so pairing two independent accumulation chains changes no result bit.
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
+__device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
+
 template <WeightType WT, int N, int CPL = 0>
 __device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& tr, int seg_bytes, int seg_chunk0,
                                          const float* xp, int nc, const float* xc, const void* scales, int K,
@@ -204,87 +197,114 @@ __device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& t
     const float4* p4 = reinterpret_cast<const float4*>(xp);
     const int cpl = CPL > 0 ? CPL : (seg_bytes >> 9);  // chunks per lane per row
     if constexpr (CPL > 0) seg_bytes = CPL * 512;
-    float a0[N], a1[N];
-#pragma unroll
-    for (int i = 0; i < N; ++i) a0[i] = a1[i] = 0.f;
     [[maybe_unused]] const int groups = K >> 7;
-#pragma unroll(CPL > 0 ? CPL : 2)
-    for (int j = 0; j < cpl; ++j) {
-        const int c = lane + 32 * j;
-        const int gc = seg_chunk0 + c;
-        if constexpr (WT == WeightType::BF16) {
-            const float4 x0 = p4[gc], x1 = p4[nc + gc];
+    if constexpr (WT == WeightType::INT4 && CPL > 0) {
+        // Compile-time tile shape: one scalar chain per row (the group scale is applied per chunk).
+        float r[N];
 #pragma unroll
-            for (int i = 0; i < N; ++i) {
-                const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
-                a0[i] = fmaf(bf16lo(w.x), x0.x, a0[i]);
-                a1[i] = fmaf(bf16lo(w.z), x1.x, a1[i]);
-                a0[i] = fmaf(bf16hi(w.x), x0.y, a0[i]);
-                a1[i] = fmaf(bf16hi(w.z), x1.y, a1[i]);
-                a0[i] = fmaf(bf16lo(w.y), x0.z, a0[i]);
-                a1[i] = fmaf(bf16lo(w.w), x1.z, a1[i]);
-                a0[i] = fmaf(bf16hi(w.y), x0.w, a0[i]);
-                a1[i] = fmaf(bf16hi(w.w), x1.w, a1[i]);
-            }
-        } else if constexpr (WT == WeightType::INT8) {
-            const float4 x0 = p4[gc], x1 = p4[nc + gc], x2 = p4[2 * nc + gc], x3 = p4[3 * nc + gc];
+        for (int i = 0; i < N; ++i) r[i] = 0.f;
+        const __half* sc = static_cast<const __half*>(scales);
 #pragma unroll
-            for (int i = 0; i < N; ++i) {
-                const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
-                const uint32_t b0 = w.x ^ 0x80808080u, b1 = w.y ^ 0x80808080u, b2 = w.z ^ 0x80808080u,
-                               b3 = w.w ^ 0x80808080u;
-                a0[i] = fmaf(i8val(b0, 0x7540), x0.x, a0[i]);
-                a1[i] = fmaf(i8val(b2, 0x7540), x2.x, a1[i]);
-                a0[i] = fmaf(i8val(b0, 0x7541), x0.y, a0[i]);
-                a1[i] = fmaf(i8val(b2, 0x7541), x2.y, a1[i]);
-                a0[i] = fmaf(i8val(b0, 0x7542), x0.z, a0[i]);
-                a1[i] = fmaf(i8val(b2, 0x7542), x2.z, a1[i]);
-                a0[i] = fmaf(i8val(b0, 0x7543), x0.w, a0[i]);
-                a1[i] = fmaf(i8val(b2, 0x7543), x2.w, a1[i]);
-                a0[i] = fmaf(i8val(b1, 0x7540), x1.x, a0[i]);
-                a1[i] = fmaf(i8val(b3, 0x7540), x3.x, a1[i]);
-                a0[i] = fmaf(i8val(b1, 0x7541), x1.y, a0[i]);
-                a1[i] = fmaf(i8val(b3, 0x7541), x3.y, a1[i]);
-                a0[i] = fmaf(i8val(b1, 0x7542), x1.z, a0[i]);
-                a1[i] = fmaf(i8val(b3, 0x7542), x3.z, a1[i]);
-                a0[i] = fmaf(i8val(b1, 0x7543), x1.w, a0[i]);
-                a1[i] = fmaf(i8val(b3, 0x7543), x3.w, a1[i]);
-            }
-        } else {
+        for (int j = 0; j < CPL; ++j) {
+            const int c = lane + 32 * j;
+            const int gc = seg_chunk0 + c;
+
             const float xsum = xc[gc];
-            const int g = gc >> 2;  // 128-column group of this chunk
-            const __half* sc = static_cast<const __half*>(scales);
-            float4 xe[4], xo[4];
+            float4 xa[4], xb[4];  // word k: columns 8k..8k+3 and 8k+4..8k+7
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                xe[k] = p4[(2 * k) * nc + gc];
-                xo[k] = p4[(2 * k + 1) * nc + gc];
+                xa[k] = p4[(2 * k) * nc + gc];
+                xb[k] = p4[(2 * k + 1) * nc + gc];
             }
 #pragma unroll
             for (int i = 0; i < N; ++i) {
                 const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
-                const float s = __half2float(__ldg(sc + static_cast<size_t>(tr.global_row(i)) * groups + g));
                 const uint32_t words[4] = {w.x, w.y, w.z, w.w};
-                float p0 = 0.f, p1 = 0.f;
+                float2 pp = make_float2(0.f, 0.f);
 #pragma unroll
                 for (int k = 0; k < 4; ++k) {
                     const uint32_t lo = words[k] & 0x0F0F0F0Fu;
                     const uint32_t hi = (words[k] >> 4) & 0x0F0F0F0Fu;
-                    p0 = fmaf(i4half(lo, 0x7044), xe[k].x, p0);
-                    p1 = fmaf(i4half(hi, 0x7044), xo[k].x, p1);
-                    p0 = fmaf(i4half(lo, 0x7144), xe[k].y, p0);
-                    p1 = fmaf(i4half(hi, 0x7144), xo[k].y, p1);
-                    p0 = fmaf(i4half(lo, 0x7244), xe[k].z, p0);
-                    p1 = fmaf(i4half(hi, 0x7244), xo[k].z, p1);
-                    p0 = fmaf(i4half(lo, 0x7344), xe[k].w, p0);
-                    p1 = fmaf(i4half(hi, 0x7344), xo[k].w, p1);
+                    pp = fma2(make_float2(i4half(lo, 0x7044), i4half(hi, 0x7044)), make_float2(xa[k].x, xa[k].y), pp);
+                    pp = fma2(make_float2(i4half(lo, 0x7144), i4half(hi, 0x7144)), make_float2(xa[k].z, xa[k].w), pp);
+                    pp = fma2(make_float2(i4half(lo, 0x7244), i4half(hi, 0x7244)), make_float2(xb[k].x, xb[k].y), pp);
+                    pp = fma2(make_float2(i4half(lo, 0x7344), i4half(hi, 0x7344)), make_float2(xb[k].z, xb[k].w), pp);
                 }
-                a0[i] = fmaf(s, fmaf(256.f, p0 + p1, -136.f * xsum), a0[i]);
+                const float si = __half2float(__ldg(sc + static_cast<size_t>(tr.global_row(i)) * groups + (gc >> 2)));
+                r[i] = fmaf(si, fmaf(256.f, pp.x + pp.y, -136.f * xsum), r[i]);
             }
         }
-    }
 #pragma unroll
-    for (int i = 0; i < N; ++i) acc[i] += a0[i] + a1[i];
+        for (int i = 0; i < N; ++i) acc[i] += r[i] + 0.f;  // + the (zero) second chain, as below
+        return;
+    } else {
+        // Two accumulation chains per row (.x and .y), advanced together by one packed instruction.
+        float2 a[N];
+#pragma unroll
+        for (int i = 0; i < N; ++i) a[i] = make_float2(0.f, 0.f);
+#pragma unroll(CPL > 0 ? CPL : 2)
+        for (int j = 0; j < cpl; ++j) {
+            const int c = lane + 32 * j;
+            const int gc = seg_chunk0 + c;
+            if constexpr (WT == WeightType::BF16) {
+                const float4 x0 = p4[gc], x1 = p4[nc + gc];
+#pragma unroll
+                for (int i = 0; i < N; ++i) {
+                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                    a[i] = fma2(make_float2(bf16lo(w.x), bf16hi(w.x)), make_float2(x0.x, x0.y), a[i]);
+                    a[i] = fma2(make_float2(bf16lo(w.y), bf16hi(w.y)), make_float2(x0.z, x0.w), a[i]);
+                    a[i] = fma2(make_float2(bf16lo(w.z), bf16hi(w.z)), make_float2(x1.x, x1.y), a[i]);
+                    a[i] = fma2(make_float2(bf16lo(w.w), bf16hi(w.w)), make_float2(x1.z, x1.w), a[i]);
+                }
+            } else if constexpr (WT == WeightType::INT8) {
+                const float4 x0 = p4[gc], x1 = p4[nc + gc], x2 = p4[2 * nc + gc], x3 = p4[3 * nc + gc];
+                const float2 bias = make_float2(-8388736.f, -8388736.f);
+#pragma unroll
+                for (int i = 0; i < N; ++i) {
+                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                    const uint32_t b0 = w.x ^ 0x80808080u, b1 = w.y ^ 0x80808080u, b2 = w.z ^ 0x80808080u,
+                                   b3 = w.w ^ 0x80808080u;
+                    a[i] = fma2(add2(make_float2(i8raw(b0, 0x7540), i8raw(b0, 0x7541)), bias), make_float2(x0.x, x0.y), a[i]);
+                    a[i] = fma2(add2(make_float2(i8raw(b0, 0x7542), i8raw(b0, 0x7543)), bias), make_float2(x0.z, x0.w), a[i]);
+                    a[i] = fma2(add2(make_float2(i8raw(b1, 0x7540), i8raw(b1, 0x7541)), bias), make_float2(x1.x, x1.y), a[i]);
+                    a[i] = fma2(add2(make_float2(i8raw(b1, 0x7542), i8raw(b1, 0x7543)), bias), make_float2(x1.z, x1.w), a[i]);
+                    a[i] = fma2(add2(make_float2(i8raw(b2, 0x7540), i8raw(b2, 0x7541)), bias), make_float2(x2.x, x2.y), a[i]);
+                    a[i] = fma2(add2(make_float2(i8raw(b2, 0x7542), i8raw(b2, 0x7543)), bias), make_float2(x2.z, x2.w), a[i]);
+                    a[i] = fma2(add2(make_float2(i8raw(b3, 0x7540), i8raw(b3, 0x7541)), bias), make_float2(x3.x, x3.y), a[i]);
+                    a[i] = fma2(add2(make_float2(i8raw(b3, 0x7542), i8raw(b3, 0x7543)), bias), make_float2(x3.z, x3.w), a[i]);
+                }
+            } else {
+                const float xsum = xc[gc];
+                const int g = gc >> 2;  // 128-column group of this chunk
+                const __half* sc = static_cast<const __half*>(scales);
+                float4 xa[4], xb[4];  // word k: columns 8k..8k+3 and 8k+4..8k+7
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    xa[k] = p4[(2 * k) * nc + gc];
+                    xb[k] = p4[(2 * k + 1) * nc + gc];
+                }
+#pragma unroll
+                for (int i = 0; i < N; ++i) {
+                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                    const float s = __half2float(__ldg(sc + static_cast<size_t>(tr.global_row(i)) * groups + g));
+                    const uint32_t words[4] = {w.x, w.y, w.z, w.w};
+                    float2 pp = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) {
+                        const uint32_t lo = words[k] & 0x0F0F0F0Fu;
+                        const uint32_t hi = (words[k] >> 4) & 0x0F0F0F0Fu;
+                        pp = fma2(make_float2(i4half(lo, 0x7044), i4half(hi, 0x7044)), make_float2(xa[k].x, xa[k].y), pp);
+                        pp = fma2(make_float2(i4half(lo, 0x7144), i4half(hi, 0x7144)), make_float2(xa[k].z, xa[k].w), pp);
+                        pp = fma2(make_float2(i4half(lo, 0x7244), i4half(hi, 0x7244)), make_float2(xb[k].x, xb[k].y), pp);
+                        pp = fma2(make_float2(i4half(lo, 0x7344), i4half(hi, 0x7344)), make_float2(xb[k].z, xb[k].w), pp);
+                    }
+                    a[i].x = fmaf(s, fmaf(256.f, pp.x + pp.y, -136.f * xsum), a[i].x);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < N; ++i) acc[i] += a[i].x + a[i].y;
+    }
 }
 
 // Row result after the warp reduction (all lanes hold it); int8 applies its per-row scale here.
