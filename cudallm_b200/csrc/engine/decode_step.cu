@@ -26,14 +26,11 @@ constexpr int kCt = 32 * kCw;      // consumer threads
 // never waits for registers that are not there.
 constexpr int kThreads = 128 + kCt;
 constexpr int kLaunchRegs = 168;  // 65536 / 384 rounded down to a multiple of 8
-constexpr int kProducerRegs = 72;
-constexpr int kConsumerRegs = 216;
+constexpr int kProducerRegs = 88;
+constexpr int kConsumerRegs = 208;
 static_assert(kProducerRegs * 128 + kConsumerRegs * kCt == kLaunchRegs * kThreads, "register split must use the launch pool");
 constexpr int kStages = 12;
-// Producer lanes: lane j of warp 0 issues the tiles t with t % kProducers == j, i.e. it owns the stages
-// s with s % kProducers == j, so four issue loops (each ~0.2-0.5 us per copy) run concurrently.
-constexpr int kProducers = 4;
-static_assert(kStages % kProducers == 0, "each stage must belong to one producer lane");
+static_assert(kStages <= 32, "one producer lane per stage");
 constexpr int kMaxK = 8192;
 constexpr int kOpsPerLayer = 4;
 constexpr int kWeightOps = kStepLayers * kOpsPerLayer + 1;  // + tied lm_head
@@ -52,16 +49,21 @@ struct Flags {
 constexpr int kOffBars = 0;
 constexpr int kOffTiles = 2 * kStages * 8;  // int per stage: tile the producer last issued into it
 constexpr int kOffFlags = 256;
+constexpr int kOffKinds = 288;  // KindRows[5]: this CTA's rows of each operation kind
 constexpr int kOffRed = 384;
 constexpr int kOffCs = 512;
 constexpr int kOffScratch = 768;
 constexpr int kOffAm = kOffScratch + kCw * 32 * 4;  // 1792
+// The residual rows this CTA owns (the same row range in the O and down projections), kept on chip for
+// the whole step so their epilogues add without reading x back.
+constexpr int kOffRes = kOffAm + kCw * 8;  // 1856
+constexpr int kMaxResRows = 48;
 constexpr int kOffXc = 2048;
 constexpr int kOffXp = 3072;
 constexpr int kOffRing = kOffXp + kMaxK * 4;  // 35840
 constexpr int kSmemBytes = kOffRing + kStages * kStageBytes;
 static_assert(kOffTiles + kStages * 4 <= kOffFlags, "barriers overflow");
-static_assert(kOffAm + kCw * 8 <= kOffXc, "argmax scratch overflow");
+static_assert(kOffAm + kCw * 8 <= kOffRes && kOffRes + kMaxResRows * 4 <= kOffXc, "argmax / residual scratch overflow");
 static_assert(kOffXc + (kMaxK / 32) * 4 <= kOffXp, "chunk sums overflow");
 static_assert(sizeof(AttSmem<__half>) <= kMaxK * 4, "attention scratch must fit in the vector area");
 static_assert(sizeof(HeadPassSmem<__half>) <= kMaxK * 4, "attention scratch must fit in the vector area");
@@ -104,9 +106,12 @@ __device__ __forceinline__ WOp weight_op(const StepParams& p, int o) {
     }
 }
 
+// Rows [lo, hi) of an n-row operation owned by this CTA. 32-bit arithmetic: n * grid stays far below 2^32
+// (vocab 128256 x 148 SMs).
 __device__ __forceinline__ void split_rows(int n, int& lo, int& hi) {
-    lo = static_cast<int>(static_cast<long long>(blockIdx.x) * n / gridDim.x);
-    hi = static_cast<int>(static_cast<long long>(blockIdx.x + 1) * n / gridDim.x);
+    const unsigned un = static_cast<unsigned>(n), g = gridDim.x;
+    lo = static_cast<int>(blockIdx.x * un / g);
+    hi = static_cast<int>((blockIdx.x + 1) * un / g);
 }
 
 __device__ __forceinline__ int op_tiles(const TileGeom& g, int lo, int hi) {
@@ -115,11 +120,13 @@ __device__ __forceinline__ int op_tiles(const TileGeom& g, int lo, int hi) {
 }
 
 __device__ __forceinline__ void trace_mark(const StepParams& p, int op, int slot) {
-    if (p.trace) p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + op * 4 + slot] = global_ns();
+    if (p.trace) p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + op * kTraceStamps + slot] = global_ns();
 }
 
-__device__ __forceinline__ void trace_tile(const StepParams& p, int o, int i, int slot) {
-    if (p.trace && blockIdx.x == 0 && o == p.trace_tile_op && i < kTraceTiles) {
+// Stamps slot `slot` of global tile t of CTA 0 when it lies in the traced window.
+__device__ __forceinline__ void trace_tile(const StepParams& p, int t, int slot) {
+    const int i = t - p.trace_t0;
+    if (p.trace && blockIdx.x == 0 && i >= 0 && i < kTraceTiles) {
         p.trace[static_cast<size_t>(gridDim.x) * kTraceSlots + i * kTraceTileStamps + slot] = global_ns();
     }
 }
@@ -181,26 +188,64 @@ __device__ bool wait_bar(const StepParams& p, uint64_t* bar, uint32_t parity, vo
 }
 
 // Cursor over this CTA's tiles of the whole step (operation by operation).
+__device__ __forceinline__ uint8_t* smem_base() {
+    extern __shared__ __align__(1024) uint8_t smem_dyn[];
+    return smem_dyn;
+}
+
+// This CTA's rows and tile count of one operation kind (the same in every layer).
+struct KindRows {
+    int lo, hi, nt;
+};
+static_assert(kOffKinds + 5 * sizeof(KindRows) <= kOffRed, "kind table overflow");
+__device__ __forceinline__ KindRows kind_rows(const TileGeom& g) {
+    KindRows r;
+    split_rows(g.out_rows, r.lo, r.hi);
+    r.nt = op_tiles(g, r.lo, r.hi);
+    return r;
+}
+
+// Fills the shared table of this CTA's rows per operation kind (qkv, o-proj, gate/up, down, lm_head);
+// one thread, before the block's first barrier.
+__device__ __forceinline__ void init_kind_rows(const StepParams& p, KindRows* kinds) {
+    kinds[kQkv] = kind_rows(p.g_qkv);
+    kinds[kWo] = kind_rows(p.g_wo);
+    kinds[kGu] = kind_rows(p.g_gu);
+    kinds[kDown] = kind_rows(p.g_down);
+    kinds[kLm] = kind_rows(p.g_lm);
+}
+
+// Cursor over this CTA's tiles of the whole step (operation by operation). Row ranges come from the
+// shared per-kind table, so crossing an operation costs no division.
+__device__ __forceinline__ const KindRows* kind_table() { return reinterpret_cast<const KindRows*>(smem_base() + kOffKinds); }
+
 struct TileCursor {
     int o = 0, i = 0, nt = 0, lo = 0, hi = 0;
-    WOp op;
-    __device__ void load(const StepParams& p) {
-        op = weight_op(p, o);
-        split_rows(op.g.out_rows, lo, hi);
-        nt = op_tiles(op.g, lo, hi);
+    __device__ void init() {
+        o = 0;
         i = 0;
+        load();
+    }
+    __device__ void load() {
+        const KindRows r = kind_table()[o == kWeightOps - 1 ? kLm : o % kOpsPerLayer];
+        lo = r.lo;
+        hi = r.hi;
+        nt = r.nt;
     }
     __device__ bool valid() const { return o < kWeightOps; }
-    __device__ void next(const StepParams& p) {
-        if (++i >= nt) {
-            if (++o < kWeightOps) load(p);
+    // Moves n tiles forward.
+    __device__ void advance(int n) {
+        i += n;
+        while (o < kWeightOps && i >= nt) {
+            i -= nt;
+            if (++o < kWeightOps) load();
         }
     }
 };
 
 __device__ __forceinline__ void issue_tile(const WOp& op, int lo, int hi, int i, uint8_t* dst, uint64_t* bar, uint64_t pol) {
     const TileGeom& g = op.g;
-    const int grp = i / g.n_seg, sg = i % g.n_seg;
+    const int grp = g.n_seg == 1 ? i : i / g.n_seg, sg = g.n_seg == 1 ? 0 : i % g.n_seg;
     const int r0 = lo + grp * g.rows_per_tile;
     const int nr = min(g.rows_per_tile, hi - r0);
     mbar_arrive_expect_tx(bar, static_cast<uint32_t>(nr * g.seg_bytes * g.halves));
@@ -219,32 +264,51 @@ __device__ __forceinline__ void issue_tile(const WOp& op, int lo, int hi, int i,
     }
 }
 
-// Warp 0, lanes 0..kProducers-1: lane j streams tiles j, j+kProducers, ... of the step (in use
-// order) into the stages it owns. A copy is issued as soon as its stage is released.
+// Warp 0: lane s < kStages owns stage s and streams the tiles t = s, s + kStages, ... of the step (in use
+// order) into it, issuing each copy as soon as the stage is released. The lanes poll their stages with
+// non-blocking tests in one converged loop, so a stage that is still in use never holds back another
+// lane's copy. Lane 0 publishes the lowest tile index not yet issued for the prefetch warp.
 __device__ void run_producer(const StepParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty, volatile int* stage_tile,
-                             volatile Flags* fl, int lane) {
+                             volatile Flags* fl) {
+    const int lane = threadIdx.x & 31;
     const uint64_t pol = l2_policy_evict_first();
     TileCursor cur;
-    cur.load(p);
-    for (int q = 0; q < lane && cur.valid(); ++q) cur.next(p);
-    int t = lane, last = -1;
-    while (cur.valid()) {
-        if (cur.i == 0) trace_mark(p, trace_op_of_weight_op(cur.o), 3);
-        const int s = t % kStages, k = t / kStages;
-        if (k > 0 && !wait_bar(p, &empty[s], (k - 1) & 1, fl, true, 1000u + cur.o)) break;
-        stage_tile[s] = t;
-        trace_tile(p, cur.o, cur.i, 0);
-        issue_tile(cur.op, cur.lo, cur.hi, cur.i, ring + s * kStageBytes, &full[s], pol);
-        last = t;
-        if (lane == 0) fl->issued = t + 1;
-        t += kProducers;
-        for (int q = 0; q < kProducers && cur.valid(); ++q) cur.next(p);
+    cur.init();
+    cur.advance(lane);
+    int t = lane, k = 0;  // next tile of this lane; copies issued into its stage so far
+    bool more = lane < kStages && cur.valid();
+    uint64_t t_idle = 0;
+    for (uint32_t it = 1;; ++it) {
+        bool progressed = false;
+        if (more && (k == 0 || mbar_test_wait(&empty[lane], (k - 1) & 1))) {
+            if (cur.i == 0) trace_mark(p, trace_op_of_weight_op(cur.o), 3);
+            stage_tile[lane] = t;
+            trace_tile(p, t, 0);
+            issue_tile(weight_op(p, cur.o), cur.lo, cur.hi, cur.i, ring + lane * kStageBytes, &full[lane], pol);
+            ++k;
+            t += kStages;
+            cur.advance(kStages);
+            more = cur.valid();
+            progressed = true;
+        }
+        const int front = __reduce_min_sync(0xffffffffu, more ? t : (1 << 30));
+        if (lane == 0) fl->issued = front;  // 1 << 30 once every tile is issued: releases the prefetch warp
+        if (!__any_sync(0xffffffffu, more)) break;
+        if (__any_sync(0xffffffffu, progressed)) {
+            t_idle = 0;
+        } else if ((it & 63) == 0) {
+            if (fl->abort) break;
+            const uint64_t now = global_ns();
+            if (t_idle == 0) {
+                t_idle = now;
+            } else if (now - t_idle > p.wait_limit_ns) {
+                if (lane == 0) fail(p, fl, kErrWaitTimeout, 1000u);
+                break;
+            }
+        }
     }
-    if (lane == 0) fl->issued = 1 << 30;  // releases the prefetch warp
-    // Every copy this lane issued lands before the CTA may exit.
-    for (int u = last; u >= 0 && u > last - kStages; u -= kProducers) {
-        wait_bar(p, &full[u % kStages], (u / kStages) & 1, fl, false, 2000u);
-    }
+    // Every copy issued lands before the CTA may exit.
+    if (lane < kStages && k > 0) wait_bar(p, &full[lane], (k - 1) & 1, fl, false, 2000u);
 }
 
 // Warp 1: L2 prefetch of the weight stream with ordinary prefetch instructions (load/store units,
@@ -252,7 +316,7 @@ __device__ void run_producer(const StepParams& p, uint8_t* ring, uint64_t* full,
 __device__ void run_prefetcher(const StepParams& p, volatile Flags* fl) {
     const int lane = threadIdx.x & 31;
     TileCursor pf;
-    pf.load(p);
+    pf.init();
     int pt = 0;
     uint64_t t0 = 0;
     while (pf.valid()) {
@@ -266,27 +330,18 @@ __device__ void run_prefetcher(const StepParams& p, volatile Flags* fl) {
             __nanosleep(128);
         }
         t0 = 0;
-        const TileGeom& g = pf.op.g;
-        const int grp = pf.i / g.n_seg, sg = pf.i % g.n_seg;
-        const int r0 = pf.lo + grp * g.rows_per_tile;
-        const int nr = min(g.rows_per_tile, pf.hi - r0);
-        for (int h = 0; h < g.halves; ++h) {
-            const size_t row = static_cast<size_t>(r0) + static_cast<size_t>(h) * g.out_rows;
-            for (int r = 0; r < (g.n_seg == 1 ? 1 : nr); ++r) {
-                const uint8_t* a = pf.op.w + (row + r) * g.row_bytes + static_cast<size_t>(sg) * g.seg_bytes;
-                const int bytes = g.n_seg == 1 ? nr * g.row_bytes : g.seg_bytes;
-                if (p.prefetch_mode == 3) {
-                    for (int off = lane * 128; off < bytes; off += 32 * 128) {
-                        asm volatile("prefetch.global.L2::evict_last [%0];" ::"l"(a + off) : "memory");
-                    }
-                } else {
-                    for (int off = lane * 128; off < bytes; off += 32 * 128) {
-                        asm volatile("prefetch.global.L2 [%0];" ::"l"(a + off) : "memory");
-                    }
-                }
+        // Whole-row tiles (every operation of the step): rows r0 .. r0+nr-1 of each half are contiguous.
+        const WOp op = weight_op(p, pf.o);
+        const int r0 = pf.lo + pf.i * op.g.rows_per_tile;
+        const int bytes = min(op.g.rows_per_tile, pf.hi - r0) * op.g.row_bytes;
+        for (int h = 0; h < op.g.halves; ++h) {
+            const uint8_t* a = op.w + (static_cast<size_t>(r0) + static_cast<size_t>(h) * op.g.out_rows) * op.g.row_bytes;
+            for (int off = lane * 128; off < bytes; off += 32 * 128) {
+                asm volatile("prefetch.global.L2 [%0];" ::"l"(a + off) : "memory");
             }
         }
-        pf.next(p);
+        if (lane == 0) trace_tile(p, pt, 4);
+        pf.advance(1);
         ++pt;
     }
 }
@@ -365,6 +420,7 @@ struct ConsumerCtx {
     float* xc;
     float* red;
     float* scratch;
+    float* res;  // [kMaxResRows] this CTA's residual rows
     int tid, cw, lane;
     int t_base;  // global tile index of the current operation's first tile
 };
@@ -397,8 +453,7 @@ __device__ __forceinline__ void signal(ConsumerCtx& c, unsigned* ctr, int top = 
 // reduces the N stage rows across the warp and leaves row i's value in my[i]. Not inlined: one copy
 // per (type, N) serves every operation with that tile shape.
 template <WeightType WT, int N, int CPL>
-__device__ __forceinline__ bool group_dot(const ConsumerCtx& c, int t0, int r0, const WOp& op, float* my, int trace_o,
-                                          int trace_t0) {
+__device__ __forceinline__ bool group_dot(const ConsumerCtx& c, int t0, int r0, const WOp& op, float* my) {
     const StepParams& p = *c.p;
     const TileGeom& g = op.g;
     const TileRows tr{r0, g.rows_per_tile, g.halves == 2 ? g.out_rows : 0, g.out_rows * g.halves - 1};
@@ -410,7 +465,7 @@ __device__ __forceinline__ bool group_dot(const ConsumerCtx& c, int t0, int r0, 
         const int t = t0 + sg;
         const int s = t % kStages;
         if (!wait_bar(p, &c.full[s], (t / kStages) & 1, c.fl, true, 3000u, &c.stage_tile[s], t)) return false;
-        if (c.lane == 0 && sg == 0) trace_tile(p, trace_o, t0 - trace_t0, 2);
+        if (c.lane == 0 && sg == 0) trace_tile(p, t0, 2);
         tile_dot<WT, N, CPL>(c.ring + s * kStageBytes, tr, g.seg_bytes, sg * (g.seg_bytes / 16), c.xp, nc, c.xc, op.s, g.cols,
                              acc, c.lane);
         __syncwarp();
@@ -435,8 +490,8 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
     const StepParams& p = *c.p;
     const WOp op = weight_op(p, o);
     const TileGeom& g = op.g;
-    int lo, hi;
-    split_rows(g.out_rows, lo, hi);
+    const KindRows kr = reinterpret_cast<const KindRows*>(smem_base() + kOffKinds)[kind];
+    const int lo = kr.lo, hi = kr.hi;
     const int R = g.rows_per_tile;
     const int ng = (hi - lo + R - 1) / R;
     float* my = c.scratch + c.cw * 32;
@@ -449,17 +504,19 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
     for (int grp = c.cw; grp < ng && ok; grp += kCw) {
         const int r0 = lo + grp * R;
         const int nr = min(R, hi - r0);
-        if (c.lane == 0) trace_tile(p, o, grp, 1);
-        ok = group_dot<WT, N, CPL>(c, c.t_base + grp * g.n_seg, r0, op, my, o, c.t_base);
+        if (c.lane == 0) trace_tile(p, c.t_base + grp * g.n_seg, 1);
+        ok = group_dot<WT, N, CPL>(c, c.t_base + grp * g.n_seg, r0, op, my);
         if (!ok) break;
-        if (c.lane == 0) trace_tile(p, o, grp, 3);
+        if (grp == 0 && c.lane == 0) trace_mark(p, trace_op_of_weight_op(o), 5);
+        if (c.lane == 0) trace_tile(p, c.t_base + grp * g.n_seg, 3);
         if (c.lane < nr) {
             const int r = r0 + c.lane;
             const float d = my[c.lane];
             if (kind == kQkv) {
                 __stcg(p.qkv + r, d);
             } else if (kind == kWo || kind == kDown) {
-                const float v = __ldcg(p.x + r) + d;
+                const float v = c.res[r - lo] + d;
+                c.res[r - lo] = v;
                 __stcg(p.x + r, v);
                 if (kind == kDown && p.debug_res) p.debug_res[static_cast<size_t>(layer + 1) * kH + r] = v;
             } else if (kind == kGu) {
@@ -475,7 +532,7 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
         __syncwarp();
     }
     if (!ok) c.fl->abort = 1;
-    c.t_base += op_tiles(g, lo, hi);
+    c.t_base += kr.nt;
     csync();
     return c.fl->abort == 0;
 }
@@ -509,7 +566,7 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
         if (p.trace) {  // the SM this CTA runs on (slot 3 of the step-end entry is otherwise unused)
             unsigned smid;
             asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
-            p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + 81 * 4 + 3] = smid;
+            p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + 81 * kTraceStamps + 3] = smid;
         }
     }
     {
@@ -518,9 +575,11 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
         split_rows(p.g_wo.out_rows, lo, hi);
         for (int r = lo + c.tid; r < hi; r += kCt) {
             const float v = emb_value<WT>(p, tok, r);
+            c.res[r - lo] = v;
             __stcg(p.x + r, v);
             if (p.debug_res) p.debug_res[r] = v;
         }
+        csync();
     }
     constexpr int kN = stage_rows<WT, kQkv>(), kCpl = seg_chunks_per_lane<WT, kQkv>();
     constexpr int kNd = stage_rows<WT, kDown>(), kCpld = seg_chunks_per_lane<WT, kDown>();
@@ -600,12 +659,14 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
             snorm = p.final_norm;
         }
         stage_vector<WT>(StageSrc<WT>{&p, svec, tok}, sK, snorm, p.eps, c.xp, c.xc, c.red, c.tid, kCt, [] { csync(); });
+        const int top = lm ? 80 : l * 5 + (kind == kQkv ? 0 : kind + 1);  // trace entry of this operation
+        if (c.tid == 0) trace_mark(p, top, 4);
         const bool ok = kind == kDown ? run_tiles<WT, kNd, kCpld>(c, o, kind, bv, bi, l)
                                       : run_tiles<WT, kN, kCpl>(c, o, kind, bv, bi, l);
         if (!ok) return;
         if (kind != kLm) {
             const int counter = kind == kQkv ? kSyncQkv : (kind == kWo ? kSyncWo : (kind == kGu ? kSyncGu : kSyncDown));
-            signal(c, p.sync + counter + l, l * 5 + (kind == kQkv ? 0 : kind + 1));
+            signal(c, p.sync + counter + l, top);
         }
     }
     // ---- lm_head done: CTA argmax, then the last CTA commits the token ----------------------
@@ -689,14 +750,15 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         fl->ok = 0;
         fl->role = 0;
         fl->issued = 0;
+        init_kind_rows(p, reinterpret_cast<KindRows*>(smem + kOffKinds));
         fence_barrier_init();
     }
     __syncthreads();
     if (threadIdx.x < 128) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
-        if (threadIdx.x < kProducers) {
-            run_producer(p, ring, full, empty, stage_tile, fl, threadIdx.x);
-        } else if (threadIdx.x >= 32 && threadIdx.x < 64 && p.prefetch_mode >= 2) {
+        if (threadIdx.x < 32) {
+            run_producer(p, ring, full, empty, stage_tile, fl);
+        } else if (threadIdx.x >= 32 && threadIdx.x < 64 && p.prefetch_mode == 2) {
             run_prefetcher(p, fl);
         }
         return;
@@ -713,6 +775,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     c.xc = reinterpret_cast<float*>(smem + kOffXc);
     c.red = reinterpret_cast<float*>(smem + kOffRed);
     c.scratch = reinterpret_cast<float*>(smem + kOffScratch);
+    c.res = reinterpret_cast<float*>(smem + kOffRes);
     c.tid = threadIdx.x - 128;
     c.cw = c.tid >> 5;
     c.lane = c.tid & 31;
@@ -750,6 +813,8 @@ int decode_step_grid() { return num_sms(); }
 
 void launch_decode_step(const StepParams& p, WeightType wt, KvType kv, cudaStream_t stream) {
     CLLM_CHECK(p.max_seq % kAttnTile == 0, "decode step: max_seq must be a multiple of 64");
+    CLLM_CHECK((kH + decode_step_grid() - 1) / decode_step_grid() <= kMaxResRows,
+               "decode step: too few SMs for the on-chip residual rows");
     const bool f16 = kv == KvType::F16;
     switch (wt) {
         case WeightType::BF16:

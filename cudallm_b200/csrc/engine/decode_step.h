@@ -38,15 +38,17 @@ struct StepLayer {
 constexpr int kStepLayers = 16;
 
 // Trace layout per CTA: operation k (layer l: 5l + {0 qkv, 1 attention, 2 o-proj, 3 gate/up, 4 down};
-// 80 lm_head; 81 step end) has 4 slots: dependency wait begins, wait ends, operation ends, producer
-// starts issuing its tiles (weight operations only); slot 3 of entry 81 holds the CTA's SM id.
+// 80 lm_head; 81 step end) has kTraceStamps slots: 0 dependency wait begins, 1 wait ends, 2 operation
+// ends, 3 producer starts issuing its tiles, 4 input vector staged, 5 consumer warp 0 done with its
+// first tile (3-5: weight operations only); slot 3 of entry 81 holds the CTA's SM id.
 constexpr int kTraceOps = 82;
-constexpr int kTraceSlots = kTraceOps * 4;
-// After the per-CTA slots: CTA 0's first kTraceTiles tiles of one weight operation (StepParams::trace_tile_op,
-// lm_head by default), 4 stamps each (producer issues the
-// copy, consumer starts waiting for it, the data is there, consumer is done with the tile).
+constexpr int kTraceStamps = 6;
+constexpr int kTraceSlots = kTraceOps * kTraceStamps;
+// After the per-CTA slots: kTraceTiles tiles of CTA 0's tile stream starting at global tile index
+// StepParams::trace_t0, 5 stamps each: producer issues the copy, consumer starts waiting for it, the data
+// is there, consumer is done with the tile, the prefetch warp has issued its L2 prefetch.
 constexpr int kTraceTiles = 256;
-constexpr int kTraceTileStamps = 4;
+constexpr int kTraceTileStamps = 5;
 inline constexpr size_t trace_words(int grid) {
     return static_cast<size_t>(grid) * kTraceSlots + kTraceTiles * kTraceTileStamps;
 }
@@ -88,9 +90,9 @@ struct StepParams {
     int group_size;
     unsigned long long wait_limit_ns;
     int prefetch_tiles;  // L2 prefetch distance of the weight stream, in tiles beyond the copies
-    int prefetch_mode;   // 0 none, 2 prefetch warp (load/store-unit prefetch instructions), 3 same with evict_last
+    int prefetch_mode;   // 0 none, 2 prefetch warp (load/store-unit prefetch instructions)
     int whole_head_max_tiles;  // contexts up to this many 64-token tiles use one CTA per KV head for attention
-    int trace_tile_op;   // weight operation (layer*4 + qkv/wo/gu/down, 64 = lm_head) whose tiles CTA 0 stamps
+    int trace_t0;        // first stamped tile (global index in CTA 0's tile stream)
     TileGeom g_qkv, g_wo, g_gu, g_down, g_lm;
 };
 

@@ -151,8 +151,8 @@ Engine::Engine(const std::string& path, const EngineOptions& opts) : opts_(opts)
             if (const char* env = std::getenv("CUDALLM_PREFETCH_MODE")) p.prefetch_mode = std::atoi(env);
             p.whole_head_max_tiles = kDefaultWholeHeadMaxTiles;
             if (const char* env = std::getenv("CUDALLM_WHOLE_HEAD_MAX_TILES")) p.whole_head_max_tiles = std::atoi(env);
-            p.trace_tile_op = 64;  // lm_head; CUDALLM_TRACE_TILE_OP picks another operation's tiles to stamp
-            if (const char* env = std::getenv("CUDALLM_TRACE_TILE_OP")) p.trace_tile_op = std::atoi(env);
+            int trace_op = 64;  // lm_head; CUDALLM_TRACE_TILE_OP picks the weight operation whose tiles are stamped first
+            if (const char* env = std::getenv("CUDALLM_TRACE_TILE_OP")) trace_op = std::atoi(env);
             // The persistent kernel is compiled for the default tile shape (matvec_rpb selects the tile rows of
             // the per-op kernels only; results do not depend on it).
             const int rpb = 0;
@@ -161,6 +161,17 @@ Engine::Engine(const std::string& path, const EngineOptions& opts) : opts_(opts)
             p.g_gu = make_tile_geom(c.wtype, Epilogue::SWIGLU, 2 * c.inter, c.hidden, rpb);
             p.g_down = make_tile_geom(c.wtype, Epilogue::ADD, c.hidden, c.inter, rpb);
             p.g_lm = make_tile_geom(c.wtype, Epilogue::STORE, c.vocab, c.hidden, rpb);
+            // Global index (in CTA 0's tile stream) of the first tile of weight operation trace_op: CTA 0 owns
+            // rows [0, rows / grid) of every operation.
+            const int grid = decode_step_grid();
+            const TileGeom* per_layer[4] = {&p.g_qkv, &p.g_wo, &p.g_gu, &p.g_down};
+            int t0 = 0;
+            for (int o = 0; o < std::min(std::max(trace_op, 0), 64); ++o) {
+                const TileGeom& g = *per_layer[o % 4];
+                const int rows = g.out_rows / grid;
+                t0 += (rows + g.rows_per_tile - 1) / g.rows_per_tile * g.n_seg;
+            }
+            p.trace_t0 = t0;
         }
     } catch (...) {
         free_all();

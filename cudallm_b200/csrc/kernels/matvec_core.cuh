@@ -199,16 +199,13 @@ __device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& t
     if constexpr (CPL > 0) seg_bytes = CPL * 512;
     [[maybe_unused]] const int groups = K >> 7;
     if constexpr (WT == WeightType::INT4 && CPL > 0) {
-        // Compile-time tile shape: one scalar chain per row (the group scale is applied per chunk).
-        float r[N];
-#pragma unroll
-        for (int i = 0; i < N; ++i) r[i] = 0.f;
+        // Compile-time tile shape: one scalar chain per row, accumulated straight into acc (the group
+        // scale is applied per chunk).
         const __half* sc = static_cast<const __half*>(scales);
 #pragma unroll
         for (int j = 0; j < CPL; ++j) {
             const int c = lane + 32 * j;
             const int gc = seg_chunk0 + c;
-
             const float xsum = xc[gc];
             float4 xa[4], xb[4];  // word k: columns 8k..8k+3 and 8k+4..8k+7
 #pragma unroll
@@ -231,11 +228,9 @@ __device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& t
                     pp = fma2(make_float2(i4half(lo, 0x7344), i4half(hi, 0x7344)), make_float2(xb[k].z, xb[k].w), pp);
                 }
                 const float si = __half2float(__ldg(sc + static_cast<size_t>(tr.global_row(i)) * groups + (gc >> 2)));
-                r[i] = fmaf(si, fmaf(256.f, pp.x + pp.y, -136.f * xsum), r[i]);
+                acc[i] = fmaf(si, fmaf(256.f, pp.x + pp.y, -136.f * xsum), acc[i]);
             }
         }
-#pragma unroll
-        for (int i = 0; i < N; ++i) acc[i] += r[i] + 0.f;  // + the (zero) second chain, as below
         return;
     } else {
         // Two accumulation chains per row (.x and .y), advanced together by one packed instruction.

@@ -186,15 +186,15 @@ class Engine:
         """Per-CTA timestamps of each following step (persistent path only)."""
         _check(_lib().cudallm_debug_trace(self._handle(), int(bool(enable))))
 
-    def read_trace(self, grid: int = 1024, slots: int = 328) -> tuple[np.ndarray, np.ndarray]:
-        """Last traced step: (uint64 [grid][ops][4] per-CTA stamps, uint64 [256][4] lm_head tile stamps
-        of CTA 0), nanoseconds (see decode_step.h)."""
-        buf = np.zeros(grid * slots + 1024, dtype=np.uint64)
+    def read_trace(self, grid: int = 1024, slots: int = 82 * 6) -> tuple[np.ndarray, np.ndarray]:
+        """Last traced step: (uint64 [grid][ops][6] per-CTA stamps, uint64 [256][5] tile stamps of CTA 0),
+        nanoseconds (layout in csrc/engine/decode_step.h)."""
+        buf = np.zeros(grid * slots + 256 * 5, dtype=np.uint64)
         g, sl = c_int(0), c_int(0)
         _check(_lib().cudallm_debug_read_trace(self._handle(), buf.ctypes.data_as(POINTER(c_ulonglong)), buf.size,
                                                ctypes.byref(g), ctypes.byref(sl)))
         n = g.value * sl.value
-        return buf[:n].reshape(g.value, sl.value // 4, 4), buf[n:n + 1024].reshape(256, 4)
+        return buf[:n].reshape(g.value, sl.value // 6, 6), buf[n:n + 256 * 5].reshape(256, 5)
 
     def step(self, token: int | None = None, *, want_logits: bool = False) -> tuple[int, np.ndarray | None]:
         nxt = c_int(0)

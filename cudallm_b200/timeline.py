@@ -7,8 +7,9 @@ Runs a seeded prompt through the engine, traces the next step (cudallm_debug_tra
     operation ends (median and slowest CTA) and when the copy producer started streaming its weights;
   * per layer, averaged over the 16 layers: the critical duration of each operation (slowest CTA's end
     minus the slowest CTA's wait end) and the median dependency wait;
-  * the tiles of one weight operation on CTA 0 (--tile-op: layer*4 + {0 qkv, 1 o-proj, 2 gate/up,
-    3 down}, 64 = lm_head): copy issued, consumer starts waiting, data ready, consumer done;
+  * 256 consecutive tiles of CTA 0 starting at weight operation --tile-op (layer*4 + {0 qkv, 1 o-proj,
+    2 gate/up, 3 down}, 64 = lm_head): L2 prefetch issued, copy issued, consumer starts waiting, data
+    ready, consumer done;
   * for gate/up and down of layer 1, the per-CTA durations (straggler spread) and the slowest SMs.
 Times are microseconds from the start of the step. Stamp layout: csrc/engine/decode_step.h.
 """
@@ -63,23 +64,32 @@ def report(tr: np.ndarray, tt: np.ndarray, tile_op: int) -> None:
     waits = us(np.sum([tr[:, k, 1] - tr[:, k, 0] for k in range(81)], axis=0))
     print(f"step span {span:.1f} us; per-CTA total dependency wait: median {np.median(waits):.1f} us, "
           f"max {waits.max():.1f} us")
-    print("per layer (mean over 16 layers): critical duration / median wait, us")
+    print("per layer (mean over 16 layers), us: critical duration / median wait; weight operations also: median "
+          "staging (wait end -> vector staged), first tile (staged -> warp 0 done with its first tile), rest")
     for kind in ("qkv", "att", "wo", "gu", "down"):
         ks = [i for i, n in enumerate(names) if n.endswith("." + kind)]
         dur = np.mean([us((tr[:, k, 2] - t0).max() - (tr[:, k, 1] - t0).max()) for k in ks])
         wt = np.mean([us(np.median(tr[:, k, 1] - tr[:, k, 0])) for k in ks])
-        print(f"  {kind:5s} {dur:6.2f} / {wt:5.2f}")
+        line = f"  {kind:5s} {dur:6.2f} / {wt:5.2f}"
+        if kind != "att":
+            stg = np.mean([us(np.median(tr[:, k, 4] - tr[:, k, 1])) for k in ks])
+            first = np.mean([us(np.median(tr[:, k, 5] - tr[:, k, 4])) for k in ks])
+            rest = np.mean([us(np.median(tr[:, k, 2] - tr[:, k, 5])) for k in ks])
+            line += f"   staging {stg:5.2f}  first tile {first:5.2f}  rest {rest:5.2f}"
+        print(line)
     n = int((tt[:, 0] > 0).sum())
     if n:
-        tt = us(tt[:n] - tt[0, 0])
-        issue, wstart, ready, done = (tt[:, k] for k in range(4))
-        print(f"tiles of weight operation {tile_op} on CTA 0 ({n}): issue / wait start / ready / done, us")
-        for i in range(min(n, 48)):
-            print(f"  {i:3d} {issue[i]:8.2f} {wstart[i]:8.2f} {ready[i]:8.2f} {done[i]:8.2f}   "
+        tt = tt[:n].astype(np.int64)
+        base = tt[0, 0]
+        rel = lambda a: np.where(a > 0, (a - base) / 1e3, np.nan)  # noqa: E731
+        issue, wstart, ready, done, pref = (rel(tt[:, k]) for k in range(5))
+        print(f"{n} tiles of CTA 0 from weight operation {tile_op}: prefetch / issue / wait start / ready / done, us")
+        for i in range(min(n, 64)):
+            print(f"  {i:3d} {pref[i]:8.2f} {issue[i]:8.2f} {wstart[i]:8.2f} {ready[i]:8.2f} {done[i]:8.2f}   "
                   f"issue->ready {ready[i] - issue[i]:6.2f}  wait {ready[i] - wstart[i]:5.2f}  "
                   f"compute {done[i] - ready[i]:5.2f}")
-        print(f"  median issue->ready {np.median(ready - issue):.2f}, data wait {np.median(ready - wstart):.2f}, "
-              f"compute {np.median(done - ready):.2f} us")
+        print(f"  median issue->ready {np.nanmedian(ready - issue):.2f}, data wait {np.nanmedian(ready - wstart):.2f}, "
+              f"compute {np.nanmedian(done - ready):.2f} us")
     sm = tr[:, 81, 3]
     for name in ("L1.gu", "L1.down"):
         k = names.index(name)

@@ -130,8 +130,10 @@ int cudallm_engine_device(cudallm_engine* e);
  * %globaltimer value (ns) at each operation's dependency-wait begin / end, its end, and when the
  * producer warp starts streaming its weights; 0 turns it off. */
 int cudallm_debug_trace(cudallm_engine* e, int enable);
-/* Copies the last traced step: grid x slots per-CTA values followed by 256 x 4 lm_head tile stamps of
- * CTA 0 (count >= grid*slots + 1024); *grid_out, *slots_out get the shape. Waits for queued work first. */
+/* Copies the last traced step: grid x slots per-CTA values followed by 256 x 5 stamps of 256 consecutive
+ * tiles of CTA 0 (from the lm_head's first tile unless CUDALLM_TRACE_TILE_OP named another weight operation
+ * when the engine was created); count >= grid*slots + 1280. *grid_out, *slots_out get the shape. Waits
+ * for queued work. */
 int cudallm_debug_read_trace(cudallm_engine* e, unsigned long long* out, unsigned long long count, int* grid_out,
                              int* slots_out);
 
