@@ -444,7 +444,7 @@ __device__ __forceinline__ void signal(ConsumerCtx& c, unsigned* ctr, int top = 
     csync();
     if (c.tid == 0) {
         if (top >= 0) trace_mark(*c.p, top, 2);
-        __threadfence();
+        // Release (cumulative): the other consumer warps' stores are ordered before it by csync().
         red_release_gpu_add(ctr, 1u);
     }
 }
@@ -631,7 +631,6 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
                     attend_tile<KV, true>(p.qkv, kNh, kNkv, cs, kc, vc, p.max_seq, h, tile, ctx, n_slots, p.part_o, p.part_ml,
                                           sm, c.tid, [] { csync(); });
                     if (c.tid == 0) {
-                        __threadfence();
                         const unsigned old = atom_acq_rel_gpu_add(p.sync + kSyncTicket + l * kNkv + h, 1u);
                         c.fl->role = (old == static_cast<unsigned>(n_tiles - 1)) ? 1 : 0;
                     }
@@ -689,7 +688,6 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
         }
         __stcg(p.am_v + blockIdx.x, v);
         __stcg(p.am_i + blockIdx.x, i);
-        __threadfence();
         const unsigned old = atom_acq_rel_gpu_add(p.sync + kSyncLm, 1u);
         c.fl->role = (old == static_cast<unsigned>(G - 1)) ? 1 : 0;
     }

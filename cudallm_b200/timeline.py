@@ -94,9 +94,12 @@ def report(tr: np.ndarray, tt: np.ndarray, tile_op: int) -> None:
     for name in ("L1.gu", "L1.down"):
         k = names.index(name)
         dur = us(tr[:, k, 2] - tr[:, k, 1])
-        slow = np.argsort(-dur)[:6]
-        print(f"{name}: per-CTA duration median {np.median(dur):.2f} max {dur.max():.2f} us; slowest (SM, us): "
-              + ", ".join(f"({int(sm[i])}, {dur[i]:.1f})" for i in slow))
+        order = np.argsort(-dur)
+        print(f"{name}: per-CTA duration median {np.median(dur):.2f} max {dur.max():.2f} us")
+        print("    cta   sm  producer_start  wait_end  staged  first_tile  end   (us from step start)")
+        for i in list(order[:6]) + list(order[-6:]):
+            st = [us(tr[i, k, j] - t0) for j in (3, 1, 4, 5, 2)]
+            print(f"    {int(i):3d} {int(sm[i]):4d} " + "  ".join(f"{v:8.2f}" for v in st))
 
 
 def main(argv: list[str] | None = None) -> int:
