@@ -143,29 +143,6 @@ __device__ __forceinline__ void fail(const StepParams& p, volatile Flags* fl, un
     atomicCAS(p.err + 1, 0u, id);
 }
 
-// Bounded spin until *ctr >= target (acquire). Gives up on timeout or when another CTA reported an
-// error; returns false then.
-__device__ bool spin_until(const StepParams& p, const unsigned* ctr, unsigned target, volatile Flags* fl, unsigned id) {
-    uint64_t t0 = 0;
-    for (uint32_t it = 1;; ++it) {
-        if (ld_acquire_gpu(ctr) >= target) return true;
-        if ((it & 31) == 0) {
-            if (*reinterpret_cast<volatile unsigned*>(p.err) != 0) {
-                fl->abort = 1;
-                return false;
-            }
-            const uint64_t t = global_ns();
-            if (t0 == 0) {
-                t0 = t;
-            } else if (t - t0 > p.wait_limit_ns) {
-                fail(p, fl, kErrWaitTimeout, id);
-                return false;
-            }
-        }
-        __nanosleep(64);
-    }
-}
-
 // Bounded wait on an mbarrier phase; also gives up when the CTA aborts (check_abort). With
 // `tile_word`, first waits until the producer has published tile `tile` into the stage (a parity wait
 // only distinguishes the barrier's current and previous phase; a consumer warp can be further ahead).
@@ -427,27 +404,132 @@ struct ConsumerCtx {
 
 __device__ __forceinline__ void csync() { named_barrier(1, kCt); }
 
-// Waits (thread 0) for a dependency; all consumer threads learn the outcome. `top` = trace op index.
-__device__ __forceinline__ bool dep_wait(ConsumerCtx& c, const unsigned* ctr, unsigned target, unsigned id, int top) {
-    if (c.tid == 0) {
-        trace_mark(*c.p, top, 0);
-        c.fl->ok = c.fl->abort ? 0 : (spin_until(*c.p, ctr, target, c.fl, id) ? 1 : 0);
-        trace_mark(*c.p, top, 1);
+// ---- Tagged activations ----------------------------------------------------------------------------
+// Every activation that crosses CTAs is written as one 64-bit word (tag << 32 | fp32 bits) by a single
+// 8-byte store, which is single-copy atomic: a reader that sees the current tag sees the value written
+// with it. The tag names the launch (step_tag), the layer and the vector, so a reader needs no counter,
+// no release and no second round trip: it polls the data until the tags are current. A slot is
+// rewritten only after every CTA has passed a later all-to-all dependency, hence after all its readers.
+enum TagKind : uint32_t { kTagQkv = 1, kTagAtt = 2, kTagXmid = 3, kTagXout = 4, kTagAct = 5 };
+__device__ __forceinline__ uint32_t act_tag(const StepParams& p, int layer, uint32_t kind) {
+    return (p.step_tag << 8) | (static_cast<uint32_t>(layer) << 3) | kind;
+}
+__device__ __forceinline__ void st_tagged(unsigned long long* dst, float v, uint32_t tag) {
+    const unsigned long long w = (static_cast<unsigned long long>(tag) << 32) | __float_as_uint(v);
+    asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(dst), "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_tagged(const unsigned long long* src) {
+    unsigned long long w;
+    asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(w) : "l"(src) : "memory");
+    return w;
+}
+__device__ __forceinline__ void ld_tagged2(const unsigned long long* src, unsigned long long& a, unsigned long long& b) {
+    asm volatile("ld.relaxed.gpu.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(src) : "memory");
+}
+__device__ __forceinline__ bool tag_is(unsigned long long w, uint32_t tag) { return static_cast<uint32_t>(w >> 32) == tag; }
+__device__ __forceinline__ float tag_value(unsigned long long w) { return __uint_as_float(static_cast<uint32_t>(w)); }
+
+// Bounded poll bookkeeping: false once the wait limit passed (recorded as a timeout) or another CTA
+// reported an error.
+struct PollClock {
+    uint64_t t0 = 0;
+    __device__ __forceinline__ bool keep_going(const StepParams& p, volatile Flags* fl, unsigned id) {
+        if (fl->abort) return false;
+        if (*reinterpret_cast<volatile unsigned*>(p.err) != 0) {
+            fl->abort = 1;
+            return false;
+        }
+        const uint64_t t = global_ns();
+        if (t0 == 0) {
+            t0 = t;
+        } else if (t - t0 > p.wait_limit_ns) {
+            fail(p, fl, kErrWaitTimeout, id);
+            return false;
+        }
+        return true;
+    }
+};
+
+// One element of a tagged vector, polled until it carries `tag` (or the wait gives up).
+__device__ __forceinline__ float get_tagged(const StepParams& p, volatile Flags* fl, const unsigned long long* src, uint32_t tag,
+                                            unsigned id) {
+    unsigned long long w = ld_tagged(src);
+    PollClock clk;
+    for (uint32_t it = 1; !tag_is(w, tag); ++it) {
+        __nanosleep(32);
+        w = ld_tagged(src);
+        if ((it & 15) == 0 && !clk.keep_going(p, fl, id)) break;
+    }
+    return tag_value(w);
+}
+
+struct TaggedSrc {
+    const StepParams* p;
+    volatile Flags* fl;
+    const unsigned long long* v;
+    uint32_t tag;
+    unsigned id;
+    __device__ __forceinline__ float operator()(int i) const { return get_tagged(*p, fl, v + i, tag, id); }
+};
+struct TaggedDst {
+    unsigned long long* v;
+    uint32_t tag;
+    __device__ __forceinline__ void operator()(int i, float x) const { st_tagged(v + i, x, tag); }
+};
+
+// Loads the input vector of an operation into v[i] (columns 4q..4q+3, q = tid + i * kCt): the
+// embedding row for the first QKV projection (src == null), else a tagged vector, where every thread
+// issues all of its loads and then re-reads only the elements whose tag is not yet current (their CTAs
+// are still computing) until all are. Returns false (all threads) if the CTA gave up.
+template <WeightType WT>
+__device__ bool load_input(ConsumerCtx& c, const unsigned long long* src, uint32_t tag, int K, int tok, unsigned id,
+                           int top, float4 (&v)[kStagePer]) {
+    const StepParams& p = *c.p;
+    const int n4 = K / 4;
+    if (src == nullptr) {
+#pragma unroll
+        for (int i = 0; i < kStagePer; ++i) {
+            const int q = c.tid + i * kCt;
+            if (q < n4) v[i] = EmbVec4<WT>{&p, tok}(q);
+        }
+        if (c.tid == 0) trace_mark(p, top, 1);
+        return true;
+    }
+    uint32_t pending = 0;
+#pragma unroll
+    for (int i = 0; i < kStagePer; ++i) {
+        const int q = c.tid + i * kCt;
+        if (q < n4) {
+            unsigned long long a, b, d, e;
+            ld_tagged2(src + 4 * q, a, b);
+            ld_tagged2(src + 4 * q + 2, d, e);
+            v[i] = make_float4(tag_value(a), tag_value(b), tag_value(d), tag_value(e));
+            if (!(tag_is(a, tag) && tag_is(b, tag) && tag_is(d, tag) && tag_is(e, tag))) pending |= 1u << i;
+        }
+    }
+    PollClock clk;
+    for (uint32_t it = 1; pending != 0; ++it) {
+        __nanosleep(64);
+#pragma unroll
+        for (int i = 0; i < kStagePer; ++i) {
+            if (pending & (1u << i)) {
+                const int q = c.tid + i * kCt;
+                unsigned long long a, b, d, e;
+                ld_tagged2(src + 4 * q, a, b);
+                ld_tagged2(src + 4 * q + 2, d, e);
+                v[i] = make_float4(tag_value(a), tag_value(b), tag_value(d), tag_value(e));
+                if (tag_is(a, tag) && tag_is(b, tag) && tag_is(d, tag) && tag_is(e, tag)) pending &= ~(1u << i);
+            }
+        }
+        if ((it & 7) == 0 && !clk.keep_going(p, c.fl, id)) break;
     }
     csync();
-    const bool ok = c.fl->ok != 0;
+    if (c.tid == 0) trace_mark(p, top, 1);
+    const bool ok = c.fl->abort == 0;
     csync();
     return ok;
 }
 
-__device__ __forceinline__ void signal(ConsumerCtx& c, unsigned* ctr, int top = -1) {
-    csync();
-    if (c.tid == 0) {
-        if (top >= 0) trace_mark(*c.p, top, 2);
-        // Release (cumulative): the other consumer warps' stores are ordered before it by csync().
-        red_release_gpu_add(ctr, 1u);
-    }
-}
 
 // Waits for, accumulates and releases the n_seg tiles of one row group (first global tile `t0`),
 // reduces the N stage rows across the warp and leaves row i's value in my[i]. Not inlined: one copy
@@ -513,14 +595,18 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
             const int r = r0 + c.lane;
             const float d = my[c.lane];
             if (kind == kQkv) {
-                __stcg(p.qkv + r, d);
+                st_tagged(p.t_qkv + r, d, act_tag(p, layer, kTagQkv));
             } else if (kind == kWo || kind == kDown) {
                 const float v = c.res[r - lo] + d;
                 c.res[r - lo] = v;
-                __stcg(p.x + r, v);
-                if (kind == kDown && p.debug_res) p.debug_res[static_cast<size_t>(layer + 1) * kH + r] = v;
+                if (kind == kWo) {
+                    st_tagged(p.t_xmid + r, v, act_tag(p, layer, kTagXmid));
+                } else {
+                    st_tagged(p.t_xout + r, v, act_tag(p, layer, kTagXout));
+                    if (p.debug_res) p.debug_res[static_cast<size_t>(layer + 1) * kH + r] = v;
+                }
             } else if (kind == kGu) {
-                __stcg(p.act + r, silu_f(d) * my[R + c.lane]);
+                st_tagged(p.t_act + r, silu_f(d) * my[R + c.lane], act_tag(p, layer, kTagAct));
             } else {
                 __stcg(p.logits + r, d);
                 if (better(d, r, bv, bi)) {
@@ -536,17 +622,6 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
     csync();
     return c.fl->abort == 0;
 }
-
-// Staging source: a global fp32 vector read through L2, or (vec == null) the embedding row `tok`.
-template <WeightType WT>
-struct StageSrc {
-    const StepParams* p;
-    const float* vec;
-    int tok;
-    __device__ __forceinline__ float4 operator()(int q) const {
-        return vec ? __ldcg(reinterpret_cast<const float4*>(vec) + q) : EmbVec4<WT>{p, tok}(q);
-    }
-};
 
 template <WeightType WT, typename KV>
 __device__ void run_consumers(ConsumerCtx& c, float* cs) {
@@ -576,7 +651,6 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
         for (int r = lo + c.tid; r < hi; r += kCt) {
             const float v = emb_value<WT>(p, tok, r);
             c.res[r - lo] = v;
-            __stcg(p.x + r, v);
             if (p.debug_res) p.debug_res[r] = v;
         }
         csync();
@@ -591,13 +665,17 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
         const bool lm = o == kWeightOps - 1;
         const int l = lm ? kStepLayers : o / kOpsPerLayer;
         const int kind = lm ? kLm : o % kOpsPerLayer;
-        const float* svec = p.x;
+        const int top = lm ? 80 : l * 5 + (kind == kQkv ? 0 : kind + 1);  // trace entry of this operation
+        // Input: the tagged vector the previous operation of every CTA wrote (the embedding row for the
+        // first QKV projection), RMS-normalised before the QKV, gate/up and lm_head projections.
+        const unsigned long long* tsrc = nullptr;
+        uint32_t tag = 0;
         const float* snorm = nullptr;
         int sK = kH;
         if (kind == kQkv) {
             const size_t layer_bytes = static_cast<size_t>(l) * kNkv * p.max_seq * kHd * sizeof(KV);
             // The cached K/V rows this CTA's attention will read do not depend on this step: pull them
-            // into L2 now, before the QKV dependency (the same assignment as the attention below).
+            // into L2 now (the same assignment as the attention below).
             for (int q = c.tid; q < 2 * kNkv * n_tiles; q += kCt) {
                 const int i = q >> 1;
                 const int h = i / n_tiles, tile = i % n_tiles;
@@ -608,28 +686,38 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
                 const uint8_t* base = static_cast<const uint8_t*>((q & 1) ? p.v_cache : p.k_cache);
                 bulk_prefetch_l2(base + layer_bytes + off, static_cast<uint32_t>(n * kHd * sizeof(KV)));
             }
-            if (l > 0 && !dep_wait(c, p.sync + kSyncDown + l - 1, G, 10u + l, l * 5 + 0)) return;
-            svec = l == 0 ? nullptr : p.x;
+            if (l > 0) {
+                tsrc = p.t_xout;
+                tag = act_tag(p, l - 1, kTagXout);
+            }
             snorm = p.layers[l].attn_norm;
         } else if (kind == kWo) {
-            // RoPE + KV write + attention, then the O projection's input.
+            // RoPE + KV write + attention (reading this layer's tagged q/k/v), then the O projection's input.
+            if (c.tid == 0) {  // no separate wait: the attention polls its tagged inputs
+                trace_mark(p, l * 5 + 1, 0);
+                trace_mark(p, l * 5 + 1, 1);
+            }
             const size_t layer_off = static_cast<size_t>(l) * kNkv * p.max_seq * kHd;
             KV* kc = static_cast<KV*>(p.k_cache) + layer_off;
             KV* vc = static_cast<KV*>(p.v_cache) + layer_off;
-            if (!dep_wait(c, p.sync + kSyncQkv + l, G, 30u + l, l * 5 + 1)) return;
+            const TaggedSrc qkv_src{&p, c.fl, p.t_qkv, act_tag(p, l, kTagQkv), 30u + l};
+            const TaggedDst att_dst{p.t_att, act_tag(p, l, kTagAtt)};
             if (whole_head) {
                 if (blockIdx.x % head_stride == 0 && blockIdx.x / head_stride < kNkv) {
+                    const int h = blockIdx.x / head_stride;
+                    uint4 hk[4];  // cached keys of the first pass: independent of this step's projections
+                    if (kHeadWarpTokens * c.cw < ctx) head_load_keys<KV>(kc, p.max_seq, h, pos, 0, c.cw, c.lane, hk);
                     HeadPassSmem<KV>& sm = *reinterpret_cast<HeadPassSmem<KV>*>(c.xp);
-                    attend_head_pass<KV>(p.qkv, kNh, kNkv, cs, kc, vc, p.max_seq, blockIdx.x / head_stride, ctx, p.att, sm,
-                                         c.tid, [] { csync(); });
-                    signal(c, p.sync + kSyncAtt + l);
+                    attend_head_pass<KV>(qkv_src, kNh, kNkv, cs, kc, vc, p.max_seq, h, ctx, att_dst, sm, c.tid, hk,
+                                         [] { csync(); });
+                    csync();
                 }
             } else {
                 AttSmem<KV>& sm = *reinterpret_cast<AttSmem<KV>*>(c.xp);
                 for (int i = blockIdx.x; i < kNkv * n_tiles; i += G) {
                     const int h = i / n_tiles, tile = i % n_tiles;
-                    attend_tile<KV, true>(p.qkv, kNh, kNkv, cs, kc, vc, p.max_seq, h, tile, ctx, n_slots, p.part_o, p.part_ml,
-                                          sm, c.tid, [] { csync(); });
+                    attend_tile<KV, true>(qkv_src, kNh, kNkv, cs, kc, vc, p.max_seq, h, tile, ctx, n_slots, p.part_o,
+                                          p.part_ml, sm, c.tid, [] { csync(); });
                     if (c.tid == 0) {
                         const unsigned old = atom_acq_rel_gpu_add(p.sync + kSyncTicket + l * kNkv + h, 1u);
                         c.fl->role = (old == static_cast<unsigned>(n_tiles - 1)) ? 1 : 0;
@@ -638,35 +726,39 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
                     const bool combiner = c.fl->role != 0;
                     csync();
                     if (combiner) {
-                        combine_head(p.part_o, p.part_ml, h, n_tiles, n_slots, p.att, c.tid);
-                        signal(c, p.sync + kSyncAtt + l);
+                        combine_head(p.part_o, p.part_ml, h, n_tiles, n_slots, att_dst, c.tid);
+                        csync();
                     }
                 }
             }
             if (c.tid == 0) trace_mark(p, l * 5 + 1, 2);
-            if (!dep_wait(c, p.sync + kSyncAtt + l, kNkv, 50u + l, l * 5 + 2)) return;
-            svec = p.att;
+            if (c.fl->abort) return;
+            tsrc = p.t_att;
+            tag = act_tag(p, l, kTagAtt);
         } else if (kind == kGu) {
-            if (!dep_wait(c, p.sync + kSyncWo + l, G, 70u + l, l * 5 + 3)) return;
+            tsrc = p.t_xmid;
+            tag = act_tag(p, l, kTagXmid);
             snorm = p.layers[l].ffn_norm;
         } else if (kind == kDown) {
-            if (!dep_wait(c, p.sync + kSyncGu + l, G, 90u + l, l * 5 + 4)) return;
-            svec = p.act;
+            tsrc = p.t_act;
+            tag = act_tag(p, l, kTagAct);
             sK = 4 * kH;
         } else {
-            if (!dep_wait(c, p.sync + kSyncDown + kStepLayers - 1, G, 110u, 80)) return;
+            tsrc = p.t_xout;
+            tag = act_tag(p, kStepLayers - 1, kTagXout);
             snorm = p.final_norm;
         }
-        stage_vector<WT>(StageSrc<WT>{&p, svec, tok}, sK, snorm, p.eps, c.xp, c.xc, c.red, c.tid, kCt, [] { csync(); });
-        const int top = lm ? 80 : l * 5 + (kind == kQkv ? 0 : kind + 1);  // trace entry of this operation
+        if (c.tid == 0) trace_mark(p, top, 0);
+        {
+            float4 v[kStagePer];
+            if (!load_input<WT>(c, tsrc, tag, sK, tok, 10u + o, top, v)) return;
+            stage_commit<WT>(v, sK, snorm, p.eps, c.xp, c.xc, c.red, c.tid, kCt, [] { csync(); });
+        }
         if (c.tid == 0) trace_mark(p, top, 4);
         const bool ok = kind == kDown ? run_tiles<WT, kNd, kCpld>(c, o, kind, bv, bi, l)
                                       : run_tiles<WT, kN, kCpl>(c, o, kind, bv, bi, l);
         if (!ok) return;
-        if (kind != kLm) {
-            const int counter = kind == kQkv ? kSyncQkv : (kind == kWo ? kSyncWo : (kind == kGu ? kSyncGu : kSyncDown));
-            signal(c, p.sync + counter + l, top);
-        }
+        if (kind != kLm && c.tid == 0) trace_mark(p, top, 2);  // run_tiles ended with a block barrier
     }
     // ---- lm_head done: CTA argmax, then the last CTA commits the token ----------------------
     float* am_v = reinterpret_cast<float*>(c.scratch);  // scratch is free again after run_tiles

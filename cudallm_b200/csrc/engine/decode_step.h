@@ -57,9 +57,10 @@ inline constexpr size_t trace_words(int grid) {
 constexpr unsigned kErrWaitTimeout = 1u;
 constexpr unsigned kErrAborted = 2u;
 
-// Counters the step uses (zeroed at creation, after an error and by the step itself at its end).
-constexpr int kSyncQkv = 0, kSyncAtt = 16, kSyncWo = 32, kSyncGu = 48, kSyncDown = 64, kSyncTicket = 80,
-              kSyncLm = 80 + 16 * 8, kSyncWords = 256;
+// Counters the step uses (zeroed at creation, after an error and by the step itself at its end): the
+// split attention's per-(layer, KV head) tickets and the lm_head ticket. Activations between operations
+// are synchronised through their tags, not counters.
+constexpr int kSyncTicket = 0, kSyncLm = 16 * 8, kSyncWords = 256;
 
 struct StepParams {
     StepLayer layers[kStepLayers];
@@ -67,10 +68,14 @@ struct StepParams {
     const void* emb_s;
     const float* final_norm;
     const float* inv_freq;
-    float* x;       // [2048] residual stream
-    float* qkv;     // [3072]
-    float* att;     // [2048]
-    float* act;     // [8192]
+    // Activations exchanged between CTAs, each element a (value, tag) word: tag = step << 8 | layer << 3 |
+    // kind (decode_step.cu), so a reader polls the data itself instead of a counter.
+    unsigned long long* t_qkv;   // [3072] q | k | v projections
+    unsigned long long* t_att;   // [2048] attention output
+    unsigned long long* t_xmid;  // [2048] residual after the O projection
+    unsigned long long* t_xout;  // [2048] residual after the down projection
+    unsigned long long* t_act;   // [8192] SwiGLU output
+    unsigned step_tag;           // this launch's step number (1 .. 2^24 - 1)
     float* logits;  // [128256]
     void* k_cache;  // [16][8][max_seq][64]
     void* v_cache;

@@ -104,6 +104,9 @@ Engine::Engine(const std::string& path, const EngineOptions& opts) : opts_(opts)
         alloc(&state_, 1);
         alloc(&sync_, kSyncWords);
         alloc(&debug_res_, static_cast<size_t>(c.n_layers + 1) * H);
+        tagged_words_ = (NH + 2 * KV) * D + NH * D + 2 * H + I;
+        alloc(&tagged_, tagged_words_);
+        CLLM_CUDA(cudaMemset(tagged_, 0, tagged_words_ * sizeof(unsigned long long)));
         CLLM_CUDA(cudaMemset(state_, 0, sizeof(DevState)));
         CLLM_CUDA(cudaMemset(sync_, 0, kSyncWords * sizeof(unsigned)));
         CLLM_CUDA(cudaMemset(k_cache_, 0, cache_elems * 2));
@@ -123,10 +126,12 @@ Engine::Engine(const std::string& path, const EngineOptions& opts) : opts_(opts)
             p.emb_s = W.tok_embeddings.scales;
             p.final_norm = W.final_norm;
             p.inv_freq = W.rope_inv_freq;
-            p.x = x_;
-            p.qkv = qkv_;
-            p.att = att_;
-            p.act = act_;
+            p.t_qkv = tagged_;
+            p.t_att = p.t_qkv + (NH + 2 * KV) * D;
+            p.t_xmid = p.t_att + NH * D;
+            p.t_xout = p.t_xmid + H;
+            p.t_act = p.t_xout + H;
+            p.step_tag = 0;
             p.logits = logits_;
             p.k_cache = k_cache_;
             p.v_cache = v_cache_;
@@ -188,7 +193,7 @@ void Engine::free_all() noexcept {
     graph_exec_ = nullptr;
     graph_ = nullptr;
     void* bufs[] = {x_,      xb_,      qkv_,  att_,  tmp_,   gu_,   act_,       logits_, k_cache_,
-                    v_cache_, part_o_, part_ml_, am_v_, am_i_, state_, sync_, debug_res_, trace_};
+                    v_cache_, part_o_, part_ml_, am_v_, am_i_, state_, sync_, debug_res_, tagged_, trace_};
     for (void* b : bufs) {
         if (b) report(cudaFree(b), "cudaFree");
     }
@@ -196,6 +201,7 @@ void Engine::free_all() noexcept {
     k_cache_ = v_cache_ = nullptr;
     am_i_ = nullptr;
     trace_ = nullptr;
+    tagged_ = nullptr;
     state_ = nullptr;
     sync_ = nullptr;
     if (stream_) report(cudaStreamDestroy(stream_), "cudaStreamDestroy");
@@ -276,6 +282,13 @@ void Engine::read_trace(unsigned long long* out, size_t count) {
 
 void Engine::enqueue_persistent(int token, float* debug_res) {
     StepParams p = step_params_;
+    // Each launch tags its activations with a fresh step number (24 bits in the tag); before it would
+    // repeat, the words are cleared so no value of an earlier launch can match.
+    if (++step_tag_ >= (1u << 24)) {
+        CLLM_CUDA(cudaMemsetAsync(tagged_, 0, tagged_words_ * sizeof(unsigned long long), stream_));
+        step_tag_ = 1;
+    }
+    p.step_tag = step_tag_;
     p.token_override = token;
     p.debug_res = debug_res;
     p.trace = trace_on_ ? trace_ : nullptr;

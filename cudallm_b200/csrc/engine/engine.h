@@ -108,6 +108,10 @@ private:
     DevState* state_ = nullptr;  // token, pos, error words
     unsigned* sync_ = nullptr;
     float* debug_res_ = nullptr;
+    // Persistent step: activations exchanged between CTAs as (value, tag) words; tag of the last launch.
+    unsigned long long* tagged_ = nullptr;
+    size_t tagged_words_ = 0;
+    unsigned step_tag_ = 0;
     unsigned long long* trace_ = nullptr;
     bool trace_on_ = false;
 };

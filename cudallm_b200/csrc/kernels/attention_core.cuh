@@ -62,6 +62,17 @@ struct AttSmem {
     float red[2][kGqa][2];
 };
 
+// Element access of the q/k/v input and of the attention output: plain fp32 vectors read and written
+// through L2 (the per-op kernels); the persistent step supplies tagged-word accessors instead.
+struct PlainSrc {
+    const float* p;
+    __device__ __forceinline__ float operator()(int i) const { return __ldcg(p + i); }
+};
+struct PlainDst {
+    float* p;
+    __device__ __forceinline__ void operator()(int i, float v) const { __stcg(p + i, v); }
+};
+
 // cos/sin of angle float(pos) * inv_freq[i] for i < 32, into cs[0..31] (cos) and cs[32..63] (sin).
 __device__ __forceinline__ void rope_table(const float* __restrict__ inv_freq, int pos, float* cs, int tid) {
     if (tid < kHd / 2) {
@@ -81,8 +92,8 @@ __device__ __forceinline__ void rope_table(const float* __restrict__ inv_freq, i
 // FUSED = true (persistent decode step): q/k/v are the raw projections in qkv ([q nh | k nkv | v nkv]
 // heads of 64), q is rotated here and the new token is inserted. FUSED = false: qkv points at the final
 // (already rotated) q [nh][64] and the cache already holds every context token.
-template <typename KV, bool FUSED, typename Sync>
-__device__ __forceinline__ void attend_tile(const float* qkv, int nh, int nkv, const float* cs, KV* k_cache, KV* v_cache,
+template <typename KV, bool FUSED, typename Sync, typename Src = PlainSrc>
+__device__ __forceinline__ void attend_tile(Src qkv, int nh, int nkv, const float* cs, KV* k_cache, KV* v_cache,
                                             int max_seq, int h, int tile, int ctx, int n_slots, float* part_o,
                                             float* part_ml, AttSmem<KV>& sm, int tid, Sync sync) {
     using KV2 = typename Kv2<KV>::T;
@@ -105,8 +116,8 @@ __device__ __forceinline__ void attend_tile(const float* qkv, int nh, int nkv, c
     // Query heads h*4 .. h*4+3 (rotated here when FUSED).
     if (tid < kGqa * kHd / 2) {
         const int g = tid >> 5, i = tid & 31;
-        const float* q = qkv + (h * kGqa + g) * kHd;
-        const float x0 = __ldcg(q + i), x1 = __ldcg(q + i + kHd / 2);
+        const int q = (h * kGqa + g) * kHd;
+        const float x0 = qkv(q + i), x1 = qkv(q + i + kHd / 2);
         if constexpr (FUSED) {
             const float c = cs[i], s = cs[kHd / 2 + i];
             sm.qs[g][i] = x0 * c - x1 * s;
@@ -121,8 +132,8 @@ __device__ __forceinline__ void attend_tile(const float* qkv, int nh, int nkv, c
         // This tile holds the new token: rotate k, round k/v to the cache type, publish, use.
         const int r = pos - t0;
         if (tid < kHd / 2) {
-            const float* k = qkv + (nh + h) * kHd;
-            const float x0 = __ldcg(k + tid), x1 = __ldcg(k + tid + kHd / 2);
+            const int k = (nh + h) * kHd;
+            const float x0 = qkv(k + tid), x1 = qkv(k + tid + kHd / 2);
             const float c = cs[tid], s = cs[kHd / 2 + tid];
             const KV k0 = to_kv<KV>(x0 * c - x1 * s);
             const KV k1 = to_kv<KV>(x1 * c + x0 * s);
@@ -133,7 +144,7 @@ __device__ __forceinline__ void attend_tile(const float* qkv, int nh, int nkv, c
             kdst[tid + kHd / 2] = k1;
         } else if (tid < kHd / 2 + kHd) {
             const int d = tid - kHd / 2;
-            const KV v = to_kv<KV>(__ldcg(qkv + (nh + nkv + h) * kHd + d));
+            const KV v = to_kv<KV>(qkv((nh + nkv + h) * kHd + d));
             sm.vs[r][d] = v;
             v_cache[(static_cast<size_t>(h) * max_seq + pos) * kHd + d] = v;
         }
@@ -180,8 +191,9 @@ __device__ __forceinline__ void attend_tile(const float* qkv, int nh, int nkv, c
 
 // Merges the n_tiles partials of the 4 query heads of KV head h in tile order (one pass with a
 // running maximum) and writes out[hq*64 + d]. Thread (g, d) = (tid/64, tid%64) of a 256-thread group.
+template <typename Dst = PlainDst>
 __device__ __forceinline__ void combine_head(const float* part_o, const float* part_ml, int h, int n_tiles, int n_slots,
-                                             float* out, int tid) {
+                                             Dst out, int tid) {
     const int g = tid >> 6, d = tid & 63;
     const int hq = h * kGqa + g;
     const float2* ml = reinterpret_cast<const float2*>(part_ml + static_cast<size_t>(hq) * n_slots * 2);
@@ -197,7 +209,7 @@ __device__ __forceinline__ void combine_head(const float* part_o, const float* p
         acc = acc * a + o * b;
         M = mn;
     }
-    __stcg(out + hq * kHd + d, acc / L);
+    out(hq * kHd + d, acc / L);
 }
 
 // ---- whole-head attention (short contexts) -------------------------------------------------------
@@ -222,9 +234,10 @@ __device__ __forceinline__ void unpack8(const uint4& u, float (&v)[8]) {
 // One 256-thread group computes all 4 query heads of KV head h over the whole context, in passes of
 // 128 tokens: warp w owns tokens p0 + 16w + i. For the scores, lane pair (2i, 2i+1) holds the key row of
 // token i (dims 0-31 and 32-63); for p.V, lane l holds V[token][2l .. 2l+1] of each of the 16 tokens.
-// A pass's key loads are issued together (in pass 0 together with the new token's q/k/v) and its value
-// loads right after the scores, so a pass costs about one L2 round trip. Each warp keeps a running softmax (max, sum, p.V) per query head; the 8 warp
-// states are merged in warp order.
+// The keys of pass 0 are loaded before the step's QKV dependency (they are cached rows); later passes
+// load their keys at the pass start. Values are loaded right after the scores (their latency overlaps
+// the softmax). Each warp keeps a running softmax (max, sum, p.V) per query head; the 8 warp states are
+// merged in warp order.
 constexpr int kHeadWarpTokens = 16;
 constexpr int kHeadPassTokens = 8 * kHeadWarpTokens;
 
@@ -263,28 +276,27 @@ __device__ __forceinline__ void head_load_values(const KV* v_cache, int max_seq,
 
 // Attention of KV head h for context ctx (= pos + 1): rotates the 4 query heads and the new key
 // (cs = rope table of pos), rounds k and v to the cache type, writes them to the cache and uses the
-// rounded values. out receives [4][64] at query head 4h. `sync()` is a barrier over the 256
-// participating threads.
-template <typename KV, typename Sync>
-__device__ __forceinline__ void attend_head_pass(const float* qkv, int nh, int nkv, const float* cs, KV* k_cache, KV* v_cache,
-                                                 int max_seq, int h, int ctx, float* out, HeadPassSmem<KV>& sm, int tid,
-                                                 Sync sync) {
+// rounded values. out receives [4][64] at query head 4h. k holds the keys of pass 0 (head_load_keys,
+// issued by the caller before it waited for the QKV projection: they do not depend on this step).
+// `sync()` is a barrier over the 256 participating threads.
+template <typename KV, typename Sync, typename Src, typename Dst>
+__device__ __forceinline__ void attend_head_pass(Src qkv, int nh, int nkv, const float* cs, KV* k_cache, KV* v_cache,
+                                                 int max_seq, int h, int ctx, Dst out, HeadPassSmem<KV>& sm, int tid,
+                                                 uint4 (&k)[4], Sync sync) {
     using KV2 = typename Kv2<KV>::T;
     const int pos = ctx - 1;
     const int w = tid >> 5, lane = tid & 31;
-    uint4 k[4];
-    if (kHeadWarpTokens * w < ctx) head_load_keys<KV>(k_cache, max_seq, h, pos, 0, w, lane, k);
     if (tid < kGqa * kHd / 2) {
         const int g = tid >> 5, i = tid & 31;
-        const float* q = qkv + (h * kGqa + g) * kHd;
-        const float x0 = __ldcg(q + i), x1 = __ldcg(q + i + kHd / 2);
+        const int q = (h * kGqa + g) * kHd;
+        const float x0 = qkv(q + i), x1 = qkv(q + i + kHd / 2);
         const float c = cs[i], s = cs[kHd / 2 + i];
         sm.qs[g][i] = x0 * c - x1 * s;
         sm.qs[g][i + kHd / 2] = x1 * c + x0 * s;
     } else if (tid < kGqa * kHd / 2 + kHd / 2) {
         const int i = tid - kGqa * kHd / 2;
-        const float* kp = qkv + (nh + h) * kHd;
-        const float x0 = __ldcg(kp + i), x1 = __ldcg(kp + i + kHd / 2);
+        const int kp = (nh + h) * kHd;
+        const float x0 = qkv(kp + i), x1 = qkv(kp + i + kHd / 2);
         const float c = cs[i], s = cs[kHd / 2 + i];
         const KV k0 = to_kv<KV>(x0 * c - x1 * s), k1 = to_kv<KV>(x1 * c + x0 * s);
         sm.kn[i] = k0;
@@ -294,7 +306,7 @@ __device__ __forceinline__ void attend_head_pass(const float* qkv, int nh, int n
         kdst[i + kHd / 2] = k1;
     } else if (tid < kGqa * kHd / 2 + kHd / 2 + kHd) {
         const int d = tid - kGqa * kHd / 2 - kHd / 2;
-        const KV vv = to_kv<KV>(__ldcg(qkv + (nh + nkv + h) * kHd + d));
+        const KV vv = to_kv<KV>(qkv((nh + nkv + h) * kHd + d));
         sm.vn[d] = vv;
         v_cache[(static_cast<size_t>(h) * max_seq + pos) * kHd + d] = vv;
     }
@@ -387,7 +399,7 @@ __device__ __forceinline__ void attend_head_pass(const float* qkv, int nh, int n
             L = fmaf(sm.wl[ww][hq], e, L);
             O = fmaf(sm.wo[ww][hq][d], e, O);
         }
-        __stcg(out + (h * kGqa + hq) * kHd + d, O / L);
+        out((h * kGqa + hq) * kHd + d, O / L);
     }
 }
 

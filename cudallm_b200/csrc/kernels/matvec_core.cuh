@@ -76,19 +76,15 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); 
 // (K/1024 float4) before using any, so staging costs one memory round trip, not K/256 of them.
 // `sync()` is a barrier over those threads; `red` is 32 floats of scratch.
 constexpr int kMaxStageK = 8192;
-template <WeightType WT, typename Src4, typename Sync>
-__device__ __forceinline__ void stage_vector(Src4 src4, int K, const float* __restrict__ norm_w, float eps, float* xp,
-                                             float* xc, float* red, int tid, int nthr, Sync sync) {
+constexpr int kStagePer = kMaxStageK / 4 / 256;  // float4 per thread at the largest K
+// Second half of stage_vector: v[i] holds columns 4q..4q+3 for q = tid + i * nthr (q < K/4).
+template <WeightType WT, typename Sync>
+__device__ __forceinline__ void stage_commit(float4 (&v)[kStagePer], int K, const float* __restrict__ norm_w, float eps,
+                                             float* xp, float* xc, float* red, int tid, int nthr, Sync sync) {
     constexpr int C = Chunk<WT>::kCols;
-    constexpr int kMaxPer = kMaxStageK / 4 / 256;
+    constexpr int kMaxPer = kStagePer;
     const int nc = K / C;
     const int n4 = K / 4;
-    float4 v[kMaxPer];
-#pragma unroll
-    for (int i = 0; i < kMaxPer; ++i) {
-        const int q = tid + i * nthr;
-        if (q < n4) v[i] = src4(q);
-    }
     if (norm_w != nullptr) {
         float ss = 0.f;
 #pragma unroll
@@ -147,6 +143,19 @@ __device__ __forceinline__ void stage_vector(Src4 src4, int K, const float* __re
         }
         sync();
     }
+}
+
+template <WeightType WT, typename Src4, typename Sync>
+__device__ __forceinline__ void stage_vector(Src4 src4, int K, const float* __restrict__ norm_w, float eps, float* xp,
+                                             float* xc, float* red, int tid, int nthr, Sync sync) {
+    const int n4 = K / 4;
+    float4 v[kStagePer];
+#pragma unroll
+    for (int i = 0; i < kStagePer; ++i) {
+        const int q = tid + i * nthr;
+        if (q < n4) v[i] = src4(q);
+    }
+    stage_commit<WT>(v, K, norm_w, eps, xp, xc, red, tid, nthr, sync);
 }
 
 // float4 source over a global fp32 vector, read through L2 (data written by other CTAs).

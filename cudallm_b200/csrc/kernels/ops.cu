@@ -180,7 +180,7 @@ __global__ void __launch_bounds__(kAttThreads) attention_partial_kernel(const fl
     const int ctx = *d_pos + 1;
     const int tile = blockIdx.y;
     if (tile * kAttnTile >= ctx) return;
-    attend_tile<KV, false>(q, nh, 0, nullptr, const_cast<KV*>(k_cache), const_cast<KV*>(v_cache), max_seq, blockIdx.x, tile,
+    attend_tile<KV, false>(PlainSrc{q}, nh, 0, nullptr, const_cast<KV*>(k_cache), const_cast<KV*>(v_cache), max_seq, blockIdx.x, tile,
                            ctx, max_seq / kAttnTile, part_o, part_ml, sm, threadIdx.x, [] { __syncthreads(); });
 }
 
@@ -189,7 +189,8 @@ __global__ void __launch_bounds__(kAttThreads) attention_combine_kernel(const fl
                                                                         const int* __restrict__ d_pos, float* out,
                                                                         int max_seq) {
     const int ctx = *d_pos + 1;
-    combine_head(part_o, part_ml, blockIdx.x, (ctx + kAttnTile - 1) / kAttnTile, max_seq / kAttnTile, out, threadIdx.x);
+    combine_head(part_o, part_ml, blockIdx.x, (ctx + kAttnTile - 1) / kAttnTile, max_seq / kAttnTile, PlainDst{out},
+                 threadIdx.x);
 }
 
 // ---- elementwise (reference src/kernels/elementwise.cu:10-24) ---------------------------------
