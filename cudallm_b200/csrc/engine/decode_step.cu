@@ -313,8 +313,12 @@ __device__ void run_prefetcher(const StepParams& p, volatile Flags* fl) {
         const int bytes = min(op.g.rows_per_tile, pf.hi - r0) * op.g.row_bytes;
         for (int h = 0; h < op.g.halves; ++h) {
             const uint8_t* a = op.w + (static_cast<size_t>(r0) + static_cast<size_t>(h) * op.g.out_rows) * op.g.row_bytes;
-            for (int off = lane * 128; off < bytes; off += 32 * 128) {
-                asm volatile("prefetch.global.L2 [%0];" ::"l"(a + off) : "memory");
+            if (p.prefetch_mode == 3) {
+                if (lane == 0) bulk_prefetch_l2(a, static_cast<uint32_t>(bytes));  // one request per half (bulk engine)
+            } else {
+                for (int off = lane * 128; off < bytes; off += 32 * 128) {
+                    asm volatile("prefetch.global.L2 [%0];" ::"l"(a + off) : "memory");
+                }
             }
         }
         if (lane == 0) trace_tile(p, pt, 4);
@@ -848,7 +852,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
         if (threadIdx.x < 32) {
             run_producer(p, ring, full, empty, stage_tile, fl);
-        } else if (threadIdx.x >= 32 && threadIdx.x < 64 && p.prefetch_mode == 2) {
+        } else if (threadIdx.x >= 32 && threadIdx.x < 64 && p.prefetch_mode >= 2) {
             run_prefetcher(p, fl);
         }
         return;

@@ -95,7 +95,7 @@ struct StepParams {
     int group_size;
     unsigned long long wait_limit_ns;
     int prefetch_tiles;  // L2 prefetch distance of the weight stream, in tiles beyond the copies
-    int prefetch_mode;   // 0 none, 2 prefetch warp (load/store-unit prefetch instructions)
+    int prefetch_mode;   // 0 none, 2 prefetch warp (load/store-unit prefetch instructions), 3 same warp, bulk prefetches
     int whole_head_max_tiles;  // contexts up to this many 64-token tiles use one CTA per KV head for attention
     int trace_t0;        // first stamped tile (global index in CTA 0's tile stream)
     TileGeom g_qkv, g_wo, g_gu, g_down, g_lm;

@@ -152,7 +152,7 @@ Engine::Engine(const std::string& path, const EngineOptions& opts) : opts_(opts)
             p.wait_limit_ns = kStepWaitLimitNs;
             p.prefetch_tiles = kDefaultPrefetchTiles;
             if (const char* env = std::getenv("CUDALLM_PREFETCH_TILES")) p.prefetch_tiles = std::max(0, std::atoi(env));
-            p.prefetch_mode = 2;
+            p.prefetch_mode = 3;  // bulk L2 prefetches from the prefetch warp
             if (const char* env = std::getenv("CUDALLM_PREFETCH_MODE")) p.prefetch_mode = std::atoi(env);
             p.whole_head_max_tiles = kDefaultWholeHeadMaxTiles;
             if (const char* env = std::getenv("CUDALLM_WHOLE_HEAD_MAX_TILES")) p.whole_head_max_tiles = std::atoi(env);
