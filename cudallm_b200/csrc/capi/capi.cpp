@@ -11,6 +11,7 @@
 
 #include "common/check.h"
 #include "engine/engine.h"
+#include "kernels/batch.h"
 #include "kernels/kernels.h"
 
 struct cudallm_engine {
@@ -415,6 +416,33 @@ int cudallm_kernel_argmax(const float* logits, int n, int* out_idx) {
         cudallm::launch_argmax(dl.as<float>(), n, dpv.as<float>(), dpi.as<int>(), dtok.as<int>(), dpos.as<int>(), 0);
         sync_and_check();
         dtok.download(out_idx, sizeof(int));
+    });
+}
+
+int cudallm_kernel_gemm(const unsigned short* w, const unsigned short* x, float* y, int n, int k, int batch, int ksplit,
+                        int epilogue) {
+    return guarded([&] {
+        require(w && x && y, "cudallm_kernel_gemm: null argument");
+        require(n > 0 && k > 0 && batch >= 1 && batch <= cudallm::kBatchMax && ksplit >= 1 && k % (64 * ksplit) == 0,
+                "cudallm_kernel_gemm: bad shape (batch 1..64, k a multiple of 64 * ksplit)");
+        require(epilogue >= 0 && epilogue <= 2 && (epilogue != 2 || n % 2 == 0), "cudallm_kernel_gemm: bad epilogue");
+        const size_t wb = static_cast<size_t>(n) * k * 2, xb = static_cast<size_t>(batch) * k * 2;
+        const int n_out = epilogue == 2 ? n / 2 : n;
+        const size_t yb = static_cast<size_t>(batch) * n_out * sizeof(float);
+        DevBuf dw(wb), dx(xb), dpart(static_cast<size_t>(ksplit) * batch * n * sizeof(float)), dy(yb), derr(sizeof(unsigned));
+        dw.upload(w, wb);
+        dx.upload(x, xb);
+        dy.upload(y, yb);  // ADD accumulates into y
+        CLLM_CUDA(cudaMemset(derr.as<void>(), 0, sizeof(unsigned)));
+        cudallm::launch_gemm_bf16(dw.as<__nv_bfloat16>(), n, k, dx.as<__nv_bfloat16>(), batch, ksplit, dpart.as<float>(),
+                                  derr.as<unsigned>(), 0);
+        cudallm::launch_gemm_reduce(dpart.as<float>(), ksplit, batch, n, static_cast<cudallm::GemmEpilogue>(epilogue),
+                                    dy.as<float>(), nullptr, 0);
+        sync_and_check();
+        unsigned e = 0;
+        derr.download(&e, sizeof(e));
+        if (e != 0) throw cudallm::StateError("cudallm_kernel_gemm: a bounded wait in the GEMM gave up");
+        dy.download(y, yb);
     });
 }
 

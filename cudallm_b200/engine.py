@@ -81,6 +81,7 @@ SIGNATURES = {
     "cudallm_engine_device": ([c_void_p], c_int),
     "cudallm_debug_trace": ([c_void_p, c_int], c_int),
     "cudallm_debug_read_trace": ([c_void_p, POINTER(c_ulonglong), c_ulonglong, _INT_P, _INT_P], c_int),
+    "cudallm_kernel_gemm": ([_USHORT_P, _USHORT_P, _FLOAT_P, c_int, c_int, c_int, c_int, c_int], c_int),
     # device pointers: q, k_cache, v_cache, ctx, out, nh, nkv, hd, max_seq, stream
     "cudallm_attention_noalloc": ([c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
                                   c_int),
@@ -276,6 +277,22 @@ def kernel_attention(impl: str | int, q: np.ndarray, k_cache: np.ndarray, v_cach
     out = np.empty(nh * hd, dtype=np.float32)
     _check(_lib().cudallm_kernel_attention(_code(_IMPL, impl), _fp(q), k.ctypes.data_as(_USHORT_P),
                                            v.ctypes.data_as(_USHORT_P), int(ctx), _fp(out), nh, nkv, hd, max_seq))
+    return out
+
+
+def kernel_gemm(w_bits: np.ndarray, x_bits: np.ndarray, *, ksplit: int = 1, epilogue: str = "store",
+                y: np.ndarray | None = None) -> np.ndarray:
+    """Batched-path GEMM hook: w_bits [n][k], x_bits [batch][k] bf16 bits (uint16) -> fp32 [batch][n]
+    (store / add onto y) or [batch][n/2] (swiglu)."""
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    n, k = w.shape
+    batch = x.shape[0]
+    ep = _EPILOGUE[epilogue]
+    n_out = n // 2 if epilogue == "swiglu" else n
+    out = np.zeros((batch, n_out), dtype=np.float32) if y is None else np.ascontiguousarray(y, dtype=np.float32).copy()
+    _check(_lib().cudallm_kernel_gemm(w.ctypes.data_as(_USHORT_P), x.ctypes.data_as(_USHORT_P), _fp(out), n, k, batch,
+                                      int(ksplit), ep))
     return out
 
 

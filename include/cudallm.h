@@ -137,6 +137,14 @@ int cudallm_debug_trace(cudallm_engine* e, int enable);
 int cudallm_debug_read_trace(cudallm_engine* e, unsigned long long* out, unsigned long long count, int* grid_out,
                              int* slots_out);
 
+/* Test hook of the batched path (no counterpart in the reference): tensor-core GEMM y[b][j] (+)= sum_k
+ * x[b][k] * w[j][k] for b < batch (1..64), w [n][k] and x [batch][k] bf16 bits, fp32 result, the K range
+ * split over `ksplit` CTA rows (k a multiple of 64 * ksplit). epilogue 0 stores, 1 adds to y, 2 applies
+ * SwiGLU (y is [batch][n/2]: silu(gate) * up, gate rows first). Host pointers; allocates, runs on the
+ * default stream and synchronises like the other hooks. */
+int cudallm_kernel_gemm(const unsigned short* w, const unsigned short* x, float* y, int n, int k, int batch, int ksplit,
+                        int epilogue);
+
 /* No counterpart in the reference. Split-K decode attention (the kernels behind
  * cudallm_kernel_attention impl 1) for callers that cannot allocate device memory: code whose device
  * memory is owned by another runtime's pool, or loops that must not enter the driver's allocator.
