@@ -10,12 +10,17 @@
 #include <string>
 
 #include "common/check.h"
+#include "engine/batch_engine.h"
 #include "engine/engine.h"
 #include "kernels/batch.h"
 #include "kernels/kernels.h"
 
 struct cudallm_engine {
     cudallm::Engine* impl;
+};
+
+struct cudallm_batch {
+    cudallm::BatchEngine* impl;
 };
 
 namespace {
@@ -419,19 +424,120 @@ int cudallm_kernel_argmax(const float* logits, int n, int* out_idx) {
     });
 }
 
-int cudallm_kernel_gemm(const unsigned short* w, const unsigned short* x, float* y, int n, int k, int batch, int ksplit,
-                        int epilogue) {
+void cudallm_default_batch_options(cudallm_batch_options* out) {
+    if (!out) return;
+    std::memset(out, 0, sizeof(*out));
+    out->struct_size = sizeof(cudallm_batch_options);
+    out->n_seq = cudallm::kBatchMax;
+    out->kv_dtype = CUDALLM_KV_FP16;
+    out->device = -1;
+    out->cuda_graph = 1;
+}
+
+int cudallm_batch_create(const char* path, const cudallm_batch_options* opts, cudallm_batch** out) {
+    return guarded([&] {
+        require(out != nullptr, "cudallm_batch_create: null argument");
+        *out = nullptr;
+        require(path && opts, "cudallm_batch_create: null argument");
+        require(opts->struct_size == static_cast<int>(sizeof(cudallm_batch_options)),
+                "cudallm_batch_create: struct_size must be sizeof(cudallm_batch_options)");
+        cudallm::BatchOptions o;
+        o.n_seq = opts->n_seq;
+        o.max_seq_len = opts->max_seq_len;
+        o.kv = static_cast<cudallm::KvType>(opts->kv_dtype);
+        o.device = opts->device;
+        o.cuda_graph = opts->cuda_graph != 0;
+        auto* e = new cudallm_batch{nullptr};
+        try {
+            e->impl = new cudallm::BatchEngine(path, o);
+        } catch (...) {
+            delete e;
+            throw;
+        }
+        *out = e;
+    });
+}
+
+void cudallm_batch_destroy(cudallm_batch* e) {
+    if (!e) return;
+    delete e->impl;
+    delete e;
+}
+
+int cudallm_batch_get_config(cudallm_batch* e, cudallm_config_info* out) {
+    return guarded([&] {
+        require(e && e->impl && out, "cudallm_batch_get_config: null argument");
+        const cudallm::ModelConfig& c = e->impl->config();
+        out->weight_dtype = static_cast<int>(c.wtype);
+        out->hidden = c.hidden;
+        out->inter = c.inter;
+        out->n_layers = c.n_layers;
+        out->n_heads = c.n_heads;
+        out->n_kv_heads = c.n_kv_heads;
+        out->head_dim = c.head_dim;
+        out->vocab = c.vocab;
+        out->max_seq_len = e->impl->max_seq();
+        out->group_size = c.group_size;
+        out->rms_eps = c.rms_eps;
+        out->weight_bytes = e->impl->weight_bytes();
+    });
+}
+
+int cudallm_batch_reset(cudallm_batch* e, int seq) {
+    return guarded([&] {
+        require(e && e->impl, "cudallm_batch_reset: null engine");
+        e->impl->reset(seq);
+    });
+}
+
+int cudallm_batch_pos(cudallm_batch* e, int seq) {
+    if (!e || !e->impl || seq < 0 || seq >= e->impl->n_seq()) {
+        set_error("cudallm_batch_pos: null engine or sequence index out of range");
+        return -1;
+    }
+    return e->impl->pos(seq);
+}
+
+int cudallm_batch_step(cudallm_batch* e, const int* tokens, int* next_out, float* logits_out) {
+    return guarded([&] {
+        require(e && e->impl, "cudallm_batch_step: null engine");
+        e->impl->step(tokens, next_out, logits_out);
+    });
+}
+
+int cudallm_batch_synchronize(cudallm_batch* e) {
+    return guarded([&] {
+        require(e && e->impl, "cudallm_batch_synchronize: null engine");
+        e->impl->synchronize();
+    });
+}
+
+void* cudallm_batch_stream(cudallm_batch* e) {
+    if (!e || !e->impl) {
+        set_error("cudallm_batch_stream: null engine");
+        return nullptr;
+    }
+    return static_cast<void*>(e->impl->stream());
+}
+
+int cudallm_kernel_gemm(const unsigned short* w, const unsigned short* x, const unsigned short* x_lo, float* y, int n, int k,
+                        int batch, int ksplit, int epilogue) {
     return guarded([&] {
         require(w && x && y, "cudallm_kernel_gemm: null argument");
-        require(n > 0 && k > 0 && batch >= 1 && batch <= cudallm::kBatchMax && ksplit >= 1 && k % (64 * ksplit) == 0,
-                "cudallm_kernel_gemm: bad shape (batch 1..64, k a multiple of 64 * ksplit)");
+        require(n > 0 && k >= 64 && k % 64 == 0 && batch >= 1 && batch <= cudallm::kBatchMax && ksplit >= 1 && ksplit <= k / 64,
+                "cudallm_kernel_gemm: bad shape (batch 1..64, k a multiple of 64, ksplit <= k / 64)");
         require(epilogue >= 0 && epilogue <= 2 && (epilogue != 2 || n % 2 == 0), "cudallm_kernel_gemm: bad epilogue");
         const size_t wb = static_cast<size_t>(n) * k * 2, xb = static_cast<size_t>(batch) * k * 2;
+        const size_t plane = static_cast<size_t>(cudallm::kBatchMax) * k * 2;
         const int n_out = epilogue == 2 ? n / 2 : n;
         const size_t yb = static_cast<size_t>(batch) * n_out * sizeof(float);
-        DevBuf dw(wb), dx(xb), dpart(static_cast<size_t>(ksplit) * batch * n * sizeof(float)), dy(yb), derr(sizeof(unsigned));
+        DevBuf dw(wb), dx(2 * plane), dpart(static_cast<size_t>(ksplit) * batch * n * sizeof(float)), dy(yb),
+            derr(sizeof(unsigned));
         dw.upload(w, wb);
-        dx.upload(x, xb);
+        // Activation planes [2][64][k]: x in the hi plane, x_lo (or zeros) in the lo plane, unused rows zero.
+        CLLM_CUDA(cudaMemset(dx.as<void>(), 0, 2 * plane));
+        CLLM_CUDA(cudaMemcpy(dx.as<void>(), x, xb, cudaMemcpyHostToDevice));
+        if (x_lo) CLLM_CUDA(cudaMemcpy(dx.as<uint8_t>() + plane, x_lo, xb, cudaMemcpyHostToDevice));
         dy.upload(y, yb);  // ADD accumulates into y
         CLLM_CUDA(cudaMemset(derr.as<void>(), 0, sizeof(unsigned)));
         cudallm::launch_gemm_bf16(dw.as<__nv_bfloat16>(), n, k, dx.as<__nv_bfloat16>(), batch, ksplit, dpart.as<float>(),

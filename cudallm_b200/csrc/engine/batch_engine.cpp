@@ -1,0 +1,279 @@
+#include "engine/batch_engine.h"
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstdlib>
+#include <string>
+
+#include "common/check.h"
+#include "common/device.h"
+#include "kernels/batch.h"
+#include "kernels/batch_ops.h"
+#include "kernels/kernels.h"
+
+namespace cudallm {
+
+namespace {
+
+template <typename T>
+void alloc_zero(T** p, size_t count) {
+    CLLM_CUDA(cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T)));
+    CLLM_CUDA(cudaMemset(*p, 0, count * sizeof(T)));
+}
+
+// The attention grid of a captured step covers whole groups of this many 64-token tiles, so a graph is
+// captured again only when the longest context crosses a group boundary (every 256 tokens); tiles past a
+// row's context return at once.
+constexpr int kTileGroup = 4;
+
+// K split of a GEMM with `mtiles` 128-row tiles and `chunks` 64-column K chunks: as many grid rows as keep
+// every SM busy with one CTA.
+int pick_ksplit(int mtiles, int chunks, int sms) { return std::max(1, std::min(chunks, sms / std::max(1, mtiles))); }
+
+}  // namespace
+
+BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : opts_(opts) {
+    const ParsedFile file = parse_cudallm(path);
+    if (opts_.n_seq < 1 || opts_.n_seq > kBatchMax) throw ArgError("n_seq must be 1..64");
+    if (opts_.max_seq_len < 0 || opts_.max_seq_len % 128 != 0) {
+        throw ArgError("max_seq_len must be 0 or a positive multiple of 128");
+    }
+    if (opts_.max_seq_len > file.config.max_seq_len) throw ArgError("max_seq_len exceeds the file's max_seq_len");
+    if (opts_.kv != KvType::F16 && opts_.kv != KvType::BF16) throw ArgError("kv_dtype must be 0 (fp16) or 1 (bf16)");
+    if (file.config.wtype != WeightType::BF16) {
+        throw ArgError(std::string("batched decode supports bf16 weights; the file holds ") + to_string(file.config.wtype));
+    }
+    if (opts_.device >= 0) {
+        int n = 0;
+        CLLM_CUDA(cudaGetDeviceCount(&n));
+        if (opts_.device >= n) throw ArgError("device ordinal out of range");
+        device_ = opts_.device;
+    } else {
+        CLLM_CUDA(cudaGetDevice(&device_));
+    }
+    DeviceGuard guard(device_);
+    weights_ = std::make_unique<Weights>(file);
+    const ModelConfig& c = weights_->config();
+    max_seq_ = opts_.max_seq_len ? opts_.max_seq_len : c.max_seq_len;
+    host_pos_.assign(opts_.n_seq, 0);
+    if (const char* env = std::getenv("CUDALLM_BATCH_PDL")) opts_.pdl = std::atoi(env) != 0;
+    try {
+        CLLM_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
+        int sms = 0;
+        CLLM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_));
+        const int H = c.hidden, I = c.inter, V = c.vocab, NH = c.n_heads, NKV = c.n_kv_heads, D = c.head_dim;
+        const int QKV = (NH + 2 * NKV) * D;
+        auto mt = [](int n) { return (n + 127) / 128; };
+        ks_qkv_ = pick_ksplit(mt(QKV), H / 64, sms);
+        ks_wo_ = pick_ksplit(mt(H), H / 64, sms);
+        ks_gu_ = pick_ksplit(mt(2 * I), H / 64, sms);
+        ks_down_ = pick_ksplit(mt(H), I / 64, sms);
+        const size_t B = kBatchMax;
+        part_floats_ = std::max({static_cast<size_t>(ks_qkv_) * B * QKV, static_cast<size_t>(ks_wo_) * B * H,
+                                 static_cast<size_t>(ks_gu_) * B * 2 * I, static_cast<size_t>(ks_down_) * B * H,
+                                 B * static_cast<size_t>(V)});
+        alloc_zero(&x_, B * H);
+        alloc_zero(reinterpret_cast<__nv_bfloat16**>(&xn_), 2 * B * std::max(H, NH * D));
+        alloc_zero(reinterpret_cast<__nv_bfloat16**>(&act_), 2 * B * I);
+        alloc_zero(&qkv_, B * QKV);
+        alloc_zero(&part_, part_floats_);
+        const size_t cache_elems = static_cast<size_t>(opts_.n_seq) * c.n_layers * NKV * max_seq_ * D;
+        CLLM_CUDA(cudaMalloc(&k_cache_, cache_elems * 2));
+        CLLM_CUDA(cudaMalloc(&v_cache_, cache_elems * 2));
+        CLLM_CUDA(cudaMemset(k_cache_, 0, cache_elems * 2));
+        CLLM_CUDA(cudaMemset(v_cache_, 0, cache_elems * 2));
+        const size_t slots = static_cast<size_t>(max_seq_ / kAttnTile);
+        alloc_zero(&att_o_, B * NH * slots * D);
+        alloc_zero(&att_ml_, B * NH * slots * 2);
+        alloc_zero(&tok_in_, B);
+        alloc_zero(&tok_, B);
+        alloc_zero(&dpos_, B);
+        alloc_zero(&err_, 1);
+        CLLM_CUDA(cudaMemset(tok_in_, 0xff, B * sizeof(int)));  // -1: feed the previous argmax
+        CLLM_CUDA(cudaDeviceSynchronize());
+    } catch (...) {
+        free_all();
+        throw;
+    }
+}
+
+void BatchEngine::free_all() noexcept {
+    auto report = [](cudaError_t err, const char* what) {
+        if (err != cudaSuccess) std::fprintf(stderr, "cudallm: %s failed in ~BatchEngine: %s\n", what, cudaGetErrorString(err));
+    };
+    if (graph_exec_) report(cudaGraphExecDestroy(graph_exec_), "cudaGraphExecDestroy");
+    if (graph_) report(cudaGraphDestroy(graph_), "cudaGraphDestroy");
+    graph_exec_ = nullptr;
+    graph_ = nullptr;
+    void* bufs[] = {x_, xn_, act_, qkv_, part_, k_cache_, v_cache_, att_o_, att_ml_, tok_in_, tok_, dpos_, err_};
+    for (void* b : bufs) {
+        if (b) report(cudaFree(b), "cudaFree");
+    }
+    x_ = qkv_ = part_ = att_o_ = att_ml_ = nullptr;
+    xn_ = act_ = k_cache_ = v_cache_ = nullptr;
+    tok_in_ = tok_ = dpos_ = nullptr;
+    err_ = nullptr;
+    if (stream_) report(cudaStreamDestroy(stream_), "cudaStreamDestroy");
+    stream_ = nullptr;
+}
+
+BatchEngine::~BatchEngine() {
+    try {
+        DeviceGuard guard(device_);
+        if (stream_) cudaStreamSynchronize(stream_);
+        free_all();
+        weights_.reset();
+    } catch (const std::exception& ex) {
+        std::fprintf(stderr, "cudallm: exception in ~BatchEngine: %s\n", ex.what());
+    } catch (...) {
+        std::fprintf(stderr, "cudallm: unknown exception in ~BatchEngine\n");
+    }
+}
+
+int BatchEngine::pos(int seq) const {
+    if (seq < 0 || seq >= opts_.n_seq) throw ArgError("pos: sequence index out of range");
+    return host_pos_[seq];
+}
+
+void BatchEngine::synchronize() {
+    DeviceGuard guard(device_);
+    CLLM_CUDA(cudaStreamSynchronize(stream_));
+    unsigned err = 0;
+    CLLM_CUDA(cudaMemcpy(&err, err_, sizeof(err), cudaMemcpyDeviceToHost));
+    if (err != 0) {
+        CLLM_CUDA(cudaMemset(err_, 0, sizeof(unsigned)));
+        throw StateError("device: a bounded wait in a batched GEMM gave up; the step's results are invalid");
+    }
+}
+
+void BatchEngine::reset(int seq) {
+    if (seq < -1 || seq >= opts_.n_seq) throw ArgError("reset: sequence index out of range");
+    synchronize();
+    DeviceGuard guard(device_);
+    if (seq < 0) {
+        CLLM_CUDA(cudaMemsetAsync(dpos_, 0, sizeof(int) * kBatchMax, stream_));
+        std::fill(host_pos_.begin(), host_pos_.end(), 0);
+    } else {
+        CLLM_CUDA(cudaMemsetAsync(dpos_ + seq, 0, sizeof(int), stream_));
+        host_pos_[seq] = 0;
+    }
+    CLLM_CUDA(cudaStreamSynchronize(stream_));
+}
+
+// Per row, the operation sequence of wasiqnauman/cudallm src/engine/engine.cpp:181-237 (unfused form:
+// RMSNorm, QKV, RoPE + KV write, attention, o_proj + residual, RMSNorm, gate/up + SwiGLU, down + residual;
+// final RMSNorm, tied lm_head, argmax), with the matvecs as batched GEMMs.
+template <typename KV>
+void BatchEngine::enqueue_layers(int tiles) {
+    const ModelConfig& c = config();
+    const Weights& W = *weights_;
+    const int B = opts_.n_seq, H = c.hidden, I = c.inter, V = c.vocab, NH = c.n_heads, NKV = c.n_kv_heads, D = c.head_dim;
+    const int QKV = (NH + 2 * NKV) * D;
+    const size_t layer_elems = static_cast<size_t>(NKV) * max_seq_ * D;
+    const size_t seq_stride = layer_elems * c.n_layers;
+    KV* kc = static_cast<KV*>(k_cache_);
+    KV* vc = static_cast<KV*>(v_cache_);
+    auto* xn = static_cast<__nv_bfloat16*>(xn_);
+    auto* act = static_cast<__nv_bfloat16*>(act_);
+    auto bf = [](const Linear& L) { return static_cast<const __nv_bfloat16*>(L.w); };
+    const bool pdl = opts_.pdl;
+    cudaStream_t s = stream_;
+    launch_embed_rows(static_cast<const uint16_t*>(W.tok_embeddings.w), tok_in_, tok_, x_, B, H, s, pdl);
+    for (int l = 0; l < c.n_layers; ++l) {
+        const LayerWeights& L = W.layers[l];
+        KV* kl = kc + l * layer_elems;
+        KV* vl = vc + l * layer_elems;
+        launch_rmsnorm_rows(x_, L.attn_norm, c.rms_eps, xn, B, H, s, pdl);
+        launch_gemm_bf16(bf(L.wqkv), QKV, H, xn, B, ks_qkv_, part_, err_, s, pdl);
+        launch_gemm_reduce(part_, ks_qkv_, B, QKV, GemmEpilogue::STORE, qkv_, nullptr, s, pdl);
+        launch_rope_kv_rows<KV>(qkv_, W.rope_inv_freq, kl, vl, seq_stride, dpos_, B, NH, NKV, D, max_seq_, s, pdl);
+        launch_attention_rows<KV>(qkv_, kl, vl, seq_stride, dpos_, tiles * kAttnTile, att_o_, att_ml_, xn, B, NH, NKV, max_seq_,
+                                  s, pdl);
+        launch_gemm_bf16(bf(L.wo), H, NH * D, xn, B, ks_wo_, part_, err_, s, pdl);
+        launch_gemm_reduce(part_, ks_wo_, B, H, GemmEpilogue::ADD, x_, nullptr, s, pdl);
+        launch_rmsnorm_rows(x_, L.ffn_norm, c.rms_eps, xn, B, H, s, pdl);
+        launch_gemm_bf16(bf(L.w_gate_up), 2 * I, H, xn, B, ks_gu_, part_, err_, s, pdl);
+        launch_gemm_reduce(part_, ks_gu_, B, 2 * I, GemmEpilogue::SWIGLU, nullptr, act, s, pdl);
+        launch_gemm_bf16(bf(L.w_down), H, I, act, B, ks_down_, part_, err_, s, pdl);
+        launch_gemm_reduce(part_, ks_down_, B, H, GemmEpilogue::ADD, x_, nullptr, s, pdl);
+    }
+    launch_rmsnorm_rows(x_, W.final_norm, c.rms_eps, xn, B, H, s, pdl);
+    launch_gemm_bf16(bf(W.tok_embeddings), V, H, xn, B, 1, part_, err_, s, pdl);  // logits = part_ [B][V]
+    launch_argmax_rows(part_, V, tok_, dpos_, B, s, pdl);
+}
+
+void BatchEngine::enqueue_step(int tiles) {
+    if (opts_.kv == KvType::F16) {
+        enqueue_layers<__half>(tiles);
+    } else {
+        enqueue_layers<__nv_bfloat16>(tiles);
+    }
+}
+
+void BatchEngine::step(const int* tokens, int* next_out, float* logits_out) {
+    const int B = opts_.n_seq;
+    int longest = 0;
+    for (int b = 0; b < B; ++b) {
+        if (host_pos_[b] >= max_seq_) {
+            throw StateError("step: sequence " + std::to_string(b) + " is full (pos == max_seq_len); reset it");
+        }
+        longest = std::max(longest, host_pos_[b] + 1);
+        if (tokens && (tokens[b] < -1 || tokens[b] >= config().vocab)) throw ArgError("step: token out of range");
+    }
+    DeviceGuard guard(device_);
+    // The caller's tokens go to the device through the driver's staging copy (the host array may be reused
+    // as soon as this returns); without tokens every row feeds its previous argmax.
+    if (tokens) {
+        CLLM_CUDA(cudaMemcpyAsync(tok_in_, tokens, sizeof(int) * B, cudaMemcpyHostToDevice, stream_));
+        tok_in_fed_ = true;
+    } else if (tok_in_fed_) {
+        CLLM_CUDA(cudaMemsetAsync(tok_in_, 0xff, sizeof(int) * B, stream_));
+        tok_in_fed_ = false;
+    }
+    const int max_tiles = max_seq_ / kAttnTile;
+    const int tiles = std::min(max_tiles, (longest + kAttnTile * kTileGroup - 1) / (kAttnTile * kTileGroup) * kTileGroup);
+    if (opts_.cuda_graph) {
+        if (!graph_exec_ || graph_tiles_ != tiles) {
+            cudaGraph_t g = nullptr;
+            CLLM_CUDA(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal));
+            try {
+                enqueue_step(tiles);
+            } catch (...) {
+                cudaGraph_t broken = nullptr;
+                cudaStreamEndCapture(stream_, &broken);
+                if (broken) cudaGraphDestroy(broken);
+                throw;
+            }
+            CLLM_CUDA(cudaStreamEndCapture(stream_, &g));
+            bool updated = false;
+            if (graph_exec_) {
+                cudaGraphExecUpdateResultInfo info{};
+                updated = cudaGraphExecUpdate(graph_exec_, g, &info) == cudaSuccess;
+                if (!updated) {
+                    cudaGetLastError();  // clear the failed update's error
+                    CLLM_CUDA(cudaGraphExecDestroy(graph_exec_));
+                    graph_exec_ = nullptr;
+                }
+            }
+            if (!updated) CLLM_CUDA(cudaGraphInstantiate(&graph_exec_, g, 0));
+            if (graph_) CLLM_CUDA(cudaGraphDestroy(graph_));
+            graph_ = g;
+            graph_tiles_ = tiles;
+        }
+        CLLM_CUDA(cudaGraphLaunch(graph_exec_, stream_));
+    } else {
+        enqueue_step(tiles);
+    }
+    for (int b = 0; b < B; ++b) host_pos_[b] += 1;
+    if (!next_out && !logits_out) return;
+    if (logits_out) {
+        CLLM_CUDA(cudaMemcpyAsync(logits_out, part_, sizeof(float) * B * config().vocab, cudaMemcpyDeviceToHost, stream_));
+    }
+    if (next_out) CLLM_CUDA(cudaMemcpyAsync(next_out, tok_, sizeof(int) * B, cudaMemcpyDeviceToHost, stream_));
+    synchronize();
+}
+
+}  // namespace cudallm

@@ -1,0 +1,92 @@
+// Batched decode engine: up to 64 independent sequences decoded together, one token each per step, on
+// one GPU. No counterpart in wasiqnauman/cudallm (its engine, src/engine/engine.h:15-65, holds one
+// sequence); each row of the batch follows that engine's per-token operation sequence
+// (src/engine/engine.cpp:181-237) on its own token, position and KV cache, so a row's logits match what
+// the batch-1 engine computes for that sequence up to fp32 summation order. The weight matvecs become
+// GEMMs on the tcgen05 tensor cores (every weight byte is read once per step for the whole batch);
+// RoPE, attention, RMSNorm and argmax run per row. Several GPUs run one engine each on their own
+// sequence groups (no collective).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "common/dtype.h"
+#include "model/weights.h"
+
+namespace cudallm {
+
+struct BatchOptions {
+    int n_seq = 64;       // 1..64 sequences
+    int max_seq_len = 0;  // 0 = the file header's value, else a positive multiple of 128 not above it
+    KvType kv = KvType::F16;
+    int device = -1;         // -1 = current device
+    bool cuda_graph = true;  // replay the step as a CUDA graph
+    bool pdl = true;         // programmatic dependent launch between the step's kernels
+};
+
+class BatchEngine {
+public:
+    BatchEngine(const std::string& path, const BatchOptions& opts);
+    ~BatchEngine();
+    BatchEngine(const BatchEngine&) = delete;
+    BatchEngine& operator=(const BatchEngine&) = delete;
+
+    const ModelConfig& config() const { return weights_->config(); }
+    const BatchOptions& options() const { return opts_; }
+    uint64_t weight_bytes() const { return weights_->total_tensor_bytes(); }
+    int n_seq() const { return opts_.n_seq; }
+    int max_seq() const { return max_seq_; }
+    int pos(int seq) const;
+    int device() const { return device_; }
+    cudaStream_t stream() const { return stream_; }
+
+    // seq in [0, n_seq): that sequence's position back to 0; -1: every sequence.
+    void reset(int seq);
+    // tokens: host [n_seq], tokens[b] >= 0 is fed to sequence b, -1 feeds b's previous argmax; null = all
+    // -1. next_out: host [n_seq] or null; logits_out: host [n_seq][vocab] or null. With both outputs null
+    // the call does not synchronise.
+    void step(const int* tokens, int* next_out, float* logits_out);
+    // Waits for queued steps and reports a device-side failure (a timed-out wait in a GEMM).
+    void synchronize();
+
+private:
+    template <typename KV>
+    void enqueue_layers(int tiles);  // tiles: 64-token attention tiles the grid covers
+    void enqueue_step(int tiles);
+    void free_all() noexcept;
+
+    std::unique_ptr<Weights> weights_;
+    BatchOptions opts_;
+    int device_ = 0;
+    int max_seq_ = 0;
+    std::vector<int> host_pos_;
+    cudaStream_t stream_ = nullptr;
+    cudaGraph_t graph_ = nullptr;
+    cudaGraphExec_t graph_exec_ = nullptr;
+    int graph_tiles_ = 0;  // attention tiles the captured graph covers
+
+    // Per-operation K splits (grid rows of the GEMM), chosen to fill the SMs.
+    int ks_qkv_ = 1, ks_wo_ = 1, ks_gu_ = 1, ks_down_ = 1;
+
+    float* x_ = nullptr;              // residual stream [64][hidden] fp32
+    void* xn_ = nullptr;              // activation planes [2][64][hidden] bf16 (normed x, attention output)
+    void* act_ = nullptr;             // activation planes [2][64][inter] bf16 (SwiGLU output)
+    float* qkv_ = nullptr;            // [64][qkv rows]
+    float* part_ = nullptr;           // GEMM partials; the lm_head's logits [64][vocab]
+    void* k_cache_ = nullptr;         // [seq][layer][kv head][max_seq][64]
+    void* v_cache_ = nullptr;
+    float* att_o_ = nullptr;          // attention partials [64][heads][max_seq/64][64]
+    float* att_ml_ = nullptr;         // [64][heads][max_seq/64][2]
+    int* tok_in_ = nullptr;           // device copy of the step's fed tokens
+    int* tok_ = nullptr;              // [64] last argmax per sequence
+    int* dpos_ = nullptr;             // [64] position per sequence
+    unsigned* err_ = nullptr;         // device error word
+    bool tok_in_fed_ = false;         // tok_in_ holds fed tokens (not all -1)
+    size_t part_floats_ = 0;
+};
+
+}  // namespace cudallm

@@ -9,6 +9,7 @@
 #include <string>
 
 #include "common/check.h"
+#include "common/device.h"
 
 namespace cudallm {
 
@@ -32,23 +33,6 @@ void validate(const EngineOptions& o, WeightType wt) {
 }
 
 namespace {
-
-// Makes the engine's device current for the lifetime of the guard.
-class DeviceGuard {
-public:
-    explicit DeviceGuard(int dev) {
-        CLLM_CUDA(cudaGetDevice(&prev_));
-        if (dev != prev_) CLLM_CUDA(cudaSetDevice(dev));
-        set_ = dev != prev_;
-    }
-    ~DeviceGuard() {
-        if (set_) cudaSetDevice(prev_);
-    }
-
-private:
-    int prev_ = 0;
-    bool set_ = false;
-};
 
 template <typename T>
 void alloc(T** p, size_t count) {

@@ -1,0 +1,36 @@
+// Per-row kernels of the batched decode step (kernels/batch_ops.cu): row b = sequence b. GEMM operands are
+// written as activation planes [2][kBatchMax][n] bf16 (hi, lo; see launch_gemm_bf16). pdl: launch with the
+// programmatic-dependent-launch attribute (every kernel here waits for its predecessor before reading).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace cudallm {
+
+// Row b's token t = tok_in[b] when >= 0, else tok[b] (the previous argmax); x[b][:] = embedding row t
+// (bf16 weights).
+void launch_embed_rows(const uint16_t* emb, const int* tok_in, const int* tok, float* x, int batch, int hidden,
+                       cudaStream_t stream, bool pdl = false);
+// out planes of rmsnorm(x[b][:]) * w.
+void launch_rmsnorm_rows(const float* x, const float* w, float eps, __nv_bfloat16* out, int batch, int n, cudaStream_t stream,
+                         bool pdl = false);
+// Rotates the q heads of every row in place and writes the rotated k and the v of row b into sequence b's
+// cache ([nkv][max_seq][hd] at k_cache + b * seq_stride) at position pos[b].
+template <typename KV>
+void launch_rope_kv_rows(float* qkv, const float* inv_freq, KV* k_cache, KV* v_cache, size_t seq_stride, const int* pos,
+                         int batch, int nh, int nkv, int hd, int max_seq, cudaStream_t stream, bool pdl = false);
+// Split-K GQA attention of every row over its own context (pos[b] + 1 tokens; max_ctx >= the largest sets
+// the grid): out = attention output planes [2][kBatchMax][nh * 64]. Partials: [batch][nh][max_seq/64][64]
+// and [...][2].
+template <typename KV>
+void launch_attention_rows(const float* qkv, const KV* k_cache, const KV* v_cache, size_t seq_stride, const int* pos,
+                           int max_ctx, float* part_o, float* part_ml, __nv_bfloat16* out, int batch, int nh, int nkv,
+                           int max_seq, cudaStream_t stream, bool pdl = false);
+// tok[b] = argmax of logits row b (lowest index on ties), pos[b] += 1.
+void launch_argmax_rows(const float* logits, int n, int* tok, int* pos, int batch, cudaStream_t stream, bool pdl = false);
+
+}  // namespace cudallm

@@ -1,12 +1,16 @@
 // Batched decode GEMM on the sm_100a tensor cores: part[ks][b][n] = sum over the ks-th K range of
 // X[b][k] * W[n][k], W the [N][K] bf16 weight matrix (row-major, as stored in the .cudallm file), X the
-// [batch][K] bf16 activations (batch <= 64). Weight rows are the MMA's M side: a CTA computes 128 weight
-// rows x 64 batch columns (tcgen05.mma.cta_group::1.kind::f16, M = 128, N = 64, K = 16 per instruction)
-// into a 64-column fp32 TMEM accumulator, so every weight element is read from HBM exactly once per step
-// and used for the whole batch. Operands arrive by 2D TMA tensor loads (128-byte swizzle, no multicast)
-// through an 8-stage ring of (W 128 x 64, X 64 x 64) tiles; one thread issues the loads, one thread the
-// MMAs, and the 4 warps read the accumulator back (warp w owns TMEM lanes 32w..32w+31). A K range per
-// grid row (blockIdx.y) spreads short operations over the SMs; gemm_reduce adds the ranges in order.
+// fp32 activations of up to 64 sequences carried as two bf16 planes, X = hi + lo (hi = bf16(X), lo =
+// bf16(X - hi)), so the product keeps ~16 mantissa bits of the fp32 activation, like the batch-1 path's
+// fp32 vectors. Weight rows are the MMA's M side: a CTA computes 128 weight rows x 64 batch columns
+// (tcgen05.mma.cta_group::1.kind::f16, M = 128, N = 64, K = 16 per instruction; one MMA per plane into the
+// same accumulator) in a 64-column fp32 TMEM accumulator, so every weight element is read from HBM once
+// per step and used for the whole batch. Operands arrive by 2D TMA tensor loads (128-byte swizzle, no
+// multicast) through a 7-stage ring of (W 128 x 64, X 2 x 64 x 64) tiles; one thread issues the loads,
+// one thread the MMAs, and the 4 warps read the accumulator back (warp w owns TMEM lanes 32w..32w+31).
+// K ranges per grid row (blockIdx.y) spread short operations over the SMs; gemm_reduce adds the ranges in
+// order. The kernels take part in programmatic dependent launch: a GEMM starts streaming its weights
+// while the kernel before it finishes and waits for it only before loading the activations.
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -20,25 +24,28 @@
 
 #include "common/check.h"
 #include "kernels/batch.h"
+#include "kernels/launch.cuh"
 #include "kernels/tcgen05.cuh"
 
 namespace cudallm {
 namespace {
 
-constexpr int kGM = 128;  // weight rows per CTA (MMA M)
-constexpr int kGN = 64;   // batch columns (MMA N)
-constexpr int kGK = 64;   // K per stage: one 128-byte swizzled row
-constexpr int kGStages = 8;
+constexpr int kGM = 128;            // weight rows per CTA (MMA M)
+constexpr int kGN = kBatchMax;      // batch columns (MMA N)
+constexpr int kGK = 64;             // K per stage: one 128-byte swizzled row
+constexpr int kXRows = 2 * kGN;     // hi plane rows 0..63, lo plane rows 64..127
+constexpr int kGStages = 7;
 constexpr int kGThreads = 128;
-constexpr int kWTileBytes = kGM * kGK * 2;  // 16 KiB
-constexpr int kXTileBytes = kGN * kGK * 2;  // 8 KiB
+constexpr int kWTileBytes = kGM * kGK * 2;     // 16 KiB
+constexpr int kXTileBytes = kXRows * kGK * 2;  // 16 KiB
+constexpr int kXPlaneBytes = kGN * kGK * 2;    // lo plane offset inside an X tile (1024-byte aligned)
 constexpr int kGSmemBytes = 1024 + kGStages * (kWTileBytes + kXTileBytes) + 256;
 constexpr uint64_t kGemmWaitNs = 1000000000ull;
 
 struct GemmArgs {
-    float* part;  // [ksplit][batch][n]
-    int n, k, batch, kchunks;  // kchunks: 64-column K chunks per grid row
-    unsigned* err;             // error word (set on a wait timeout)
+    float* part;                // [ksplit][batch][n]
+    int n, batch, chunks, ksplit;  // chunks: 64-column K chunks in total
+    unsigned* err;              // error word (set on a wait timeout)
 };
 
 // Bounded wait on an mbarrier phase; false (and the error word set) after kGemmWaitNs.
@@ -70,7 +77,11 @@ __global__ void __launch_bounds__(kGThreads, 1)
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n0 = blockIdx.x * kGM;
-    const int kc0 = blockIdx.y * a.kchunks;
+    // This grid row's K chunks: [c0, c1), an even split of the chunks over the ksplit rows.
+    const int c0 = static_cast<int>(static_cast<long long>(blockIdx.y) * a.chunks / a.ksplit);
+    const int c1 = static_cast<int>(static_cast<long long>(blockIdx.y + 1) * a.chunks / a.ksplit);
+    const int nch = c1 - c0;
+    grid_dep_launch();
     if (threadIdx.x == 0) {
         for (int s = 0; s < kGStages; ++s) {
             mbar_init(&full[s], 1);
@@ -88,15 +99,23 @@ __global__ void __launch_bounds__(kGThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0 && lane == 0) {
-        // TMA producer: chunk i of this CTA's K range into stage i % kGStages.
+        // TMA producer: chunk i of this CTA's K range into stage i % kGStages. The weight tiles of the
+        // first ring pass do not depend on the previous kernel and are issued before waiting for it.
         const uint64_t pol = l2_policy_evict_first();
-        int issued = 0;
-        for (int i = 0; i < a.kchunks; ++i) {
+        const int pre = nch < kGStages ? nch : kGStages;
+        for (int i = 0; i < pre; ++i) {
+            mbar_arrive_expect_tx(&full[i], kWTileBytes + kXTileBytes);
+            tma_load_2d_hint(wt + i * kWTileBytes, &wmap, (c0 + i) * kGK, n0, &full[i], pol);
+        }
+        grid_dep_wait();
+        for (int i = 0; i < pre; ++i) tma_load_2d(xt + i * kXTileBytes, &xmap, (c0 + i) * kGK, 0, &full[i]);
+        int issued = pre;
+        for (int i = pre; i < nch; ++i) {
             const int s = i % kGStages;
-            if (i >= kGStages && !gemm_wait(&empty[s], ((i / kGStages) - 1) & 1, a.err)) break;
+            if (!gemm_wait(&empty[s], ((i / kGStages) - 1) & 1, a.err)) break;
             mbar_arrive_expect_tx(&full[s], kWTileBytes + kXTileBytes);
-            tma_load_2d_hint(wt + s * kWTileBytes, &wmap, (kc0 + i) * kGK, n0, &full[s], pol);
-            tma_load_2d(xt + s * kXTileBytes, &xmap, (kc0 + i) * kGK, 0, &full[s]);
+            tma_load_2d_hint(wt + s * kWTileBytes, &wmap, (c0 + i) * kGK, n0, &full[s], pol);
+            tma_load_2d(xt + s * kXTileBytes, &xmap, (c0 + i) * kGK, 0, &full[s]);
             issued = i + 1;
         }
         // Every load issued lands before the CTA may exit (the MMA thread consumes them; this only
@@ -105,24 +124,29 @@ __global__ void __launch_bounds__(kGThreads, 1)
             gemm_wait(&full[i % kGStages], (i / kGStages) & 1, a.err);
         }
     } else if (warp == 1 && lane == 0) {
-        // MMA issuer: 4 MMAs (K = 16 each, +32 bytes inside the swizzled 128-byte rows) per stage.
+        // MMA issuer: per stage, 4 K steps of 16 (+32 bytes inside the swizzled 128-byte rows), each one
+        // MMA with the hi plane and one with the lo plane into the same accumulator.
         constexpr uint32_t idesc = idesc_bf16_f32(kGM, kGN);
-        for (int i = 0; i < a.kchunks; ++i) {
+        for (int i = 0; i < nch; ++i) {
             const int s = i % kGStages;
             if (!gemm_wait(&full[s], (i / kGStages) & 1, a.err)) break;
             tc_fence_after();
             const uint64_t ad = smem_desc_sw128(smem_addr(wt + s * kWTileBytes));
-            const uint64_t bd = smem_desc_sw128(smem_addr(xt + s * kXTileBytes));
+            const uint64_t bh = smem_desc_sw128(smem_addr(xt + s * kXTileBytes));
+            const uint64_t bl = smem_desc_sw128(smem_addr(xt + s * kXTileBytes + kXPlaneBytes));
 #pragma unroll
             for (int kk = 0; kk < kGK / 16; ++kk) {
-                mma_f16(tmem, ad + 2u * kk, bd + 2u * kk, idesc, i > 0 || kk > 0);
+                mma_f16(tmem, ad + 2u * kk, bh + 2u * kk, idesc, i > 0 || kk > 0);
+                mma_f16(tmem, ad + 2u * kk, bl + 2u * kk, idesc, true);
             }
             mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
         }
         mma_commit(done);
     }
     __syncwarp();
-    // Epilogue: TMEM lane m = weight row n0 + m, column b = batch row b.
+    // Epilogue: TMEM lane m = weight row n0 + m, column b = batch row b. The partials buffer may still be
+    // read by the kernel before this one until it has completed.
+    grid_dep_wait();
     if (lane == 0) gemm_wait(done, 0, a.err);
     __syncwarp();
     tc_fence_after();
@@ -189,11 +213,14 @@ const CUtensorMap* tensor_map(const void* base, int rows, int cols, int box_rows
 __device__ __forceinline__ float silu_g(float x) { return x / (1.f + __expf(-x)); }
 
 // out[b][j] from sum over ks of part[ks][b][j] (added in ks order): STORE / ADD (residual) / SWIGLU
-// (j < n/2: silu(s[j]) * s[n/2 + j]); outb (optional) gets the bf16 copy of what out receives.
+// (j < n/2: silu(s[j]) * s[n/2 + j]); outb (optional) gets the value as hi/lo bf16 planes.
 __global__ void gemm_reduce_kernel(const float* __restrict__ part, int ksplit, int batch, int n, int ep, float* out,
                                    __nv_bfloat16* outb) {
+    grid_dep_launch();
+    grid_dep_wait();
     const int n_out = ep == static_cast<int>(GemmEpilogue::SWIGLU) ? n / 2 : n;
     const size_t total = static_cast<size_t>(batch) * n_out;
+    const size_t plane = static_cast<size_t>(kBatchMax) * n_out;
     for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
          idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
         const int b = static_cast<int>(idx / n_out), j = static_cast<int>(idx % n_out);
@@ -212,7 +239,11 @@ __global__ void gemm_reduce_kernel(const float* __restrict__ part, int ksplit, i
             v = ep == static_cast<int>(GemmEpilogue::ADD) ? out[idx] + s : s;
         }
         if (out) out[idx] = v;
-        if (outb) outb[idx] = __float2bfloat16_rn(v);
+        if (outb) {
+            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+            outb[idx] = hi;
+            outb[plane + idx] = __float2bfloat16_rn(v - __bfloat162float(hi));
+        }
     }
 }
 
@@ -221,10 +252,11 @@ __global__ void gemm_reduce_kernel(const float* __restrict__ part, int ksplit, i
 int gemm_smem_bytes() { return kGSmemBytes; }
 
 void launch_gemm_bf16(const __nv_bfloat16* w, int n, int k, const __nv_bfloat16* x, int batch, int ksplit, float* part,
-                      unsigned* err, cudaStream_t stream) {
+                      unsigned* err, cudaStream_t stream, bool pdl) {
     CLLM_CHECK(w && x && part && err, "launch_gemm_bf16: null pointer");
     CLLM_CHECK(batch >= 1 && batch <= kGN, "launch_gemm_bf16: batch must be 1..64");
-    CLLM_CHECK(n >= 1 && ksplit >= 1 && k % (kGK * ksplit) == 0, "launch_gemm_bf16: k must be a multiple of 64 * ksplit");
+    CLLM_CHECK(n >= 1 && k >= kGK && k % kGK == 0 && ksplit >= 1 && ksplit <= k / kGK,
+               "launch_gemm_bf16: k must be a multiple of 64 with at least ksplit 64-column chunks");
     CLLM_CHECK((reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
                "launch_gemm_bf16: operands must be 16-byte aligned");
     static bool configured[64] = {};
@@ -235,21 +267,21 @@ void launch_gemm_bf16(const __nv_bfloat16* w, int n, int k, const __nv_bfloat16*
         if (dev < 64) configured[dev] = true;
     }
     const CUtensorMap* wm = tensor_map(w, n, k, kGM);
-    const CUtensorMap* xm = tensor_map(x, batch, k, kGN);
-    GemmArgs a{part, n, k, batch, k / kGK / ksplit, err};
-    const dim3 grid((n + kGM - 1) / kGM, ksplit);
-    gemm_bf16_kernel<<<grid, kGThreads, kGSmemBytes, stream>>>(*wm, *xm, a);
-    CLLM_CUDA(cudaGetLastError());
+    const CUtensorMap* xm = tensor_map(x, kXRows, k, kXRows);
+    GemmArgs a{part, n, batch, k / kGK, ksplit, err};
+    launch_kernel(gemm_bf16_kernel, dim3((n + kGM - 1) / kGM, ksplit), dim3(kGThreads), kGSmemBytes, stream, pdl, *wm, *xm,
+                  a);
 }
 
 void launch_gemm_reduce(const float* part, int ksplit, int batch, int n, GemmEpilogue ep, float* out, __nv_bfloat16* outb,
-                        cudaStream_t stream) {
-    CLLM_CHECK(part && (out || outb) && batch >= 1 && n >= 1 && ksplit >= 1, "launch_gemm_reduce: bad arguments");
+                        cudaStream_t stream, bool pdl) {
+    CLLM_CHECK(part && (out || outb) && batch >= 1 && batch <= kBatchMax && n >= 1 && ksplit >= 1,
+               "launch_gemm_reduce: bad arguments");
     CLLM_CHECK(ep != GemmEpilogue::ADD || out, "launch_gemm_reduce: ADD needs out");
     const size_t total = static_cast<size_t>(batch) * (ep == GemmEpilogue::SWIGLU ? n / 2 : n);
     const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 8));
-    gemm_reduce_kernel<<<blocks, 256, 0, stream>>>(part, ksplit, batch, n, static_cast<int>(ep), out, outb);
-    CLLM_CUDA(cudaGetLastError());
+    launch_kernel(gemm_reduce_kernel, dim3(blocks), dim3(256), 0, stream, pdl, part, ksplit, batch, n, static_cast<int>(ep), out,
+                  outb);
 }
 
 }  // namespace cudallm

@@ -102,4 +102,11 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Programmatic dependent launch. grid_dep_wait: blocks until the grids this one depends on have completed
+// and their memory is visible (a no-op when the grid was launched without the programmatic attribute).
+// grid_dep_launch: lets the next grid on the stream start launching; its own grid_dep_wait still waits
+// for this grid's completion.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 }  // namespace cudallm

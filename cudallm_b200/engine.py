@@ -36,6 +36,11 @@ class CudallmOptionsEx(ctypes.Structure):
                 ("reserved", c_int * 4)]
 
 
+class CudallmBatchOptions(ctypes.Structure):
+    _fields_ = [("struct_size", c_int), ("n_seq", c_int), ("max_seq_len", c_int), ("kv_dtype", c_int),
+                ("device", c_int), ("cuda_graph", c_int), ("reserved", c_int * 4)]
+
+
 class CudallmConfigInfo(ctypes.Structure):
     _fields_ = [("weight_dtype", c_int), ("hidden", c_int), ("inter", c_int), ("n_layers", c_int),
                 ("n_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int), ("vocab", c_int),
@@ -81,7 +86,16 @@ SIGNATURES = {
     "cudallm_engine_device": ([c_void_p], c_int),
     "cudallm_debug_trace": ([c_void_p, c_int], c_int),
     "cudallm_debug_read_trace": ([c_void_p, POINTER(c_ulonglong), c_ulonglong, _INT_P, _INT_P], c_int),
-    "cudallm_kernel_gemm": ([_USHORT_P, _USHORT_P, _FLOAT_P, c_int, c_int, c_int, c_int, c_int], c_int),
+    "cudallm_default_batch_options": ([POINTER(CudallmBatchOptions)], None),
+    "cudallm_batch_create": ([c_char_p, POINTER(CudallmBatchOptions), POINTER(c_void_p)], c_int),
+    "cudallm_batch_destroy": ([c_void_p], None),
+    "cudallm_batch_get_config": ([c_void_p, POINTER(CudallmConfigInfo)], c_int),
+    "cudallm_batch_reset": ([c_void_p, c_int], c_int),
+    "cudallm_batch_pos": ([c_void_p, c_int], c_int),
+    "cudallm_batch_step": ([c_void_p, _INT_P, _INT_P, _FLOAT_P], c_int),
+    "cudallm_batch_synchronize": ([c_void_p], c_int),
+    "cudallm_batch_stream": ([c_void_p], c_void_p),
+    "cudallm_kernel_gemm": ([_USHORT_P, _USHORT_P, _USHORT_P, _FLOAT_P, c_int, c_int, c_int, c_int, c_int], c_int),
     # device pointers: q, k_cache, v_cache, ctx, out, nh, nkv, hd, max_seq, stream
     "cudallm_attention_noalloc": ([c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
                                   c_int),
@@ -232,6 +246,87 @@ class Engine:
             self.close()
 
 
+class BatchEngine:
+    """Batched decode of up to 64 independent sequences on one GPU (cudallm_batch_* entry points)."""
+
+    def __init__(self, path: Path | str, *, n_seq: int = 64, max_seq_len: int = 0, kv_dtype: str = "fp16",
+                 device: int = -1, cuda_graph: bool = True):
+        self._h = None
+        lib_ = _lib()
+        opts = CudallmBatchOptions()
+        lib_.cudallm_default_batch_options(ctypes.byref(opts))
+        opts.n_seq = int(n_seq)
+        opts.max_seq_len = int(max_seq_len)
+        opts.kv_dtype = _KV[kv_dtype]
+        opts.device = int(device)
+        opts.cuda_graph = int(bool(cuda_graph))
+        h = c_void_p()
+        _check(lib_.cudallm_batch_create(str(path).encode(), ctypes.byref(opts), ctypes.byref(h)))
+        self._h = h
+        info = CudallmConfigInfo()
+        _check(lib_.cudallm_batch_get_config(self._h, ctypes.byref(info)))
+        self.config: dict = {name: getattr(info, name) for name, _ in CudallmConfigInfo._fields_}
+        self.n_seq = int(n_seq)
+        self._vocab = info.vocab
+
+    def _handle(self) -> c_void_p:
+        if self._h is None:
+            raise CudaLLMError(5, "engine is closed")
+        return self._h
+
+    def pos(self, seq: int) -> int:
+        return _lib().cudallm_batch_pos(self._handle(), int(seq))
+
+    @property
+    def stream_handle(self) -> int:
+        return int(_lib().cudallm_batch_stream(self._handle()) or 0)
+
+    def reset(self, seq: int = -1) -> None:
+        _check(_lib().cudallm_batch_reset(self._handle(), int(seq)))
+
+    def synchronize(self) -> None:
+        _check(_lib().cudallm_batch_synchronize(self._handle()))
+
+    def _tokens(self, tokens) -> np.ndarray | None:
+        if tokens is None:
+            return None
+        t = np.ascontiguousarray(tokens, dtype=np.int32)
+        if t.shape != (self.n_seq,):
+            raise ValueError(f"tokens must have shape ({self.n_seq},)")
+        return t
+
+    def step(self, tokens=None, *, want_logits: bool = False) -> tuple[np.ndarray, np.ndarray | None]:
+        """One step of every sequence: tokens [n_seq] (-1 = the sequence's previous argmax; None = all -1)
+        -> (next token per sequence, logits [n_seq][vocab] if asked)."""
+        t = self._tokens(tokens)
+        nxt = np.empty(self.n_seq, dtype=np.int32)
+        logits = np.empty((self.n_seq, self._vocab), dtype=np.float32) if want_logits else None
+        _check(_lib().cudallm_batch_step(self._handle(), t.ctypes.data_as(_INT_P) if t is not None else None,
+                                         nxt.ctypes.data_as(_INT_P), _fp(logits) if logits is not None else None))
+        return nxt, logits
+
+    def step_async(self, tokens=None) -> None:
+        """Enqueues one step without waiting or copying anything back."""
+        t = self._tokens(tokens)
+        _check(_lib().cudallm_batch_step(self._handle(), t.ctypes.data_as(_INT_P) if t is not None else None, None,
+                                         None))
+
+    def close(self) -> None:
+        if self._h is not None:
+            _lib().cudallm_batch_destroy(self._h)
+            self._h = None
+
+    def __enter__(self) -> "BatchEngine":
+        return self
+
+    def __exit__(self, *exc) -> None:
+        self.close()
+
+    def __del__(self) -> None:
+        if getattr(self, "_h", None) is not None:
+            self.close()
+
+
 def kernel_matvec(impl: str | int, wtype: str | int, epilogue: str | int, fuse_norm: bool | int, rpb: int,
                   w: np.ndarray, scales: np.ndarray | None, x: np.ndarray, norm_w: np.ndarray | None, eps: float,
                   y_init: np.ndarray | None, rows: int, cols: int) -> np.ndarray:
@@ -280,18 +375,24 @@ def kernel_attention(impl: str | int, q: np.ndarray, k_cache: np.ndarray, v_cach
     return out
 
 
-def kernel_gemm(w_bits: np.ndarray, x_bits: np.ndarray, *, ksplit: int = 1, epilogue: str = "store",
-                y: np.ndarray | None = None) -> np.ndarray:
-    """Batched-path GEMM hook: w_bits [n][k], x_bits [batch][k] bf16 bits (uint16) -> fp32 [batch][n]
-    (store / add onto y) or [batch][n/2] (swiglu)."""
+def kernel_gemm(w_bits: np.ndarray, x_bits: np.ndarray, *, x_lo_bits: np.ndarray | None = None, ksplit: int = 1,
+                epilogue: str = "store", y: np.ndarray | None = None) -> np.ndarray:
+    """Batched-path GEMM hook: w_bits [n][k], x_bits (and optionally x_lo_bits, added to x) [batch][k] bf16
+    bits (uint16) -> fp32 [batch][n] (store / add onto y) or [batch][n/2] (swiglu)."""
     w = np.ascontiguousarray(w_bits, dtype=np.uint16)
     x = np.ascontiguousarray(x_bits, dtype=np.uint16)
     n, k = w.shape
     batch = x.shape[0]
+    lo = None
+    if x_lo_bits is not None:
+        lo = np.ascontiguousarray(x_lo_bits, dtype=np.uint16)
+        if lo.shape != x.shape:
+            raise ValueError("x_lo_bits must have the shape of x_bits")
     ep = _EPILOGUE[epilogue]
     n_out = n // 2 if epilogue == "swiglu" else n
     out = np.zeros((batch, n_out), dtype=np.float32) if y is None else np.ascontiguousarray(y, dtype=np.float32).copy()
-    _check(_lib().cudallm_kernel_gemm(w.ctypes.data_as(_USHORT_P), x.ctypes.data_as(_USHORT_P), _fp(out), n, k, batch,
+    _check(_lib().cudallm_kernel_gemm(w.ctypes.data_as(_USHORT_P), x.ctypes.data_as(_USHORT_P),
+                                      lo.ctypes.data_as(_USHORT_P) if lo is not None else None, _fp(out), n, k, batch,
                                       int(ksplit), ep))
     return out
 

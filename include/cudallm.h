@@ -137,13 +137,54 @@ int cudallm_debug_trace(cudallm_engine* e, int enable);
 int cudallm_debug_read_trace(cudallm_engine* e, unsigned long long* out, unsigned long long count, int* grid_out,
                              int* slots_out);
 
+/* ---- batched decode (no counterpart in the reference, whose engine holds one sequence): up to 64
+ * independent sequences decoded together on one GPU, one token each per step; every row runs the
+ * reference engine's per-token sequence (src/engine/engine.cpp:181-237) on its own token, position and KV
+ * cache, with the weight matvecs as tensor-core GEMMs (bf16 weights). Several GPUs: one batch engine per
+ * device (device field), each on its own sequences; no communication between them. */
+typedef struct cudallm_batch cudallm_batch;
+
+typedef struct {
+    int struct_size; /* sizeof(cudallm_batch_options) */
+    int n_seq;       /* 1..64 */
+    int max_seq_len; /* 0 = the file header's value, else a positive multiple of 128 not above it */
+    int kv_dtype;    /* CUDALLM_KV_FP16 or CUDALLM_KV_BF16 */
+    int device;      /* CUDA device ordinal; -1 = the calling thread's current device */
+    int cuda_graph;  /* 1: replay the step as a CUDA graph */
+    int reserved[4];
+} cudallm_batch_options;
+
+/* Fills n_seq 64, max_seq_len 0, kv fp16, device -1, cuda_graph 1. */
+void cudallm_default_batch_options(cudallm_batch_options* out);
+/* Loads a .cudallm file (bf16 weights) for n_seq sequences; *out = NULL on failure. */
+int cudallm_batch_create(const char* path, const cudallm_batch_options* opts, cudallm_batch** out);
+/* NULL-safe. */
+void cudallm_batch_destroy(cudallm_batch* e);
+/* As cudallm_get_config; max_seq_len is the engine's. */
+int cudallm_batch_get_config(cudallm_batch* e, cudallm_config_info* out);
+/* seq in [0, n_seq): that sequence's position back to 0; seq = -1: every sequence. */
+int cudallm_batch_reset(cudallm_batch* e, int seq);
+/* Host mirror of sequence seq's position; -1 for a NULL engine or an index out of range. */
+int cudallm_batch_pos(cudallm_batch* e, int seq);
+/* One decode step of every sequence. tokens: host [n_seq], tokens[b] >= 0 is fed to sequence b, -1 feeds
+ * b's previous argmax; NULL = all -1. next_out: host [n_seq] (each row's argmax, lowest index on ties) or
+ * NULL; logits_out: host [n_seq][vocab] or NULL. With both outputs NULL the call does not synchronise.
+ * Every sequence must have room (pos < max_seq_len), else CUDALLM_ERR_STATE and nothing runs. */
+int cudallm_batch_step(cudallm_batch* e, const int* tokens, int* next_out, float* logits_out);
+/* Waits for every queued step; reports a device-side failure. */
+int cudallm_batch_synchronize(cudallm_batch* e);
+/* The engine's CUDA stream (a cudaStream_t); NULL for a NULL engine. */
+void* cudallm_batch_stream(cudallm_batch* e);
+
 /* Test hook of the batched path (no counterpart in the reference): tensor-core GEMM y[b][j] (+)= sum_k
- * x[b][k] * w[j][k] for b < batch (1..64), w [n][k] and x [batch][k] bf16 bits, fp32 result, the K range
- * split over `ksplit` CTA rows (k a multiple of 64 * ksplit). epilogue 0 stores, 1 adds to y, 2 applies
- * SwiGLU (y is [batch][n/2]: silu(gate) * up, gate rows first). Host pointers; allocates, runs on the
- * default stream and synchronises like the other hooks. */
-int cudallm_kernel_gemm(const unsigned short* w, const unsigned short* x, float* y, int n, int k, int batch, int ksplit,
-                        int epilogue);
+ * (x[b][k] + x_lo[b][k]) * w[j][k] for b < batch (1..64), w [n][k], x and x_lo [batch][k] bf16 bits (x_lo
+ * may be NULL = zeros; the engine passes an fp32 activation as its bf16 rounding plus the bf16 rounding of
+ * the remainder), fp32 result, the 64-column K chunks split evenly over `ksplit` CTA rows (k a multiple of
+ * 64, ksplit <= k / 64). epilogue 0 stores, 1 adds to y, 2 applies SwiGLU (y is [batch][n/2]: silu(gate) *
+ * up, gate rows first). Host pointers; allocates, runs on the default stream and synchronises like the
+ * other hooks. */
+int cudallm_kernel_gemm(const unsigned short* w, const unsigned short* x, const unsigned short* x_lo, float* y, int n, int k,
+                        int batch, int ksplit, int epilogue);
 
 /* No counterpart in the reference. Split-K decode attention (the kernels behind
  * cudallm_kernel_attention impl 1) for callers that cannot allocate device memory: code whose device

@@ -1,0 +1,239 @@
+"""GPU: batched decode (cudallm_batch_* entry points) on the seeded Llama-3.2-1B bf16 file.
+
+Every row of the batch is one independent sequence. Each row is checked against what the batch-1 engine
+computes for the same sequence, and row 0 (fed the golden prompt) against wasiqnauman/cudallm's own
+ReferenceModel run (golden_full_bf16_fp16.npz):
+  * row 0's greedy ids equal the reference's for all 64 generated tokens, and its logits at the last
+    prompt step are within max |delta| < 2e-2 of the reference's (the reference test tolerance);
+  * every row's logits at its last prompt step are within max |delta| < 2e-3 of the batch-1 engine's
+    (fp32 activations on both paths; the batched GEMMs carry them as bf16 hi + lo planes), and its greedy
+    ids equal the batch-1 engine's up to the first step whose batch-1 top-2 margin is below 5e-3;
+  * rows see only their own token, position and KV cache: equal inputs give bitwise-equal logits, a
+    reset row reproduces its first run bitwise, and graph replay equals direct launches bitwise;
+  * contexts crossing the 256-token boundaries at which the step's graph is captured again stay in
+    agreement with the batch-1 engine (teacher-forced on the same tokens).
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from cudallm_b200.engine import BatchEngine, CudaLLMError, Engine
+
+pytestmark = pytest.mark.gpu
+
+GEN = 64
+LOGIT_TOL = 2e-3       # batched vs batch-1 engine, same weights and tokens
+REF_LOGIT_TOL = 2e-2   # batched vs the reference's ReferenceModel (its own test tolerance)
+MARGIN = 5e-3          # ids compared while the batch-1 top-2 margin is at least this
+
+
+def _margin(logits: np.ndarray) -> float:
+    top2 = np.partition(logits, -2)[-2:]
+    return float(top2[1] - top2[0])
+
+
+def _bs1(path, tokens, gen, *, kv_dtype="fp16", max_seq_len=0):
+    """Batch-1 engine over `tokens` then `gen` greedy steps: (logits at the last fed token, generated ids,
+    top-2 margin of each generated step's logits)."""
+    ids, margins = [], []
+    with Engine(path, kv_dtype=kv_dtype, max_seq_len=max_seq_len) as eng:
+        lg = None
+        for t in tokens:
+            nxt, lg = eng.step(int(t), want_logits=True)
+        last = lg
+        ids.append(nxt)
+        margins.append(_margin(lg))
+        while len(ids) < gen:
+            nxt, lg = eng.step(None, want_logits=True)
+            ids.append(nxt)
+            margins.append(_margin(lg))
+    return last, ids, margins
+
+
+def _run_batch(eng: BatchEngine, prompts: list[list[int]], gen: int):
+    """Feeds row b its prompt, then lets it generate `gen` tokens (rows with shorter prompts start
+    generating while others are still fed). Returns (logits of each row at its last prompt step, ids)."""
+    n = len(prompts)
+    total = max(len(p) for p in prompts) + gen - 1
+    last = [None] * n
+    ids: list[list[int]] = [[] for _ in range(n)]
+    for i in range(total):
+        toks = np.array([p[i] if i < len(p) else -1 for p in prompts], dtype=np.int32)
+        want = any(i == len(p) - 1 for p in prompts)
+        nxt, lg = eng.step(toks, want_logits=want)
+        for b, p in enumerate(prompts):
+            if i == len(p) - 1:
+                last[b] = lg[b].copy()
+            if len(p) - 1 <= i and len(ids[b]) < gen:
+                ids[b].append(int(nxt[b]))
+    return last, ids
+
+
+@pytest.fixture(scope="module")
+def bf16_path(model_path, golden):
+    g = golden("full_bf16_fp16")
+    path, digest = model_path("bf16")
+    assert digest == str(g["digest"]), "synthetic weights differ from the ones the golden run used"
+    return path
+
+
+@pytest.fixture(scope="module")
+def mixed_run(bf16_path, golden):
+    g = golden("full_bf16_fp16")
+    rng = np.random.default_rng(1234)
+    lens = [len(g["prompt"]), 5, 17, 1, 40, 23]
+    prompts = [[int(t) for t in g["prompt"]]] + [[int(t) for t in rng.integers(0, 128256, n)] for n in lens[1:]]
+    with BatchEngine(bf16_path, n_seq=len(prompts), max_seq_len=256) as eng:
+        last, ids = _run_batch(eng, prompts, GEN)
+        positions = [eng.pos(b) for b in range(len(prompts))]
+    return {"prompts": prompts, "last": last, "ids": ids, "pos": positions, "golden": g}
+
+
+def test_row0_greedy_ids_match_reference(mixed_run):
+    g = mixed_run["golden"]
+    assert mixed_run["ids"][0] == [int(t) for t in g["ids"][:GEN]]
+
+
+def test_row0_logits_match_reference(mixed_run):
+    g = mixed_run["golden"]
+    ref = g["logits_31"]
+    got = mixed_run["last"][0]
+    assert np.abs(got - ref).max() < REF_LOGIT_TOL
+    assert int(np.argmax(got)) == int(np.argmax(ref))
+
+
+@pytest.mark.parametrize("row", range(6))
+def test_rows_match_batch1_engine(mixed_run, bf16_path, row):
+    prompt = mixed_run["prompts"][row]
+    last, ids, margins = _bs1(bf16_path, prompt, GEN, max_seq_len=256)
+    got = mixed_run["last"][row]
+    assert np.abs(got - last).max() < LOGIT_TOL
+    n_cmp = next((i for i, m in enumerate(margins) if m < MARGIN), GEN)
+    assert mixed_run["ids"][row][:n_cmp] == ids[:n_cmp]
+
+
+def test_positions_advance_per_step(mixed_run):
+    total = max(len(p) for p in mixed_run["prompts"]) + GEN - 1
+    assert mixed_run["pos"] == [total] * len(mixed_run["prompts"])
+
+
+def test_rows_independent_and_deterministic(bf16_path):
+    """Rows 0 and 2 get the same tokens, row 1 others: rows 0 and 2 agree bitwise at every step; resetting
+    row 1 alone and feeding it row 0's tokens reproduces row 0 bitwise; graph replay equals direct
+    launches bitwise."""
+    rng = np.random.default_rng(7)
+    a = [int(t) for t in rng.integers(0, 128256, 12)]
+    b = [int(t) for t in rng.integers(0, 128256, 12)]
+    runs = {}
+    for graph in (True, False):
+        with BatchEngine(bf16_path, n_seq=3, max_seq_len=128, cuda_graph=graph) as eng:
+            lgs = []
+            for i in range(12):
+                _, lg = eng.step(np.array([a[i], b[i], a[i]], dtype=np.int32), want_logits=True)
+                lgs.append(lg.copy())
+                np.testing.assert_array_equal(lg[0], lg[2])
+            eng.reset(1)
+            assert [eng.pos(r) for r in range(3)] == [12, 0, 12]
+            for i in range(12):
+                _, lg = eng.step(np.array([b[i % 12], a[i], b[i % 12]], dtype=np.int32), want_logits=True)
+                np.testing.assert_array_equal(lg[1], lgs[i][0])
+            runs[graph] = np.stack([x[0] for x in lgs])
+    np.testing.assert_array_equal(runs[True], runs[False])
+
+
+def test_full_batch_sampled_rows_match_batch1(bf16_path):
+    """64 rows (the per-GPU batch of the batched benchmark), 16 random prompt tokens then 16 generated:
+    rows 0, 31 and 63 at the last step against the batch-1 engine fed the same tokens."""
+    rng = np.random.default_rng(99)
+    prompts = rng.integers(0, 128256, (64, 16)).astype(np.int32)
+    hist = [[int(t) for t in prompts[r]] for r in range(64)]
+    with BatchEngine(bf16_path, n_seq=64, max_seq_len=128) as eng:
+        for i in range(16):
+            nxt, _ = eng.step(prompts[:, i])
+        for i in range(15):
+            for r in range(64):
+                hist[r].append(int(nxt[r]))
+            nxt, lg = eng.step(None, want_logits=(i == 14))
+    for r in (0, 31, 63):
+        with Engine(bf16_path, max_seq_len=128) as one:
+            for t in hist[r]:
+                _, ref = one.step(t, want_logits=True)
+        assert np.abs(lg[r] - ref).max() < LOGIT_TOL
+        assert int(nxt[r]) == int(np.argmax(ref)) or _margin(ref) < MARGIN
+
+
+def test_context_crossing_graph_tile_groups(bf16_path):
+    """300 teacher-forced steps (the attention grid grows at 256 tokens and the graph is re-captured):
+    logits at steps 255, 256 and 299 against the batch-1 engine on the same tokens."""
+    rng = np.random.default_rng(5)
+    toks = rng.integers(0, 128256, (2, 300)).astype(np.int32)
+    check = (255, 256, 299)
+    got = {}
+    with BatchEngine(bf16_path, n_seq=2, max_seq_len=512) as eng:
+        for i in range(300):
+            if i in check:
+                _, lg = eng.step(toks[:, i], want_logits=True)
+                got[i] = lg.copy()
+            else:
+                eng.step_async(toks[:, i])
+    for r in range(2):
+        with Engine(bf16_path, max_seq_len=512) as one:
+            for i in range(300):
+                if i in check:
+                    _, ref = one.step(int(toks[r, i]), want_logits=True)
+                    assert np.abs(got[i][r] - ref).max() < LOGIT_TOL, f"row {r} step {i}"
+                else:
+                    one.step_async(int(toks[r, i]))
+
+
+def test_bf16_kv_cache(bf16_path):
+    rng = np.random.default_rng(11)
+    toks = rng.integers(0, 128256, (2, 20)).astype(np.int32)
+    with BatchEngine(bf16_path, n_seq=2, max_seq_len=128, kv_dtype="bf16") as eng:
+        for i in range(20):
+            _, lg = eng.step(toks[:, i], want_logits=(i == 19))
+    for r in range(2):
+        with Engine(bf16_path, max_seq_len=128, kv_dtype="bf16") as one:
+            for t in toks[r]:
+                _, ref = one.step(int(t), want_logits=True)
+        # A one-ulp bf16 rounding flip of a cached value moves logits by more than the fp16 bound.
+        assert np.abs(lg[r] - ref).max() < REF_LOGIT_TOL
+
+
+def test_errors(bf16_path, model_path):
+    with pytest.raises(CudaLLMError) as e:
+        BatchEngine(bf16_path, n_seq=0)
+    assert e.value.code == 1
+    with pytest.raises(CudaLLMError) as e:
+        BatchEngine(bf16_path, n_seq=65)
+    assert e.value.code == 1
+    with pytest.raises(CudaLLMError) as e:
+        BatchEngine(bf16_path, max_seq_len=100)
+    assert e.value.code == 1
+    int4_path, _ = model_path("int4")
+    with pytest.raises(CudaLLMError) as e:
+        BatchEngine(int4_path, n_seq=2)
+    assert e.value.code == 1
+    with BatchEngine(bf16_path, n_seq=2, max_seq_len=128) as eng:
+        with pytest.raises(CudaLLMError) as e:
+            eng.step(np.array([0, 128256], dtype=np.int32))
+        assert e.value.code == 1
+        with pytest.raises(CudaLLMError) as e:
+            eng.reset(2)
+        assert e.value.code == 1
+        assert eng.pos(5) == -1
+        for i in range(128):
+            eng.step_async(np.array([i, 2 * i], dtype=np.int32))
+        eng.synchronize()
+        assert eng.pos(0) == 128
+        with pytest.raises(CudaLLMError) as e:
+            eng.step(None)
+        assert e.value.code == 5
+        eng.reset(0)
+        with pytest.raises(CudaLLMError) as e:
+            eng.step(None)  # row 1 is still full
+        assert e.value.code == 5
+        eng.reset()
+        nxt, _ = eng.step(np.array([1, 2], dtype=np.int32))
+        assert all(0 <= t < 128256 for t in nxt)
