@@ -11,6 +11,10 @@ engine's stream, bracketed by a barrier and a device synchronise. With N GPUs (t
 per GPU) every rank decodes its own sequence (replicas: the batch-1 path does not shard) and the value
 is N*K divided by the slowest rank's time.
 
+Also measured on every rank (unless --quick): batched decode of 64 sequences per GPU
+(512-token prompts, then timed greedy decode steps; tensor-core GEMMs), reported under "batched" as the
+whole-job tok/s over all ranks.
+
 Reported (one JSON line on rank 0): value = tok/s with weights resident; e2e = tok/s through the C ABI
 when every step takes its token from the host and returns the next token to the host; roofline of the
 persistent decode-step kernel (algorithmic bytes = weight bytes + KV bytes read at the step's context,
@@ -166,6 +170,53 @@ def time_e2e(eng, prompt: list[int], steps: int, torch, barrier) -> dict:
     return {"total_ms": start.elapsed_time(end), "wall_ms": wall * 1e3}
 
 
+BATCH_SEQS, BATCH_PROMPT, BATCH_GEN = 64, 512, 256  # BASELINE config 5, per GPU
+
+
+def time_batched(args, device: int, torch, barrier) -> dict:
+    """Batched decode (64 independent sequences on this GPU): every sequence steps a 512-token random
+    prompt (untimed), then 256 greedy decode steps are timed with CUDA events on the engine's stream
+    (positions 512..767, all 64 sequences per step); then 64 more steps through the C ABI with the tokens
+    sent from the host and the next tokens read back each step (e2e)."""
+    import numpy as np
+    from cudallm_b200 import synth
+    from cudallm_b200.engine import BatchEngine
+    path, _ = synth.ensure_model("bf16", seed=0, max_seq_len=4096)
+    rng = np.random.default_rng([0, device])
+    prompts = rng.integers(0, 128256, (BATCH_PROMPT, BATCH_SEQS)).astype(np.int32)
+    gen = min(BATCH_GEN, 1024 - BATCH_PROMPT - 64)
+    with BatchEngine(path, n_seq=BATCH_SEQS, max_seq_len=1024, kv_dtype=args.kv, device=device) as eng:
+        stream = torch.cuda.ExternalStream(eng.stream_handle, device=torch.device("cuda", device))
+        for i in range(BATCH_PROMPT):
+            eng.step_async(prompts[i])
+        eng.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(device)
+        start.record(stream)
+        for _ in range(gen):
+            eng.step_async(None)
+        end.record(stream)
+        eng.synchronize()
+        torch.cuda.synchronize(device)
+        barrier()
+        ms = start.elapsed_time(end)
+        nxt, _ = eng.step(None)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize(device)
+        e0.record(stream)
+        n_e2e = 64
+        for _ in range(n_e2e):
+            nxt, _ = eng.step(nxt)
+        e1.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        e2e_ms = e0.elapsed_time(e1)
+        weight_bytes = eng.config["weight_bytes"]
+    return {"ms": ms, "steps": gen, "e2e_ms": e2e_ms, "e2e_steps": n_e2e, "weight_bytes": weight_bytes}
+
+
 def cpu_reference_tokps(path: Path, prompt: list[int], kv: str, n_prompt: int, n_decode: int,
                         time_budget_s: float | None = None) -> dict:
     """The oracle's restatement of the reference CPU model (per-call dequantisation, all host threads)."""
@@ -297,6 +348,24 @@ def run_ours(args) -> None:
                      "roofline_frac": (b / (kms * 1e-3) / 1e9) / peaks["hbm_gbs"],
                      "achieved_gbs": b / (kms * 1e-3) / 1e9, "ms_per_token": ms / args.steps}
 
+    batched = None
+    if not args.quick:
+        b = time_batched(args, local_rank, torch, barrier)
+        b_ms = max_over_ranks(b["ms"])
+        b_e2e_ms = max_over_ranks(b["e2e_ms"])
+        avg_ctx_b = BATCH_PROMPT + (b["steps"] + 1) / 2
+        b_bytes = b["weight_bytes"] + BATCH_SEQS * KV_BYTES_PER_TOKEN * avg_ctx_b
+        b_gbs = b_bytes / (b_ms / b["steps"] * 1e-3) / 1e9
+        batched = {"metric": "batched decode aggregate tok/s (bf16 weights)",
+                   "value": world * BATCH_SEQS * b["steps"] / (b_ms * 1e-3), "unit": "tok/s",
+                   "per_gpu_tok_s": BATCH_SEQS * b["steps"] / (b_ms * 1e-3), "ms_per_step": b_ms / b["steps"],
+                   "sequences_per_gpu": BATCH_SEQS, "prompt": BATCH_PROMPT, "timed_decode_steps": b["steps"],
+                   "kv": args.kv, "bytes_per_step": int(b_bytes), "achieved_gbs": b_gbs,
+                   "roofline_frac": b_gbs / peaks["hbm_gbs"],
+                   "e2e": {"value": world * BATCH_SEQS * b["e2e_steps"] / (b_e2e_ms * 1e-3), "unit": "tok/s",
+                           "h2d_bytes_per_step": 4 * BATCH_SEQS, "d2h_bytes_per_step": 4 * BATCH_SEQS + 4},
+                   "scaling": "weak (64 sequences per GPU, no collective)"}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         path, _ = synth.ensure_model(args.dtype, seed=0, max_seq_len=4096)
@@ -324,6 +393,7 @@ def run_ours(args) -> None:
             "gpu_launches": args.steps,
             "clocks": head["clocks"],
             "precisions": extra,
+            "batched": batched,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

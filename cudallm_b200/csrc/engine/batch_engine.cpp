@@ -60,6 +60,8 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
     max_seq_ = opts_.max_seq_len ? opts_.max_seq_len : c.max_seq_len;
     host_pos_.assign(opts_.n_seq, 0);
     if (const char* env = std::getenv("CUDALLM_BATCH_PDL")) opts_.pdl = std::atoi(env) != 0;
+    if (const char* env = std::getenv("CUDALLM_BATCH_ATTN")) opts_.attn_mode = std::atoi(env);
+    if (opts_.attn_mode < 0 || opts_.attn_mode > 2) throw ArgError("attention mode must be 0, 1 or 2");
     try {
         CLLM_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
         int sms = 0;
@@ -67,6 +69,9 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
         const int H = c.hidden, I = c.inter, V = c.vocab, NH = c.n_heads, NKV = c.n_kv_heads, D = c.head_dim;
         const int QKV = (NH + 2 * NKV) * D;
         auto mt = [](int n) { return (n + 127) / 128; };
+        // One streaming CTA per (KV head, sequence) once that fills the SMs; fewer sequences split their
+        // contexts over more CTAs.
+        attn_stream_ = opts_.attn_mode == 1 || (opts_.attn_mode == 0 && opts_.n_seq * NKV >= sms);
         ks_qkv_ = pick_ksplit(mt(QKV), H / 64, sms);
         ks_wo_ = pick_ksplit(mt(H), H / 64, sms);
         ks_gu_ = pick_ksplit(mt(2 * I), H / 64, sms);
@@ -86,12 +91,17 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
         CLLM_CUDA(cudaMemset(k_cache_, 0, cache_elems * 2));
         CLLM_CUDA(cudaMemset(v_cache_, 0, cache_elems * 2));
         const size_t slots = static_cast<size_t>(max_seq_ / kAttnTile);
-        alloc_zero(&att_o_, B * NH * slots * D);
-        alloc_zero(&att_ml_, B * NH * slots * 2);
+        if (!attn_stream_) {
+            alloc_zero(&att_o_, B * NH * slots * D);
+            alloc_zero(&att_ml_, B * NH * slots * 2);
+        }
         alloc_zero(&tok_in_, B);
         alloc_zero(&tok_, B);
         alloc_zero(&dpos_, B);
         alloc_zero(&err_, 1);
+        alloc_zero(&am_v_, B * kArgmaxSplit);
+        alloc_zero(&am_i_, B * kArgmaxSplit);
+        alloc_zero(&am_ticket_, B);
         CLLM_CUDA(cudaMemset(tok_in_, 0xff, B * sizeof(int)));  // -1: feed the previous argmax
         CLLM_CUDA(cudaDeviceSynchronize());
     } catch (...) {
@@ -108,11 +118,13 @@ void BatchEngine::free_all() noexcept {
     if (graph_) report(cudaGraphDestroy(graph_), "cudaGraphDestroy");
     graph_exec_ = nullptr;
     graph_ = nullptr;
-    void* bufs[] = {x_, xn_, act_, qkv_, part_, k_cache_, v_cache_, att_o_, att_ml_, tok_in_, tok_, dpos_, err_};
+    void* bufs[] = {x_, xn_, act_, qkv_, part_, k_cache_, v_cache_, att_o_, att_ml_, tok_in_, tok_, dpos_, err_, am_v_, am_i_, am_ticket_};
     for (void* b : bufs) {
         if (b) report(cudaFree(b), "cudaFree");
     }
-    x_ = qkv_ = part_ = att_o_ = att_ml_ = nullptr;
+    x_ = qkv_ = part_ = att_o_ = att_ml_ = am_v_ = nullptr;
+    am_i_ = nullptr;
+    am_ticket_ = nullptr;
     xn_ = act_ = k_cache_ = v_cache_ = nullptr;
     tok_in_ = tok_ = dpos_ = nullptr;
     err_ = nullptr;
@@ -145,7 +157,8 @@ void BatchEngine::synchronize() {
     CLLM_CUDA(cudaMemcpy(&err, err_, sizeof(err), cudaMemcpyDeviceToHost));
     if (err != 0) {
         CLLM_CUDA(cudaMemset(err_, 0, sizeof(unsigned)));
-        throw StateError("device: a bounded wait in a batched GEMM gave up; the step's results are invalid");
+        throw StateError("device: a bounded wait in the batched step gave up (flags " + std::to_string(err) +
+                         "); the step's results are invalid");
     }
 }
 
@@ -190,8 +203,12 @@ void BatchEngine::enqueue_layers(int tiles) {
         launch_gemm_bf16(bf(L.wqkv), QKV, H, xn, B, ks_qkv_, part_, err_, s, pdl);
         launch_gemm_reduce(part_, ks_qkv_, B, QKV, GemmEpilogue::STORE, qkv_, nullptr, s, pdl);
         launch_rope_kv_rows<KV>(qkv_, W.rope_inv_freq, kl, vl, seq_stride, dpos_, B, NH, NKV, D, max_seq_, s, pdl);
-        launch_attention_rows<KV>(qkv_, kl, vl, seq_stride, dpos_, tiles * kAttnTile, att_o_, att_ml_, xn, B, NH, NKV, max_seq_,
-                                  s, pdl);
+        if (attn_stream_) {
+            launch_attention_rows_stream<KV>(qkv_, kl, vl, seq_stride, dpos_, xn, B, NH, NKV, max_seq_, err_, s, pdl);
+        } else {
+            launch_attention_rows<KV>(qkv_, kl, vl, seq_stride, dpos_, tiles * kAttnTile, att_o_, att_ml_, xn, B, NH, NKV,
+                                      max_seq_, s, pdl);
+        }
         launch_gemm_bf16(bf(L.wo), H, NH * D, xn, B, ks_wo_, part_, err_, s, pdl);
         launch_gemm_reduce(part_, ks_wo_, B, H, GemmEpilogue::ADD, x_, nullptr, s, pdl);
         launch_rmsnorm_rows(x_, L.ffn_norm, c.rms_eps, xn, B, H, s, pdl);
@@ -202,7 +219,7 @@ void BatchEngine::enqueue_layers(int tiles) {
     }
     launch_rmsnorm_rows(x_, W.final_norm, c.rms_eps, xn, B, H, s, pdl);
     launch_gemm_bf16(bf(W.tok_embeddings), V, H, xn, B, 1, part_, err_, s, pdl);  // logits = part_ [B][V]
-    launch_argmax_rows(part_, V, tok_, dpos_, B, s, pdl);
+    launch_argmax_rows(part_, V, am_v_, am_i_, am_ticket_, tok_, dpos_, B, s, pdl);
 }
 
 void BatchEngine::enqueue_step(int tiles) {
@@ -233,8 +250,12 @@ void BatchEngine::step(const int* tokens, int* next_out, float* logits_out) {
         CLLM_CUDA(cudaMemsetAsync(tok_in_, 0xff, sizeof(int) * B, stream_));
         tok_in_fed_ = false;
     }
+    // The split attention's grid covers the longest context (rounded up to a tile group); the streaming
+    // kernel reads each row's context length on the device, so its graph never needs re-capturing.
     const int max_tiles = max_seq_ / kAttnTile;
-    const int tiles = std::min(max_tiles, (longest + kAttnTile * kTileGroup - 1) / (kAttnTile * kTileGroup) * kTileGroup);
+    const int tiles = attn_stream_ ? max_tiles
+                                   : std::min(max_tiles, (longest + kAttnTile * kTileGroup - 1) / (kAttnTile * kTileGroup) *
+                                                             kTileGroup);
     if (opts_.cuda_graph) {
         if (!graph_exec_ || graph_tiles_ != tiles) {
             cudaGraph_t g = nullptr;

@@ -26,6 +26,9 @@ struct BatchOptions {
     int device = -1;         // -1 = current device
     bool cuda_graph = true;  // replay the step as a CUDA graph
     bool pdl = true;         // programmatic dependent launch between the step's kernels
+    // Attention kernel: 0 = choose by size, 1 = one CTA per (KV head, sequence) streaming the whole
+    // context, 2 = split over 64-token tiles and merged by a second kernel (more CTAs for few sequences).
+    int attn_mode = 0;
 };
 
 class BatchEngine {
@@ -67,7 +70,8 @@ private:
     cudaStream_t stream_ = nullptr;
     cudaGraph_t graph_ = nullptr;
     cudaGraphExec_t graph_exec_ = nullptr;
-    int graph_tiles_ = 0;  // attention tiles the captured graph covers
+    int graph_tiles_ = 0;  // attention tiles the captured graph covers (split attention only)
+    bool attn_stream_ = true;
 
     // Per-operation K splits (grid rows of the GEMM), chosen to fill the SMs.
     int ks_qkv_ = 1, ks_wo_ = 1, ks_gu_ = 1, ks_down_ = 1;
@@ -85,6 +89,9 @@ private:
     int* tok_ = nullptr;              // [64] last argmax per sequence
     int* dpos_ = nullptr;             // [64] position per sequence
     unsigned* err_ = nullptr;         // device error word
+    float* am_v_ = nullptr;           // argmax slice results [64][kArgmaxSplit]
+    int* am_i_ = nullptr;
+    unsigned* am_ticket_ = nullptr;   // [64] per-row tickets (zero between launches)
     bool tok_in_fed_ = false;         // tok_in_ holds fed tokens (not all -1)
     size_t part_floats_ = 0;
 };

@@ -30,7 +30,18 @@ template <typename KV>
 void launch_attention_rows(const float* qkv, const KV* k_cache, const KV* v_cache, size_t seq_stride, const int* pos,
                            int max_ctx, float* part_o, float* part_ml, __nv_bfloat16* out, int batch, int nh, int nkv,
                            int max_seq, cudaStream_t stream, bool pdl = false);
-// tok[b] = argmax of logits row b (lowest index on ties), pos[b] += 1.
-void launch_argmax_rows(const float* logits, int n, int* tok, int* pos, int batch, cudaStream_t stream, bool pdl = false);
+// The same attention as launch_attention_rows, one CTA per (KV head, row) streaming the row's whole
+// context through shared memory (bulk async copies); no partials. err: device word, bit 1 set if a
+// bounded wait for a copy gave up. Caches 16-byte aligned.
+template <typename KV>
+void launch_attention_rows_stream(const float* qkv, const KV* k_cache, const KV* v_cache, size_t seq_stride, const int* pos,
+                                  __nv_bfloat16* out, int batch, int nh, int nkv, int max_seq, unsigned* err,
+                                  cudaStream_t stream, bool pdl = false);
+// tok[b] = argmax of logits row b (lowest index on ties), pos[b] += 1. Each row is split over
+// kArgmaxSplit blocks; scratch_v / scratch_i hold [batch][kArgmaxSplit] slice results and ticket [batch]
+// counters that must be zero before the first launch (each launch leaves them zero).
+constexpr int kArgmaxSplit = 16;
+void launch_argmax_rows(const float* logits, int n, float* scratch_v, int* scratch_i, unsigned* ticket, int* tok, int* pos,
+                        int batch, cudaStream_t stream, bool pdl = false);
 
 }  // namespace cudallm

@@ -81,6 +81,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
     const int c0 = static_cast<int>(static_cast<long long>(blockIdx.y) * a.chunks / a.ksplit);
     const int c1 = static_cast<int>(static_cast<long long>(blockIdx.y + 1) * a.chunks / a.ksplit);
     const int nch = c1 - c0;
+    // CTAs of one grid row start at different chunks of their K range (and wrap around), so that at any
+    // moment they read different activation tiles instead of all hitting the same L2 lines.
+    const int rot = static_cast<int>(blockIdx.x % static_cast<unsigned>(nch));
+    auto chunk_x = [&](int i) { return (c0 + (i + rot) % nch) * kGK; };
     grid_dep_launch();
     if (threadIdx.x == 0) {
         for (int s = 0; s < kGStages; ++s) {
@@ -105,17 +109,17 @@ __global__ void __launch_bounds__(kGThreads, 1)
         const int pre = nch < kGStages ? nch : kGStages;
         for (int i = 0; i < pre; ++i) {
             mbar_arrive_expect_tx(&full[i], kWTileBytes + kXTileBytes);
-            tma_load_2d_hint(wt + i * kWTileBytes, &wmap, (c0 + i) * kGK, n0, &full[i], pol);
+            tma_load_2d_hint(wt + i * kWTileBytes, &wmap, chunk_x(i), n0, &full[i], pol);
         }
         grid_dep_wait();
-        for (int i = 0; i < pre; ++i) tma_load_2d(xt + i * kXTileBytes, &xmap, (c0 + i) * kGK, 0, &full[i]);
+        for (int i = 0; i < pre; ++i) tma_load_2d(xt + i * kXTileBytes, &xmap, chunk_x(i), 0, &full[i]);
         int issued = pre;
         for (int i = pre; i < nch; ++i) {
             const int s = i % kGStages;
             if (!gemm_wait(&empty[s], ((i / kGStages) - 1) & 1, a.err)) break;
             mbar_arrive_expect_tx(&full[s], kWTileBytes + kXTileBytes);
-            tma_load_2d_hint(wt + s * kWTileBytes, &wmap, (c0 + i) * kGK, n0, &full[s], pol);
-            tma_load_2d(xt + s * kXTileBytes, &xmap, (c0 + i) * kGK, 0, &full[s]);
+            tma_load_2d_hint(wt + s * kWTileBytes, &wmap, chunk_x(i), n0, &full[s], pol);
+            tma_load_2d(xt + s * kXTileBytes, &xmap, chunk_x(i), 0, &full[s]);
             issued = i + 1;
         }
         // Every load issued lands before the CTA may exit (the MMA thread consumes them; this only

@@ -78,15 +78,26 @@ def bf16_path(model_path, golden):
     return path
 
 
-@pytest.fixture(scope="module")
-def mixed_run(bf16_path, golden):
-    g = golden("full_bf16_fp16")
-    rng = np.random.default_rng(1234)
-    lens = [len(g["prompt"]), 5, 17, 1, 40, 23]
-    prompts = [[int(t) for t in g["prompt"]]] + [[int(t) for t in rng.integers(0, 128256, n)] for n in lens[1:]]
-    with BatchEngine(bf16_path, n_seq=len(prompts), max_seq_len=256) as eng:
-        last, ids = _run_batch(eng, prompts, GEN)
-        positions = [eng.pos(b) for b in range(len(prompts))]
+@pytest.fixture(scope="module", params=["split", "stream"])
+def mixed_run(bf16_path, golden, request):
+    """Six rows (split attention is what 6 rows select; the streaming kernel is forced for the second
+    parametrisation)."""
+    import os
+    old = os.environ.get("CUDALLM_BATCH_ATTN")
+    os.environ["CUDALLM_BATCH_ATTN"] = {"split": "2", "stream": "1"}[request.param]
+    try:
+        g = golden("full_bf16_fp16")
+        rng = np.random.default_rng(1234)
+        lens = [len(g["prompt"]), 5, 17, 1, 40, 23]
+        prompts = [[int(t) for t in g["prompt"]]] + [[int(t) for t in rng.integers(0, 128256, n)] for n in lens[1:]]
+        with BatchEngine(bf16_path, n_seq=len(prompts), max_seq_len=256) as eng:
+            last, ids = _run_batch(eng, prompts, GEN)
+            positions = [eng.pos(b) for b in range(len(prompts))]
+    finally:
+        if old is None:
+            del os.environ["CUDALLM_BATCH_ATTN"]
+        else:
+            os.environ["CUDALLM_BATCH_ATTN"] = old
     return {"prompts": prompts, "last": last, "ids": ids, "pos": positions, "golden": g}
 
 
@@ -118,10 +129,12 @@ def test_positions_advance_per_step(mixed_run):
     assert mixed_run["pos"] == [total] * len(mixed_run["prompts"])
 
 
-def test_rows_independent_and_deterministic(bf16_path):
+@pytest.mark.parametrize("attn", ["split", "stream"])
+def test_rows_independent_and_deterministic(bf16_path, monkeypatch, attn):
     """Rows 0 and 2 get the same tokens, row 1 others: rows 0 and 2 agree bitwise at every step; resetting
     row 1 alone and feeding it row 0's tokens reproduces row 0 bitwise; graph replay equals direct
     launches bitwise."""
+    monkeypatch.setenv("CUDALLM_BATCH_ATTN", {"split": "2", "stream": "1"}[attn])
     rng = np.random.default_rng(7)
     a = [int(t) for t in rng.integers(0, 128256, 12)]
     b = [int(t) for t in rng.integers(0, 128256, 12)]
@@ -163,9 +176,12 @@ def test_full_batch_sampled_rows_match_batch1(bf16_path):
         assert int(nxt[r]) == int(np.argmax(ref)) or _margin(ref) < MARGIN
 
 
-def test_context_crossing_graph_tile_groups(bf16_path):
-    """300 teacher-forced steps (the attention grid grows at 256 tokens and the graph is re-captured):
-    logits at steps 255, 256 and 299 against the batch-1 engine on the same tokens."""
+@pytest.mark.parametrize("attn", ["split", "stream"])
+def test_context_crossing_graph_tile_groups(bf16_path, monkeypatch, attn):
+    """300 teacher-forced steps (the split attention's grid grows at 256 tokens and the graph is
+    re-captured; the streaming attention walks 5 tiles through its 4-deep copy ring): logits at steps 255,
+    256 and 299 against the batch-1 engine on the same tokens."""
+    monkeypatch.setenv("CUDALLM_BATCH_ATTN", {"split": "2", "stream": "1"}[attn])
     rng = np.random.default_rng(5)
     toks = rng.integers(0, 128256, (2, 300)).astype(np.int32)
     check = (255, 256, 299)
@@ -187,7 +203,9 @@ def test_context_crossing_graph_tile_groups(bf16_path):
                     one.step_async(int(toks[r, i]))
 
 
-def test_bf16_kv_cache(bf16_path):
+@pytest.mark.parametrize("attn", ["split", "stream"])
+def test_bf16_kv_cache(bf16_path, monkeypatch, attn):
+    monkeypatch.setenv("CUDALLM_BATCH_ATTN", {"split": "2", "stream": "1"}[attn])
     rng = np.random.default_rng(11)
     toks = rng.integers(0, 128256, (2, 20)).astype(np.int32)
     with BatchEngine(bf16_path, n_seq=2, max_seq_len=128, kv_dtype="bf16") as eng:
