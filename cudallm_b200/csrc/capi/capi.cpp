@@ -6,6 +6,7 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <cstring>
 #include <string>
 
@@ -524,15 +525,15 @@ int cudallm_kernel_gemm(const unsigned short* w, const unsigned short* x, const 
                         int batch, int ksplit, int epilogue) {
     return guarded([&] {
         require(w && x && y, "cudallm_kernel_gemm: null argument");
-        require(n > 0 && k >= 64 && k % 64 == 0 && batch >= 1 && batch <= cudallm::kBatchMax && ksplit >= 1 && ksplit <= k / 64,
-                "cudallm_kernel_gemm: bad shape (batch 1..64, k a multiple of 64, ksplit <= k / 64)");
+        require(n > 0 && k >= 64 && k % 64 == 0 && batch >= 1 && batch <= cudallm::kBatchMax && ksplit >= 1 &&
+                    ksplit <= std::min(16, k / 64),
+                "cudallm_kernel_gemm: bad shape (batch 1..64, k a multiple of 64, ksplit <= min(16, k / 64))");
         require(epilogue >= 0 && epilogue <= 2 && (epilogue != 2 || n % 2 == 0), "cudallm_kernel_gemm: bad epilogue");
         const size_t wb = static_cast<size_t>(n) * k * 2, xb = static_cast<size_t>(batch) * k * 2;
         const size_t plane = static_cast<size_t>(cudallm::kBatchMax) * k * 2;
         const int n_out = epilogue == 2 ? n / 2 : n;
         const size_t yb = static_cast<size_t>(batch) * n_out * sizeof(float);
-        DevBuf dw(wb), dx(2 * plane), dpart(static_cast<size_t>(ksplit) * batch * n * sizeof(float)), dy(yb),
-            derr(sizeof(unsigned));
+        DevBuf dw(wb), dx(2 * plane), dy(yb), derr(sizeof(unsigned));
         dw.upload(w, wb);
         // Activation planes [2][64][k]: x in the hi plane, x_lo (or zeros) in the lo plane, unused rows zero.
         CLLM_CUDA(cudaMemset(dx.as<void>(), 0, 2 * plane));
@@ -540,10 +541,19 @@ int cudallm_kernel_gemm(const unsigned short* w, const unsigned short* x, const 
         if (x_lo) CLLM_CUDA(cudaMemcpy(dx.as<uint8_t>() + plane, x_lo, xb, cudaMemcpyHostToDevice));
         dy.upload(y, yb);  // ADD accumulates into y
         CLLM_CUDA(cudaMemset(derr.as<void>(), 0, sizeof(unsigned)));
-        cudallm::launch_gemm_bf16(dw.as<__nv_bfloat16>(), n, k, dx.as<__nv_bfloat16>(), batch, ksplit, dpart.as<float>(),
-                                  derr.as<unsigned>(), 0);
-        cudallm::launch_gemm_reduce(dpart.as<float>(), ksplit, batch, n, static_cast<cudallm::GemmEpilogue>(epilogue),
-                                    dy.as<float>(), nullptr, 0);
+        cudallm::GemmEpi epi;
+        epi.kind = static_cast<cudallm::GemmEpilogue>(epilogue);
+        epi.y = dy.as<float>();
+        const __nv_bfloat16* wdev = dw.as<__nv_bfloat16>();
+        DevBuf dwi(epilogue == 2 ? wb : 0);
+        if (epilogue == 2) {
+            // The SwiGLU epilogue takes gate/up rows interleaved per 128-row tile, as the batched engine
+            // lays them out.
+            require(n % 128 == 0, "cudallm_kernel_gemm: SWIGLU needs n % 128 == 0");
+            cudallm::interleave_gate_up(wdev, dwi.as<__nv_bfloat16>(), n / 2, k, 0);
+            wdev = dwi.as<__nv_bfloat16>();
+        }
+        cudallm::launch_gemm(wdev, n, k, dx.as<__nv_bfloat16>(), batch, ksplit, epi, derr.as<unsigned>(), 0);
         sync_and_check();
         unsigned e = 0;
         derr.download(&e, sizeof(e));

@@ -29,10 +29,6 @@ void alloc_zero(T** p, size_t count) {
 // row's context return at once.
 constexpr int kTileGroup = 4;
 
-// K split of a GEMM with `mtiles` 128-row tiles and `chunks` 64-column K chunks: as many grid rows as keep
-// every SM busy with one CTA.
-int pick_ksplit(int mtiles, int chunks, int sms) { return std::max(1, std::min(chunks, sms / std::max(1, mtiles))); }
-
 }  // namespace
 
 BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : opts_(opts) {
@@ -54,44 +50,52 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
     } else {
         CLLM_CUDA(cudaGetDevice(&device_));
     }
+    if (const char* env = std::getenv("CUDALLM_BATCH_PDL")) opts_.pdl = std::atoi(env) != 0;
+    if (const char* env = std::getenv("CUDALLM_BATCH_ATTN")) opts_.attn_mode = std::atoi(env);
+    if (opts_.attn_mode < 0 || opts_.attn_mode > 2) throw ArgError("attention mode must be 0, 1 or 2");
     DeviceGuard guard(device_);
     weights_ = std::make_unique<Weights>(file);
     const ModelConfig& c = weights_->config();
     max_seq_ = opts_.max_seq_len ? opts_.max_seq_len : c.max_seq_len;
     host_pos_.assign(opts_.n_seq, 0);
-    if (const char* env = std::getenv("CUDALLM_BATCH_PDL")) opts_.pdl = std::atoi(env) != 0;
-    if (const char* env = std::getenv("CUDALLM_BATCH_ATTN")) opts_.attn_mode = std::atoi(env);
-    if (opts_.attn_mode < 0 || opts_.attn_mode > 2) throw ArgError("attention mode must be 0, 1 or 2");
     try {
         CLLM_CUDA(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking));
         int sms = 0;
         CLLM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device_));
         const int H = c.hidden, I = c.inter, V = c.vocab, NH = c.n_heads, NKV = c.n_kv_heads, D = c.head_dim;
         const int QKV = (NH + 2 * NKV) * D;
-        auto mt = [](int n) { return (n + 127) / 128; };
+        CLLM_CHECK(H % kGemmTileRows == 0 && H / kGemmTileRows <= 16 && I % (kGemmTileRows / 2) == 0 &&
+                       QKV % kGemmTileRows == 0 && D == 64 && NH * D == H,
+                   "batched decode: unsupported model shape");
         // One streaming CTA per (KV head, sequence) once that fills the SMs; fewer sequences split their
         // contexts over more CTAs.
         attn_stream_ = opts_.attn_mode == 1 || (opts_.attn_mode == 0 && opts_.n_seq * NKV >= sms);
-        ks_qkv_ = pick_ksplit(mt(QKV), H / 64, sms);
-        ks_wo_ = pick_ksplit(mt(H), H / 64, sms);
-        ks_gu_ = pick_ksplit(mt(2 * I), H / 64, sms);
-        ks_down_ = pick_ksplit(mt(H), I / 64, sms);
+        ks_qkv_ = gemm_pick_ksplit(QKV, H);
+        ks_wo_ = gemm_pick_ksplit(H, NH * D);
+        ks_gu_ = gemm_pick_ksplit(2 * I, H);
+        ks_down_ = gemm_pick_ksplit(H, I);
+        lm_tiles_ = (V + kGemmTileRows - 1) / kGemmTileRows;
+        if (std::getenv("CUDALLM_BATCH_VERBOSE")) {
+            std::fprintf(stderr, "cudallm batch: K splits qkv %d wo %d gate/up %d down %d; attention %s; pdl %d\n", ks_qkv_, ks_wo_,
+                         ks_gu_, ks_down_, attn_stream_ ? "stream" : "split", opts_.pdl ? 1 : 0);
+        }
         const size_t B = kBatchMax;
-        part_floats_ = std::max({static_cast<size_t>(ks_qkv_) * B * QKV, static_cast<size_t>(ks_wo_) * B * H,
-                                 static_cast<size_t>(ks_gu_) * B * 2 * I, static_cast<size_t>(ks_down_) * B * H,
-                                 B * static_cast<size_t>(V)});
         alloc_zero(&x_, B * H);
-        alloc_zero(reinterpret_cast<__nv_bfloat16**>(&xn_), 2 * B * std::max(H, NH * D));
+        alloc_zero(reinterpret_cast<__nv_bfloat16**>(&pa_), 2 * B * H);
+        alloc_zero(reinterpret_cast<__nv_bfloat16**>(&pb_), 2 * B * H);
         alloc_zero(reinterpret_cast<__nv_bfloat16**>(&act_), 2 * B * I);
+        alloc_zero(&ssq_, static_cast<size_t>(16) * B);
         alloc_zero(&qkv_, B * QKV);
-        alloc_zero(&part_, part_floats_);
+        alloc_zero(&logits_, B * V);
+        alloc_zero(&am_v_, B * lm_tiles_);
+        alloc_zero(&am_i_, B * lm_tiles_);
         const size_t cache_elems = static_cast<size_t>(opts_.n_seq) * c.n_layers * NKV * max_seq_ * D;
         CLLM_CUDA(cudaMalloc(&k_cache_, cache_elems * 2));
         CLLM_CUDA(cudaMalloc(&v_cache_, cache_elems * 2));
         CLLM_CUDA(cudaMemset(k_cache_, 0, cache_elems * 2));
         CLLM_CUDA(cudaMemset(v_cache_, 0, cache_elems * 2));
-        const size_t slots = static_cast<size_t>(max_seq_ / kAttnTile);
         if (!attn_stream_) {
+            const size_t slots = static_cast<size_t>(max_seq_ / kAttnTile);
             alloc_zero(&att_o_, B * NH * slots * D);
             alloc_zero(&att_ml_, B * NH * slots * 2);
         }
@@ -99,10 +103,21 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
         alloc_zero(&tok_, B);
         alloc_zero(&dpos_, B);
         alloc_zero(&err_, 1);
-        alloc_zero(&am_v_, B * kArgmaxSplit);
-        alloc_zero(&am_i_, B * kArgmaxSplit);
-        alloc_zero(&am_ticket_, B);
         CLLM_CUDA(cudaMemset(tok_in_, 0xff, B * sizeof(int)));  // -1: feed the previous argmax
+        // The gate/up matrices are re-laid out in place so that each 128-row GEMM tile holds 64 gate rows and
+        // the 64 matching up rows (the SwiGLU epilogue needs both); this engine owns its copy of the weights.
+        {
+            const size_t gu_elems = static_cast<size_t>(2) * I * H;
+            __nv_bfloat16* tmp = nullptr;
+            CLLM_CUDA(cudaMalloc(&tmp, gu_elems * 2));
+            for (const LayerWeights& L : weights_->layers) {
+                auto* w = const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(L.w_gate_up.w));
+                interleave_gate_up(w, tmp, I, H, stream_);
+                CLLM_CUDA(cudaMemcpyAsync(w, tmp, gu_elems * 2, cudaMemcpyDeviceToDevice, stream_));
+            }
+            CLLM_CUDA(cudaStreamSynchronize(stream_));
+            CLLM_CUDA(cudaFree(tmp));
+        }
         CLLM_CUDA(cudaDeviceSynchronize());
     } catch (...) {
         free_all();
@@ -118,15 +133,14 @@ void BatchEngine::free_all() noexcept {
     if (graph_) report(cudaGraphDestroy(graph_), "cudaGraphDestroy");
     graph_exec_ = nullptr;
     graph_ = nullptr;
-    void* bufs[] = {x_, xn_, act_, qkv_, part_, k_cache_, v_cache_, att_o_, att_ml_, tok_in_, tok_, dpos_, err_, am_v_, am_i_, am_ticket_};
+    void* bufs[] = {x_,    pa_,      pb_,      act_,   ssq_,    qkv_, logits_, am_v_, am_i_,
+                    k_cache_, v_cache_, att_o_, att_ml_, tok_in_, tok_, dpos_,   err_};
     for (void* b : bufs) {
         if (b) report(cudaFree(b), "cudaFree");
     }
-    x_ = qkv_ = part_ = att_o_ = att_ml_ = am_v_ = nullptr;
-    am_i_ = nullptr;
-    am_ticket_ = nullptr;
-    xn_ = act_ = k_cache_ = v_cache_ = nullptr;
-    tok_in_ = tok_ = dpos_ = nullptr;
+    x_ = ssq_ = qkv_ = logits_ = am_v_ = att_o_ = att_ml_ = nullptr;
+    pa_ = pb_ = act_ = k_cache_ = v_cache_ = nullptr;
+    am_i_ = tok_in_ = tok_ = dpos_ = nullptr;
     err_ = nullptr;
     if (stream_) report(cudaStreamDestroy(stream_), "cudaStreamDestroy");
     stream_ = nullptr;
@@ -176,9 +190,11 @@ void BatchEngine::reset(int seq) {
     CLLM_CUDA(cudaStreamSynchronize(stream_));
 }
 
-// Per row, the operation sequence of wasiqnauman/cudallm src/engine/engine.cpp:181-237 (unfused form:
-// RMSNorm, QKV, RoPE + KV write, attention, o_proj + residual, RMSNorm, gate/up + SwiGLU, down + residual;
-// final RMSNorm, tied lm_head, argmax), with the matvecs as batched GEMMs.
+// Per row, the operation sequence of wasiqnauman/cudallm src/engine/engine.cpp:181-237 (RMSNorm, QKV,
+// RoPE + KV write, attention, o_proj + residual, RMSNorm, gate/up + SwiGLU, down + residual; final
+// RMSNorm, tied lm_head, argmax) as five launches per layer: each GEMM applies the RMSNorm of its input
+// (statistics from the epilogue that produced it, gain folded into the activation planes) and fuses the
+// operations that follow it into its epilogue.
 template <typename KV>
 void BatchEngine::enqueue_layers(int tiles) {
     const ModelConfig& c = config();
@@ -189,37 +205,80 @@ void BatchEngine::enqueue_layers(int tiles) {
     const size_t seq_stride = layer_elems * c.n_layers;
     KV* kc = static_cast<KV*>(k_cache_);
     KV* vc = static_cast<KV*>(v_cache_);
-    auto* xn = static_cast<__nv_bfloat16*>(xn_);
+    auto* pa = static_cast<__nv_bfloat16*>(pa_);
+    auto* pb = static_cast<__nv_bfloat16*>(pb_);
     auto* act = static_cast<__nv_bfloat16*>(act_);
     auto bf = [](const Linear& L) { return static_cast<const __nv_bfloat16*>(L.w); };
     const bool pdl = opts_.pdl;
+    const bool kv_bf16 = opts_.kv == KvType::BF16;
     cudaStream_t s = stream_;
-    launch_embed_rows(static_cast<const uint16_t*>(W.tok_embeddings.w), tok_in_, tok_, x_, B, H, s, pdl);
+    const int tiles_h = H / kGemmTileRows;
+    // x, planes of x * attn_norm[0] and its statistics (one partial).
+    launch_embed_rows(static_cast<const uint16_t*>(W.tok_embeddings.w), tok_in_, tok_, W.layers[0].attn_norm, x_, pa, ssq_, B, H,
+                      s, pdl);
+    int ssq_count = 1;
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerWeights& L = W.layers[l];
         KV* kl = kc + l * layer_elems;
         KV* vl = vc + l * layer_elems;
-        launch_rmsnorm_rows(x_, L.attn_norm, c.rms_eps, xn, B, H, s, pdl);
-        launch_gemm_bf16(bf(L.wqkv), QKV, H, xn, B, ks_qkv_, part_, err_, s, pdl);
-        launch_gemm_reduce(part_, ks_qkv_, B, QKV, GemmEpilogue::STORE, qkv_, nullptr, s, pdl);
-        launch_rope_kv_rows<KV>(qkv_, W.rope_inv_freq, kl, vl, seq_stride, dpos_, B, NH, NKV, D, max_seq_, s, pdl);
+        GemmEpi q;
+        q.kind = GemmEpilogue::QKV_ROPE;
+        q.ssq_in = ssq_;
+        q.ssq_count = ssq_count;
+        q.norm_n = H;
+        q.eps = c.rms_eps;
+        q.q_out = qkv_;
+        q.inv_freq = W.rope_inv_freq;
+        q.k_cache = kl;
+        q.v_cache = vl;
+        q.seq_stride = seq_stride;
+        q.pos = dpos_;
+        q.nh = NH;
+        q.nkv = NKV;
+        q.max_seq = max_seq_;
+        q.kv_bf16 = kv_bf16;
+        launch_gemm(bf(L.wqkv), QKV, H, pa, B, ks_qkv_, q, err_, s, pdl);
         if (attn_stream_) {
-            launch_attention_rows_stream<KV>(qkv_, kl, vl, seq_stride, dpos_, xn, B, NH, NKV, max_seq_, err_, s, pdl);
+            launch_attention_rows_stream<KV>(qkv_, kl, vl, seq_stride, dpos_, pb, B, NH, NKV, max_seq_, err_, s, pdl);
         } else {
-            launch_attention_rows<KV>(qkv_, kl, vl, seq_stride, dpos_, tiles * kAttnTile, att_o_, att_ml_, xn, B, NH, NKV,
+            launch_attention_rows<KV>(qkv_, kl, vl, seq_stride, dpos_, tiles * kAttnTile, att_o_, att_ml_, pb, B, NH, NKV,
                                       max_seq_, s, pdl);
         }
-        launch_gemm_bf16(bf(L.wo), H, NH * D, xn, B, ks_wo_, part_, err_, s, pdl);
-        launch_gemm_reduce(part_, ks_wo_, B, H, GemmEpilogue::ADD, x_, nullptr, s, pdl);
-        launch_rmsnorm_rows(x_, L.ffn_norm, c.rms_eps, xn, B, H, s, pdl);
-        launch_gemm_bf16(bf(L.w_gate_up), 2 * I, H, xn, B, ks_gu_, part_, err_, s, pdl);
-        launch_gemm_reduce(part_, ks_gu_, B, 2 * I, GemmEpilogue::SWIGLU, nullptr, act, s, pdl);
-        launch_gemm_bf16(bf(L.w_down), H, I, act, B, ks_down_, part_, err_, s, pdl);
-        launch_gemm_reduce(part_, ks_down_, B, H, GemmEpilogue::ADD, x_, nullptr, s, pdl);
+        GemmEpi o;
+        o.kind = GemmEpilogue::ADD;
+        o.y = x_;
+        o.planes = pa;
+        o.gain = L.ffn_norm;
+        o.ssq_out = ssq_;
+        launch_gemm(bf(L.wo), H, NH * D, pb, B, ks_wo_, o, err_, s, pdl);
+        GemmEpi g;
+        g.kind = GemmEpilogue::SWIGLU;
+        g.ssq_in = ssq_;
+        g.ssq_count = tiles_h;
+        g.norm_n = H;
+        g.eps = c.rms_eps;
+        g.planes = act;
+        launch_gemm(bf(L.w_gate_up), 2 * I, H, pa, B, ks_gu_, g, err_, s, pdl);
+        GemmEpi d;
+        d.kind = GemmEpilogue::ADD;
+        d.y = x_;
+        d.planes = pa;
+        d.gain = l + 1 < c.n_layers ? W.layers[l + 1].attn_norm : W.final_norm;
+        d.ssq_out = ssq_;
+        launch_gemm(bf(L.w_down), H, I, act, B, ks_down_, d, err_, s, pdl);
+        ssq_count = tiles_h;
     }
-    launch_rmsnorm_rows(x_, W.final_norm, c.rms_eps, xn, B, H, s, pdl);
-    launch_gemm_bf16(bf(W.tok_embeddings), V, H, xn, B, 1, part_, err_, s, pdl);  // logits = part_ [B][V]
-    launch_argmax_rows(part_, V, am_v_, am_i_, am_ticket_, tok_, dpos_, B, s, pdl);
+    GemmEpi lm;
+    lm.kind = GemmEpilogue::LOGITS;
+    lm.ssq_in = ssq_;
+    lm.ssq_count = ssq_count;
+    lm.norm_n = H;
+    lm.eps = c.rms_eps;
+    lm.y = logits_;
+    lm.am_v = am_v_;
+    lm.am_i = am_i_;
+    launch_gemm(bf(W.tok_embeddings), V, H, pa, B, 1, lm, err_, s, pdl);
+    launch_argmax_tiles(am_v_, am_i_, lm_tiles_, tok_, dpos_, B, s, pdl);
 }
 
 void BatchEngine::enqueue_step(int tiles) {
@@ -291,7 +350,7 @@ void BatchEngine::step(const int* tokens, int* next_out, float* logits_out) {
     for (int b = 0; b < B; ++b) host_pos_[b] += 1;
     if (!next_out && !logits_out) return;
     if (logits_out) {
-        CLLM_CUDA(cudaMemcpyAsync(logits_out, part_, sizeof(float) * B * config().vocab, cudaMemcpyDeviceToHost, stream_));
+        CLLM_CUDA(cudaMemcpyAsync(logits_out, logits_, sizeof(float) * B * config().vocab, cudaMemcpyDeviceToHost, stream_));
     }
     if (next_out) CLLM_CUDA(cudaMemcpyAsync(next_out, tok_, sizeof(int) * B, cudaMemcpyDeviceToHost, stream_));
     synchronize();

@@ -4,7 +4,8 @@
 // (src/engine/engine.cpp:181-237) on its own token, position and KV cache, so a row's logits match what
 // the batch-1 engine computes for that sequence up to fp32 summation order. The weight matvecs become
 // GEMMs on the tcgen05 tensor cores (every weight byte is read once per step for the whole batch);
-// RoPE, attention, RMSNorm and argmax run per row. Several GPUs run one engine each on their own
+// RMSNorm, residual adds, RoPE with the KV-cache write, SwiGLU and the logits' argmax partials are fused
+// into the GEMM epilogues; attention runs per row. Several GPUs run one engine each on their own
 // sequence groups (no collective).
 #pragma once
 
@@ -73,27 +74,28 @@ private:
     int graph_tiles_ = 0;  // attention tiles the captured graph covers (split attention only)
     bool attn_stream_ = true;
 
-    // Per-operation K splits (grid rows of the GEMM), chosen to fill the SMs.
+    // Per-operation K splits (cluster sizes of the GEMMs), chosen to fill the SMs.
     int ks_qkv_ = 1, ks_wo_ = 1, ks_gu_ = 1, ks_down_ = 1;
+    int lm_tiles_ = 0;
 
     float* x_ = nullptr;              // residual stream [64][hidden] fp32
-    void* xn_ = nullptr;              // activation planes [2][64][hidden] bf16 (normed x, attention output)
-    void* act_ = nullptr;             // activation planes [2][64][inter] bf16 (SwiGLU output)
-    float* qkv_ = nullptr;            // [64][qkv rows]
-    float* part_ = nullptr;           // GEMM partials; the lm_head's logits [64][vocab]
+    void* pa_ = nullptr;              // activation planes [2][64][hidden] bf16: RMSNorm inputs (x * gain)
+    void* pb_ = nullptr;              // activation planes [2][64][hidden] bf16: attention output
+    void* act_ = nullptr;             // activation planes [2][64][inter] bf16: SwiGLU output
+    float* ssq_ = nullptr;            // RMSNorm statistics: partial sums of x^2 [<= 256][64]
+    float* qkv_ = nullptr;            // [64][qkv rows] (rotated q heads)
+    float* logits_ = nullptr;         // [64][vocab]
+    float* am_v_ = nullptr;           // per-tile argmax partials of the logits [64][vocab / 128]
+    int* am_i_ = nullptr;
     void* k_cache_ = nullptr;         // [seq][layer][kv head][max_seq][64]
     void* v_cache_ = nullptr;
-    float* att_o_ = nullptr;          // attention partials [64][heads][max_seq/64][64]
+    float* att_o_ = nullptr;          // split attention partials [64][heads][max_seq/64][64]
     float* att_ml_ = nullptr;         // [64][heads][max_seq/64][2]
     int* tok_in_ = nullptr;           // device copy of the step's fed tokens
     int* tok_ = nullptr;              // [64] last argmax per sequence
     int* dpos_ = nullptr;             // [64] position per sequence
     unsigned* err_ = nullptr;         // device error word
-    float* am_v_ = nullptr;           // argmax slice results [64][kArgmaxSplit]
-    int* am_i_ = nullptr;
-    unsigned* am_ticket_ = nullptr;   // [64] per-row tickets (zero between launches)
     bool tok_in_fed_ = false;         // tok_in_ holds fed tokens (not all -1)
-    size_t part_floats_ = 0;
 };
 
 }  // namespace cudallm

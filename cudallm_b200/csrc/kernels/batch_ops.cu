@@ -34,16 +34,32 @@ struct PlaneDst {
 };
 
 // Token of row b: tok_in[b] when >= 0 (fed by the caller), else the previous step's argmax tok[b].
-// x[b][j] = emb[token][j] (bf16 weights), one block per row.
-__global__ void embed_rows_kernel(const uint16_t* __restrict__ emb, const int* __restrict__ tok_in, const int* tok,
-                                  float* __restrict__ x, int hidden) {
+// x[b][j] = emb[token][j] (bf16 weights); planes of x[b][j] * gain[j] (the first RMSNorm's input) and
+// ssq[b] = sum_j x[b][j]^2 (reduced in a fixed order), one 256-thread block per row.
+__global__ void __launch_bounds__(256) embed_rows_kernel(const uint16_t* __restrict__ emb, const int* __restrict__ tok_in,
+                                                         const int* tok, const float* __restrict__ gain, float* __restrict__ x,
+                                                         __nv_bfloat16* __restrict__ planes, float* __restrict__ ssq,
+                                                         int hidden) {
     grid_dep_launch();
     grid_dep_wait();
+    __shared__ float red[8];
     const int b = blockIdx.x;
     const int t = tok_in[b] >= 0 ? tok_in[b] : tok[b];
     const uint16_t* row = emb + static_cast<size_t>(t) * hidden;
+    float ss = 0.f;
     for (int j = threadIdx.x; j < hidden; j += blockDim.x) {
-        x[static_cast<size_t>(b) * hidden + j] = __uint_as_float(static_cast<uint32_t>(row[j]) << 16);
+        const float v = __uint_as_float(static_cast<uint32_t>(row[j]) << 16);
+        x[static_cast<size_t>(b) * hidden + j] = v;
+        ss = fmaf(v, v, ss);
+        store_planes(planes, static_cast<size_t>(kBatchMax) * hidden, static_cast<size_t>(b) * hidden + j, v * gain[j]);
+    }
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float s2 = 0.f;
+        for (int i = 0; i < 8; ++i) s2 += red[i];
+        ssq[b] = s2;
     }
 }
 
@@ -174,7 +190,8 @@ __global__ void __launch_bounds__(kRowAttThreads) attention_rows_stream_kernel(c
         fence_barrier_init();
     }
     __syncthreads();
-    grid_dep_wait();  // q, the new k / v and pos come from the kernels before
+    // pos and the cached tokens before pos were written by earlier steps, so tiles that end before pos
+    // are fetched before waiting for the kernel that produces q and the new token's k / v.
     const int ctx = pos_v[b] + 1;
     const int n_tiles = (ctx + kAttnTile - 1) / kAttnTile;
     const KV* kg = k_cache + seq_stride * b + static_cast<size_t>(h) * max_seq * kHd;
@@ -187,8 +204,14 @@ __global__ void __launch_bounds__(kRowAttThreads) attention_rows_stream_kernel(c
         bulk_load(&sm.k[st][0][0], kg + static_cast<size_t>(t) * kAttnTile * kHd, bytes, &sm.full[st], pol);
         bulk_load(&sm.v[st][0][0], vg + static_cast<size_t>(t) * kAttnTile * kHd, bytes, &sm.full[st], pol);
     };
+    const int first = min(kRowAttStages, n_tiles);
+    const int early = min(first, (ctx - 1) / kAttnTile);  // tiles wholly before pos
     if (tid == 0) {
-        for (int t = 0; t < min(kRowAttStages, n_tiles); ++t) issue(t);
+        for (int t = 0; t < early; ++t) issue(t);
+    }
+    grid_dep_wait();  // q, the new k / v come from the kernel before
+    if (tid == 0) {
+        for (int t = early; t < first; ++t) issue(t);
     }
     // q of the 4 heads, dims 8*c8 .. 8*c8+7, pre-scaled pairs.
     float2 q[kGqa][4];
@@ -419,12 +442,53 @@ __global__ void __launch_bounds__(1024) argmax_rows_kernel(const float* __restri
     }
 }
 
+// grid batch, block 256: tok[b] = the best of row b's per-tile (value, index) partials (lowest index on
+// ties; all-NaN row -> 0), pos[b] += 1.
+__global__ void __launch_bounds__(256) argmax_tiles_kernel(const float* __restrict__ am_v, const int* __restrict__ am_i,
+                                                           int n_tiles, int* tok, int* pos_v) {
+    grid_dep_launch();
+    grid_dep_wait();
+    __shared__ float sv[8];
+    __shared__ int si[8];
+    const int b = blockIdx.x;
+    float bv = -FLT_MAX;
+    int bi = INT_MAX;
+    for (int t = threadIdx.x; t < n_tiles; t += 256) {
+        better(bv, bi, am_v[static_cast<size_t>(b) * n_tiles + t], am_i[static_cast<size_t>(b) * n_tiles + t]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        better(bv, bi, ov, oi);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        sv[threadIdx.x >> 5] = bv;
+        si[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float v = sv[0];
+        int i = si[0];
+        for (int w = 1; w < 8; ++w) better(v, i, sv[w], si[w]);
+        tok[b] = i == INT_MAX ? 0 : i;
+        pos_v[b] += 1;
+    }
+}
+
 }  // namespace
 
-void launch_embed_rows(const uint16_t* emb, const int* tok_in, const int* tok, float* x, int batch, int hidden, cudaStream_t stream,
-                       bool pdl) {
-    CLLM_CHECK(emb && tok_in && tok && x && batch >= 1, "launch_embed_rows: bad arguments");
-    launch_kernel(embed_rows_kernel, dim3(batch), dim3(256), 0, stream, pdl, emb, tok_in, tok, x, hidden);
+void launch_argmax_tiles(const float* am_v, const int* am_i, int n_tiles, int* tok, int* pos, int batch, cudaStream_t stream,
+                         bool pdl) {
+    CLLM_CHECK(am_v && am_i && tok && pos && batch >= 1 && n_tiles >= 1, "launch_argmax_tiles: bad arguments");
+    launch_kernel(argmax_tiles_kernel, dim3(batch), dim3(256), 0, stream, pdl, am_v, am_i, n_tiles, tok, pos);
+}
+
+void launch_embed_rows(const uint16_t* emb, const int* tok_in, const int* tok, const float* gain, float* x,
+                       __nv_bfloat16* planes, float* ssq, int batch, int hidden, cudaStream_t stream, bool pdl) {
+    CLLM_CHECK(emb && tok_in && tok && gain && x && planes && ssq && batch >= 1 && batch <= kBatchMax,
+               "launch_embed_rows: bad arguments");
+    launch_kernel(embed_rows_kernel, dim3(batch), dim3(256), 0, stream, pdl, emb, tok_in, tok, gain, x, planes, ssq, hidden);
 }
 
 void launch_rmsnorm_rows(const float* x, const float* w, float eps, __nv_bfloat16* out, int batch, int n, cudaStream_t stream,

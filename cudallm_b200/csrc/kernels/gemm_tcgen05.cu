@@ -1,51 +1,67 @@
-// Batched decode GEMM on the sm_100a tensor cores: part[ks][b][n] = sum over the ks-th K range of
-// X[b][k] * W[n][k], W the [N][K] bf16 weight matrix (row-major, as stored in the .cudallm file), X the
-// fp32 activations of up to 64 sequences carried as two bf16 planes, X = hi + lo (hi = bf16(X), lo =
-// bf16(X - hi)), so the product keeps ~16 mantissa bits of the fp32 activation, like the batch-1 path's
-// fp32 vectors. Weight rows are the MMA's M side: a CTA computes 128 weight rows x 64 batch columns
-// (tcgen05.mma.cta_group::1.kind::f16, M = 128, N = 64, K = 16 per instruction; one MMA per plane into the
-// same accumulator) in a 64-column fp32 TMEM accumulator, so every weight element is read from HBM once
-// per step and used for the whole batch. Operands arrive by 2D TMA tensor loads (128-byte swizzle, no
-// multicast) through a 7-stage ring of (W 128 x 64, X 2 x 64 x 64) tiles; one thread issues the loads,
-// one thread the MMAs, and the 4 warps read the accumulator back (warp w owns TMEM lanes 32w..32w+31).
-// K ranges per grid row (blockIdx.y) spread short operations over the SMs; gemm_reduce adds the ranges in
-// order. The kernels take part in programmatic dependent launch: a GEMM starts streaming its weights
-// while the kernel before it finishes and waits for it only before loading the activations.
+// Batched decode GEMM on the sm_100a tensor cores with fused epilogues. s[b][j] = sum_k X[b][k] * W[j][k]:
+// W the [N][K] bf16 weight matrix (row-major, as stored in the .cudallm file), X the fp32 activations of
+// up to 64 sequences carried as two bf16 planes, X = hi + lo (hi = bf16(X), lo = bf16(X - hi)), so the
+// product keeps ~16 mantissa bits of the fp32 activation, like the batch-1 path's fp32 vectors.
+//
+// Mainloop: weight rows are the MMA's M side; a CTA computes 128 weight rows x 64 batch columns
+// (tcgen05.mma.cta_group::1.kind::f16, M = 128, N = 64, K = 16 per instruction; one MMA per plane into
+// the same accumulator) in a 64-column fp32 TMEM accumulator, so every weight element is read from HBM
+// once per step and used for the whole batch. Operands arrive by 2D TMA tensor loads (128-byte swizzle,
+// no multicast) through a 7-stage ring of (W 128 x 64, X 2 x 64 x 64) tiles; one thread issues the loads,
+// one thread the MMAs. The CTAs of one 128-row tile split K (grid rows = cluster ranks) and start at
+// different chunks of their range, so they do not all read the same activation tile at once.
+//
+// Epilogue: the accumulator goes from TMEM to shared memory; the tile's cluster adds the K-split partial
+// sums through distributed shared memory (rank r reduces slice r of the tile, peers added in rank order,
+// so results do not depend on timing) and applies the fused epilogue (GemmEpi): residual add with the
+// next RMSNorm's statistics and activation planes, SwiGLU into activation planes, RoPE with the KV-cache
+// write, or logits with per-tile argmax partials. Programmatic dependent launch: a GEMM starts streaming
+// its weights while the kernel before it finishes and waits for it only before loading activations.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <cfloat>
+#include <climits>
 #include <cstdint>
+#include <cstdlib>
 #include <map>
 #include <mutex>
 #include <tuple>
 
 #include "common/check.h"
 #include "kernels/batch.h"
-#include "kernels/launch.cuh"
 #include "kernels/tcgen05.cuh"
 
 namespace cudallm {
 namespace {
 
-constexpr int kGM = 128;            // weight rows per CTA (MMA M)
+constexpr int kGM = kGemmTileRows;  // weight rows per CTA (MMA M)
 constexpr int kGN = kBatchMax;      // batch columns (MMA N)
 constexpr int kGK = 64;             // K per stage: one 128-byte swizzled row
 constexpr int kXRows = 2 * kGN;     // hi plane rows 0..63, lo plane rows 64..127
-constexpr int kGStages = 7;
+constexpr int kGStages = 7;        // deep ring: one CTA per SM
+constexpr int kGStagesLogits = 3;  // shallow ring: two CTAs per SM, one's epilogue overlaps the other's stream
 constexpr int kGThreads = 128;
+constexpr int kMaxKsplit = 16;
 constexpr int kWTileBytes = kGM * kGK * 2;     // 16 KiB
 constexpr int kXTileBytes = kXRows * kGK * 2;  // 16 KiB
 constexpr int kXPlaneBytes = kGN * kGK * 2;    // lo plane offset inside an X tile (1024-byte aligned)
-constexpr int kGSmemBytes = 1024 + kGStages * (kWTileBytes + kXTileBytes) + 256;
+constexpr int kCtrlBytes = 1024;  // barriers, TMEM slot, inv_rms[64], pos[64], inv_freq[32]
+constexpr int ring_bytes(int stages) { return stages * (kWTileBytes + kXTileBytes); }
+constexpr int smem_bytes(int stages) { return 1024 + ring_bytes(stages) + kCtrlBytes; }
 constexpr uint64_t kGemmWaitNs = 1000000000ull;
+static_assert(smem_bytes(kGStages) <= 232448, "GEMM shared memory above the per-block limit");
+static_assert(2 * smem_bytes(kGStagesLogits) <= 228 * 1024 - 2 * 1024, "two lm_head CTAs must fit an SM");
+static_assert(ring_bytes(kGStagesLogits) >= 2 * kGN * kGM * 4, "the epilogue scratch lives in the ring");
 
 struct GemmArgs {
-    float* part;                // [ksplit][batch][n]
-    int n, batch, chunks, ksplit;  // chunks: 64-column K chunks in total
-    unsigned* err;              // error word (set on a wait timeout)
+    int n, batch, chunks, ksplit, n_tiles;  // chunks: 64-column K chunks in total
+    unsigned* err;                          // error word (set on a wait timeout)
+    GemmEpi epi;
 };
 
 // Bounded wait on an mbarrier phase; false (and the error word set) after kGemmWaitNs.
@@ -65,29 +81,92 @@ __device__ bool gemm_wait(uint64_t* bar, uint32_t parity, unsigned* err) {
     }
 }
 
+__device__ __forceinline__ void store_planes_g(__nv_bfloat16* p, size_t plane, size_t i, float v) {
+    const __nv_bfloat16 hi = __float2bfloat16_rn(v);
+    p[i] = hi;
+    p[plane + i] = __float2bfloat16_rn(v - __bfloat162float(hi));
+}
+
+__device__ __forceinline__ float silu_g(float x) { return x / (1.f + __expf(-x)); }
+
+template <typename KV>
+__device__ __forceinline__ KV to_cache(float v);
+template <>
+__device__ __forceinline__ __half to_cache<__half>(float v) {
+    return __float2half_rn(v);
+}
+template <>
+__device__ __forceinline__ __nv_bfloat16 to_cache<__nv_bfloat16>(float v) {
+    return __float2bfloat16_rn(v);
+}
+
+// The tile's accumulator in shared memory, column-major ([batch column][128 rows] fp32), summed over
+// the cluster's K-split ranks in rank order. sum4 returns rows row..row+3 of one column: the loads from
+// every rank are issued before any is added, so the distributed-shared-memory latency is paid once.
+struct TileSum {
+    const float* own;
+    uint32_t own_saddr;
+    uint32_t ks;
+    __device__ __forceinline__ float4 sum4(int col, int row) const {
+        const int idx = col * kGM + row;
+        if (ks == 1) return *reinterpret_cast<const float4*>(own + idx);
+        float4 part[kMaxKsplit];
+#pragma unroll
+        for (uint32_t r = 0; r < kMaxKsplit; ++r) {
+            if (r < ks) part[r] = ld_peer_f32x4(peer_smem(own_saddr + 4u * idx, r));
+        }
+        float4 s = part[0];
+#pragma unroll
+        for (uint32_t r = 1; r < kMaxKsplit; ++r) {
+            if (r < ks) {
+                s.x += part[r].x;
+                s.y += part[r].y;
+                s.z += part[r].z;
+                s.w += part[r].w;
+            }
+        }
+        return s;
+    }
+};
+
+__device__ __forceinline__ float f4get(const float4& v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+
+__device__ __forceinline__ void argmax_better(float& bv, int& bi, float v, int i) {
+    if (v > bv || (v == bv && i < bi)) {
+        bv = v;
+        bi = i;
+    }
+}
+
+template <int EPI, typename KV, int ST>
 __global__ void __launch_bounds__(kGThreads, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, GemmArgs a) {
+    gemm_kernel(const __grid_constant__ CUtensorMap wmap, const __grid_constant__ CUtensorMap xmap, const GemmArgs a) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* wt = smem;
-    uint8_t* xt = smem + kGStages * kWTileBytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(xt + kGStages * kXTileBytes);
-    uint64_t* empty = full + kGStages;
-    uint64_t* done = empty + kGStages;
+    uint8_t* xt = smem + ST * kWTileBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + ring_bytes(ST));
+    uint64_t* empty = full + ST;
+    uint64_t* done = empty + ST;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * kGM;
+    float* inv_rms = reinterpret_cast<float*>(smem + ring_bytes(ST) + 256);
+    int* pos_s = reinterpret_cast<int*>(smem + ring_bytes(ST) + 512);          // QKV_ROPE: pos[64]
+    float* freq_s = reinterpret_cast<float*>(smem + ring_bytes(ST) + 768);     // QKV_ROPE: inv_freq[32]
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+    const int tile = blockIdx.x;
+    const int n0 = tile * kGM;
+    const GemmEpi& e = a.epi;
     // This grid row's K chunks: [c0, c1), an even split of the chunks over the ksplit rows.
     const int c0 = static_cast<int>(static_cast<long long>(blockIdx.y) * a.chunks / a.ksplit);
     const int c1 = static_cast<int>(static_cast<long long>(blockIdx.y + 1) * a.chunks / a.ksplit);
     const int nch = c1 - c0;
-    // CTAs of one grid row start at different chunks of their K range (and wrap around), so that at any
-    // moment they read different activation tiles instead of all hitting the same L2 lines.
+    // CTAs start at different chunks of their K range (and wrap around), so that at any moment they read
+    // different activation tiles instead of all hitting the same L2 lines.
     const int rot = static_cast<int>(blockIdx.x % static_cast<unsigned>(nch));
     auto chunk_x = [&](int i) { return (c0 + (i + rot) % nch) * kGK; };
     grid_dep_launch();
-    if (threadIdx.x == 0) {
-        for (int s = 0; s < kGStages; ++s) {
+    if (tid == 0) {
+        for (int s = 0; s < ST; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -103,10 +182,10 @@ __global__ void __launch_bounds__(kGThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0 && lane == 0) {
-        // TMA producer: chunk i of this CTA's K range into stage i % kGStages. The weight tiles of the
+        // TMA producer: chunk i of this CTA's K range into stage i % ST. The weight tiles of the
         // first ring pass do not depend on the previous kernel and are issued before waiting for it.
         const uint64_t pol = l2_policy_evict_first();
-        const int pre = nch < kGStages ? nch : kGStages;
+        const int pre = nch < ST ? nch : ST;
         for (int i = 0; i < pre; ++i) {
             mbar_arrive_expect_tx(&full[i], kWTileBytes + kXTileBytes);
             tma_load_2d_hint(wt + i * kWTileBytes, &wmap, chunk_x(i), n0, &full[i], pol);
@@ -115,8 +194,8 @@ __global__ void __launch_bounds__(kGThreads, 1)
         for (int i = 0; i < pre; ++i) tma_load_2d(xt + i * kXTileBytes, &xmap, chunk_x(i), 0, &full[i]);
         int issued = pre;
         for (int i = pre; i < nch; ++i) {
-            const int s = i % kGStages;
-            if (!gemm_wait(&empty[s], ((i / kGStages) - 1) & 1, a.err)) break;
+            const int s = i % ST;
+            if (!gemm_wait(&empty[s], ((i / ST) - 1) & 1, a.err)) break;
             mbar_arrive_expect_tx(&full[s], kWTileBytes + kXTileBytes);
             tma_load_2d_hint(wt + s * kWTileBytes, &wmap, chunk_x(i), n0, &full[s], pol);
             tma_load_2d(xt + s * kXTileBytes, &xmap, chunk_x(i), 0, &full[s]);
@@ -124,16 +203,16 @@ __global__ void __launch_bounds__(kGThreads, 1)
         }
         // Every load issued lands before the CTA may exit (the MMA thread consumes them; this only
         // matters when a wait gave up).
-        for (int i = issued > kGStages ? issued - kGStages : 0; i < issued; ++i) {
-            gemm_wait(&full[i % kGStages], (i / kGStages) & 1, a.err);
+        for (int i = issued > ST ? issued - ST : 0; i < issued; ++i) {
+            gemm_wait(&full[i % ST], (i / ST) & 1, a.err);
         }
     } else if (warp == 1 && lane == 0) {
         // MMA issuer: per stage, 4 K steps of 16 (+32 bytes inside the swizzled 128-byte rows), each one
         // MMA with the hi plane and one with the lo plane into the same accumulator.
         constexpr uint32_t idesc = idesc_bf16_f32(kGM, kGN);
         for (int i = 0; i < nch; ++i) {
-            const int s = i % kGStages;
-            if (!gemm_wait(&full[s], (i / kGStages) & 1, a.err)) break;
+            const int s = i % ST;
+            if (!gemm_wait(&full[s], (i / ST) & 1, a.err)) break;
             tc_fence_after();
             const uint64_t ad = smem_desc_sw128(smem_addr(wt + s * kWTileBytes));
             const uint64_t bh = smem_desc_sw128(smem_addr(xt + s * kXTileBytes));
@@ -146,30 +225,247 @@ __global__ void __launch_bounds__(kGThreads, 1)
             mma_commit(&empty[s]);  // the stage is free once these MMAs have read it
         }
         mma_commit(done);
+    } else if (warp >= 2) {
+        // Idle during the mainloop: the RMSNorm scale of each batch row from the partial sums of squares.
+        grid_dep_wait();
+        const int b = tid - 64;
+        float inv = 1.f;
+        if (e.ssq_in) {
+            // Up to 16 partials (one per 128-row tile of the producing GEMM): loads issued together, added in
+            // order.
+            float part[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) part[i] = i < e.ssq_count ? __ldcg(e.ssq_in + i * kBatchMax + b) : 0.f;
+            float s = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; ++i) s += part[i];
+            inv = rsqrtf(s / static_cast<float>(e.norm_n) + e.eps);
+        }
+        inv_rms[b] = inv;
+        if constexpr (EPI == static_cast<int>(GemmEpilogue::QKV_ROPE)) {
+            pos_s[b] = b < a.batch ? e.pos[b] : 0;
+            if (b < 32) freq_s[b] = e.inv_freq[b];
+        }
     }
     __syncwarp();
-    // Epilogue: TMEM lane m = weight row n0 + m, column b = batch row b. The partials buffer may still be
-    // read by the kernel before this one until it has completed.
+    // Everything below may write buffers the previous kernel reads.
     grid_dep_wait();
     if (lane == 0) gemm_wait(done, 0, a.err);
     __syncwarp();
     tc_fence_after();
-    const int n = n0 + 32 * warp + lane;
+    // Accumulator -> shared memory T[col][row] (the ring is idle: every load landed and every MMA ended).
+    float* T = reinterpret_cast<float*>(smem);
+    {
+        const int row = 32 * warp + lane;
 #pragma unroll
-    for (int c = 0; c < kGN; c += 32) {
-        float v[32];
-        tmem_ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + static_cast<uint32_t>(c), v);
-        if (n < a.n) {
+        for (int c = 0; c < kGN; c += 32) {
+            float v[32];
+            tmem_ld32(tmem + (static_cast<uint32_t>(32 * warp) << 16) + static_cast<uint32_t>(c), v);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                const int b = c + j;
-                if (b < a.batch) a.part[(static_cast<size_t>(blockIdx.y) * a.batch + b) * a.n + n] = v[j];
-            }
+            for (int j = 0; j < 32; ++j) T[(c + j) * kGM + row] = v[j];
         }
     }
     tc_fence_before();
     __syncthreads();
     if (warp == 0) tmem_dealloc(tmem, kGN);
+    const uint32_t ks = static_cast<uint32_t>(a.ksplit);
+    const uint32_t rank = ks > 1 ? cluster_rank() : 0u;
+    if (ks > 1) cluster_sync();  // every rank's partial tile is in its shared memory
+    const TileSum tsum{T, smem_addr(T), ks};
+    auto sum = [&](int col, int row) { return tsum.sum4(col, row); };
+    const int batch = a.batch;
+    if constexpr (EPI == static_cast<int>(GemmEpilogue::STORE) || EPI == static_cast<int>(GemmEpilogue::LOGITS) ||
+                  EPI == static_cast<int>(GemmEpilogue::ADD)) {
+        // Slice `rank` of the tile's rows, in groups of 4 rows; items (row group, batch column) with
+        // consecutive threads on consecutive row groups. Full groups use 16-byte accesses.
+        const int g0 = static_cast<int>(rank) * (kGM / 4) / static_cast<int>(ks);
+        const int len = (static_cast<int>(rank) + 1) * (kGM / 4) / static_cast<int>(ks) - g0;
+        float* sq = T + kGN * kGM;  // ADD: squares per (batch column, row group) after T in the idle ring
+        const size_t plane = static_cast<size_t>(kBatchMax) * a.n;
+        for (int it = tid; it < kGN * len; it += kGThreads) {
+            const int el = it % len, b = it / len;
+            const int row = 4 * (g0 + el), j = n0 + row;
+            const size_t at = static_cast<size_t>(b) * a.n + j;
+            const bool full4 = j + 3 < a.n && (at & 3) == 0;
+            float sq4 = 0.f;
+            if (b < batch && j < a.n) {
+                float4 y4 = make_float4(0.f, 0.f, 0.f, 0.f);
+                if constexpr (EPI == static_cast<int>(GemmEpilogue::ADD)) {
+                    // The residual is fetched before the partial sums, so both latencies overlap.
+                    if (full4) {
+                        y4 = *reinterpret_cast<const float4*>(e.y + at);
+                    } else {
+                        y4.x = e.y[at];
+                        if (j + 1 < a.n) y4.y = e.y[at + 1];
+                        if (j + 2 < a.n) y4.z = e.y[at + 2];
+                    }
+                }
+                const float4 s4 = sum(b, row);
+                const float sc = inv_rms[b];
+                float4 v4 = make_float4(s4.x * sc + y4.x, s4.y * sc + y4.y, s4.z * sc + y4.z, s4.w * sc + y4.w);
+                if (full4) {
+                    *reinterpret_cast<float4*>(e.y + at) = v4;
+                } else {
+                    for (int q = 0; q < 4 && j + q < a.n; ++q) e.y[at + q] = f4get(v4, q);
+                }
+                if constexpr (EPI == static_cast<int>(GemmEpilogue::ADD)) {
+                    sq4 = v4.x * v4.x + v4.y * v4.y + v4.z * v4.z + v4.w * v4.w;
+                    if (e.planes && !full4) {
+                        for (int q = 0; q < 4 && j + q < a.n; ++q) {
+                            store_planes_g(e.planes, plane, at + q, f4get(v4, q) * e.gain[j + q]);
+                        }
+                    } else if (e.planes) {
+                        const float4 g4 = *reinterpret_cast<const float4*>(e.gain + j);
+                        const float w0 = v4.x * g4.x, w1 = v4.y * g4.y, w2 = v4.z * g4.z, w3 = v4.w * g4.w;
+                        const __nv_bfloat162 h01 = __floats2bfloat162_rn(w0, w1), h23 = __floats2bfloat162_rn(w2, w3);
+                        const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+                        const __nv_bfloat162 l01 = __floats2bfloat162_rn(w0 - f01.x, w1 - f01.y);
+                        const __nv_bfloat162 l23 = __floats2bfloat162_rn(w2 - f23.x, w3 - f23.y);
+                        uint2 hv, lv;
+                        hv.x = *reinterpret_cast<const uint32_t*>(&h01);
+                        hv.y = *reinterpret_cast<const uint32_t*>(&h23);
+                        lv.x = *reinterpret_cast<const uint32_t*>(&l01);
+                        lv.y = *reinterpret_cast<const uint32_t*>(&l23);
+                        *reinterpret_cast<uint2*>(e.planes + at) = hv;
+                        *reinterpret_cast<uint2*>(e.planes + plane + at) = lv;
+                    }
+                }
+            }
+            if constexpr (EPI == static_cast<int>(GemmEpilogue::ADD)) sq[b * len + el] = sq4;
+        }
+        if constexpr (EPI == static_cast<int>(GemmEpilogue::ADD)) {
+            if (e.ssq_out) {
+                // Per batch row: this rank's slice sum (in row order), then rank 0 adds the ranks in order,
+                // one partial per tile.
+                float* sqs = sq + kGN * (kGM / 4);
+                __syncthreads();
+                if (tid < kGN) {
+                    float s = 0.f;
+                    for (int el = 0; el < len; ++el) s += sq[tid * len + el];
+                    sqs[tid] = s;
+                }
+                __syncthreads();
+                if (ks > 1) cluster_sync();
+                if (rank == 0 && tid < kGN) {
+                    float s = 0.f;
+                    if (ks == 1) {
+                        s = sqs[tid];
+                    } else {
+                        for (uint32_t r = 0; r < ks; ++r) s += ld_peer_f32(peer_smem(smem_addr(sqs + tid), r));
+                    }
+                    e.ssq_out[static_cast<size_t>(tile) * kBatchMax + tid] = s;
+                }
+            }
+        }
+        if constexpr (EPI == static_cast<int>(GemmEpilogue::LOGITS)) {
+            // ksplit is 1: the whole tile is local. Threads b and 64 + b: the largest scaled output of rows
+            // 0-63 / 64-127 for batch row b; then merged.
+            float* mv = T + kGN * kGM;
+            int* mi = reinterpret_cast<int*>(mv + kGThreads);
+            {
+                const int b = tid & 63, half = tid >> 6;
+                float bv = -FLT_MAX;
+                int bi = INT_MAX;
+                const float sc = inv_rms[b];
+                for (int row = 64 * half; row < 64 * half + 64 && n0 + row < a.n; ++row) {
+                    argmax_better(bv, bi, T[b * kGM + row] * sc, n0 + row);
+                }
+                mv[tid] = bv;
+                mi[tid] = bi;
+            }
+            __syncthreads();
+            if (tid < batch) {
+                float bv = mv[tid];
+                int bi = mi[tid];
+                argmax_better(bv, bi, mv[64 + tid], mi[64 + tid]);
+                e.am_v[static_cast<size_t>(tid) * a.n_tiles + tile] = bv;
+                e.am_i[static_cast<size_t>(tid) * a.n_tiles + tile] = bi;
+            }
+        }
+    } else if constexpr (EPI == static_cast<int>(GemmEpilogue::SWIGLU)) {
+        // Pairs (gate row p, up row 64 + p) of the interleaved layout -> output feature 64 * tile + p, in
+        // groups of 4 pairs.
+        const int g0 = static_cast<int>(rank) * (kGM / 8) / static_cast<int>(ks);
+        const int len = (static_cast<int>(rank) + 1) * (kGM / 8) / static_cast<int>(ks) - g0;
+        const int n_out = a.n / 2;
+        const size_t plane = static_cast<size_t>(kBatchMax) * n_out;
+        for (int it = tid; it < kGN * len; it += kGThreads) {
+            const int el = it % len, b = it / len;
+            if (b >= batch) continue;
+            const int p = 4 * (g0 + el);
+            const float4 g4 = sum(b, p), u4 = sum(b, kGM / 2 + p);
+            const float sc = inv_rms[b];
+            float v[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) v[q] = silu_g(f4get(g4, q) * sc) * (f4get(u4, q) * sc);
+            const size_t idx = static_cast<size_t>(b) * n_out + tile * (kGM / 2) + p;
+            if (e.y) *reinterpret_cast<float4*>(e.y + idx) = make_float4(v[0], v[1], v[2], v[3]);
+            if (e.planes) {
+                const __nv_bfloat162 h01 = __floats2bfloat162_rn(v[0], v[1]), h23 = __floats2bfloat162_rn(v[2], v[3]);
+                const float2 f01 = __bfloat1622float2(h01), f23 = __bfloat1622float2(h23);
+                const __nv_bfloat162 l01 = __floats2bfloat162_rn(v[0] - f01.x, v[1] - f01.y);
+                const __nv_bfloat162 l23 = __floats2bfloat162_rn(v[2] - f23.x, v[3] - f23.y);
+                uint2 hv, lv;
+                hv.x = *reinterpret_cast<const uint32_t*>(&h01);
+                hv.y = *reinterpret_cast<const uint32_t*>(&h23);
+                lv.x = *reinterpret_cast<const uint32_t*>(&l01);
+                lv.y = *reinterpret_cast<const uint32_t*>(&l23);
+                *reinterpret_cast<uint2*>(e.planes + idx) = hv;
+                *reinterpret_cast<uint2*>(e.planes + plane + idx) = lv;
+            }
+        }
+    } else {
+        // QKV_ROPE: pairs (dim i, dim i + 32) of the tile's two heads, in groups of 4 pairs.
+        const int g0 = static_cast<int>(rank) * (kGM / 8) / static_cast<int>(ks);
+        const int len = (static_cast<int>(rank) + 1) * (kGM / 8) / static_cast<int>(ks) - g0;
+        const int stride = (e.nh + 2 * e.nkv) * 64;
+        for (int it = tid; it < kGN * len; it += kGThreads) {
+            const int el = it % len, b = it / len;
+            if (b >= batch) continue;
+            const int p = 4 * (g0 + el), hh = p >> 5, i0 = p & 31;
+            const int ra = hh * 64 + i0, rb = ra + 32;
+            const int gh = (n0 + ra) >> 6;  // global head: q < nh <= k < nh + nkv <= v
+            const float4 a4 = sum(b, ra), b4 = sum(b, rb);
+            const float sc = inv_rms[b];
+            const int pos = pos_s[b];
+            float y0[4], y1[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const float x0 = f4get(a4, q) * sc, x1 = f4get(b4, q) * sc;
+                if (gh < e.nh + e.nkv) {
+                    float sn, cs;
+                    sincosf(static_cast<float>(pos) * freq_s[i0 + q], &sn, &cs);
+                    y0[q] = x0 * cs - x1 * sn;
+                    y1[q] = x1 * cs + x0 * sn;
+                } else {
+                    y0[q] = x0;
+                    y1[q] = x1;
+                }
+            }
+            if (gh < e.nh) {
+                float* qp = e.q_out + static_cast<size_t>(b) * stride + gh * 64 + i0;
+                *reinterpret_cast<float4*>(qp) = make_float4(y0[0], y0[1], y0[2], y0[3]);
+                *reinterpret_cast<float4*>(qp + 32) = make_float4(y1[0], y1[1], y1[2], y1[3]);
+            } else {
+                const bool is_k = gh < e.nh + e.nkv;
+                KV* c = static_cast<KV*>(is_k ? e.k_cache : e.v_cache) + e.seq_stride * b +
+                        (static_cast<size_t>(gh - e.nh - (is_k ? 0 : e.nkv)) * e.max_seq + pos) * 64 + i0;
+                union Pack4 {
+                    KV h[4];
+                    uint2 u;
+                } lo4, hi4;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    lo4.h[q] = to_cache<KV>(y0[q]);
+                    hi4.h[q] = to_cache<KV>(y1[q]);
+                }
+                *reinterpret_cast<uint2*>(c) = lo4.u;
+                *reinterpret_cast<uint2*>(c + 32) = hi4.u;
+            }
+        }
+    }
+    __syncwarp();
+    if (ks > 1) cluster_sync();  // peers read this CTA's tile until every rank is done
 }
 
 }  // namespace
@@ -214,78 +510,153 @@ const CUtensorMap* tensor_map(const void* base, int rows, int cols, int box_rows
     return &cache.emplace(key, map).first->second;
 }
 
-__device__ __forceinline__ float silu_g(float x) { return x / (1.f + __expf(-x)); }
+using GemmFn = void (*)(CUtensorMap, CUtensorMap, GemmArgs);
 
-// out[b][j] from sum over ks of part[ks][b][j] (added in ks order): STORE / ADD (residual) / SWIGLU
-// (j < n/2: silu(s[j]) * s[n/2 + j]); outb (optional) gets the value as hi/lo bf16 planes.
-__global__ void gemm_reduce_kernel(const float* __restrict__ part, int ksplit, int batch, int n, int ep, float* out,
-                                   __nv_bfloat16* outb) {
-    grid_dep_launch();
-    grid_dep_wait();
-    const int n_out = ep == static_cast<int>(GemmEpilogue::SWIGLU) ? n / 2 : n;
-    const size_t total = static_cast<size_t>(batch) * n_out;
-    const size_t plane = static_cast<size_t>(kBatchMax) * n_out;
-    for (size_t idx = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; idx < total;
-         idx += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const int b = static_cast<int>(idx / n_out), j = static_cast<int>(idx % n_out);
-        float v;
-        if (ep == static_cast<int>(GemmEpilogue::SWIGLU)) {
-            float g = 0.f, u = 0.f;
-            for (int ks = 0; ks < ksplit; ++ks) {
-                const float* pr = part + (static_cast<size_t>(ks) * batch + b) * n;
-                g += pr[j];
-                u += pr[n_out + j];
-            }
-            v = silu_g(g) * u;
-        } else {
-            float s = 0.f;
-            for (int ks = 0; ks < ksplit; ++ks) s += part[(static_cast<size_t>(ks) * batch + b) * n + j];
-            v = ep == static_cast<int>(GemmEpilogue::ADD) ? out[idx] + s : s;
-        }
-        if (out) out[idx] = v;
-        if (outb) {
-            const __nv_bfloat16 hi = __float2bfloat16_rn(v);
-            outb[idx] = hi;
-            outb[plane + idx] = __float2bfloat16_rn(v - __bfloat162float(hi));
-        }
+// Ring depth: 7 stages (one CTA per SM) or 3 (two CTAs per SM, so the next kernel's CTAs can start
+// streaming while this one's epilogue runs). The lm_head always uses 3; CUDALLM_GEMM_STAGES=7 selects
+// the deep ring for the others.
+int deep_ring() {
+    static const bool deep = [] {
+        const char* env = std::getenv("CUDALLM_GEMM_STAGES");
+        return env && std::atoi(env) == 7;
+    }();
+    return deep;
+}
+
+template <int ST>
+GemmFn gemm_fn_st(GemmEpilogue kind, bool kv_bf16) {
+    switch (kind) {
+        case GemmEpilogue::STORE: return gemm_kernel<0, __half, ST>;
+        case GemmEpilogue::ADD: return gemm_kernel<1, __half, ST>;
+        case GemmEpilogue::SWIGLU: return gemm_kernel<2, __half, ST>;
+        case GemmEpilogue::QKV_ROPE: return kv_bf16 ? gemm_kernel<3, __nv_bfloat16, ST> : gemm_kernel<3, __half, ST>;
+        case GemmEpilogue::LOGITS: return gemm_kernel<4, __half, ST>;
     }
+    return nullptr;
+}
+
+int gemm_stages(GemmEpilogue kind) { return kind != GemmEpilogue::LOGITS && deep_ring() ? kGStages : kGStagesLogits; }
+
+GemmFn gemm_fn(GemmEpilogue kind, bool kv_bf16) {
+    return gemm_stages(kind) == kGStages ? gemm_fn_st<kGStages>(kind, kv_bf16) : gemm_fn_st<kGStagesLogits>(kind, kv_bf16);
+}
+
+int gemm_smem(GemmEpilogue kind) { return smem_bytes(gemm_stages(kind)); }
+
+// Shared-memory size and cluster permission, once per (kernel, device).
+void configure(GemmFn fn, int smem) {
+    static std::mutex mu;
+    static std::map<std::pair<GemmFn, int>, bool> done;
+    int dev = 0;
+    CLLM_CUDA(cudaGetDevice(&dev));
+    std::lock_guard<std::mutex> lock(mu);
+    if (done.count({fn, dev})) return;
+    CLLM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    CLLM_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+    done[{fn, dev}] = true;
+}
+
+__global__ void interleave_gate_up_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, int inter, int row_u4) {
+    // dst row r: tile t = r / 128, q = r % 128 -> gate row 64t + q (q < 64) or up row 64t + q - 64.
+    const int r = blockIdx.x;
+    const int t = r / kGM, q = r % kGM;
+    const int s = q < kGM / 2 ? kGM / 2 * t + q : inter + kGM / 2 * t + (q - kGM / 2);
+    for (int c = threadIdx.x; c < row_u4; c += blockDim.x) dst[static_cast<size_t>(r) * row_u4 + c] = src[static_cast<size_t>(s) * row_u4 + c];
 }
 
 }  // namespace
 
-int gemm_smem_bytes() { return kGSmemBytes; }
-
-void launch_gemm_bf16(const __nv_bfloat16* w, int n, int k, const __nv_bfloat16* x, int batch, int ksplit, float* part,
-                      unsigned* err, cudaStream_t stream, bool pdl) {
-    CLLM_CHECK(w && x && part && err, "launch_gemm_bf16: null pointer");
-    CLLM_CHECK(batch >= 1 && batch <= kGN, "launch_gemm_bf16: batch must be 1..64");
-    CLLM_CHECK(n >= 1 && k >= kGK && k % kGK == 0 && ksplit >= 1 && ksplit <= k / kGK,
-               "launch_gemm_bf16: k must be a multiple of 64 with at least ksplit 64-column chunks");
-    CLLM_CHECK((reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
-               "launch_gemm_bf16: operands must be 16-byte aligned");
-    static bool configured[64] = {};
-    int dev = 0;
+int gemm_pick_ksplit(int n, int k) {
+    int dev = 0, sms = 0;
     CLLM_CUDA(cudaGetDevice(&dev));
-    if (dev >= 64 || !configured[dev]) {
-        CLLM_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kGSmemBytes));
-        if (dev < 64) configured[dev] = true;
+    CLLM_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int mtiles = (n + kGM - 1) / kGM;
+    const int chunks = k / kGK;
+    GemmFn fn = gemm_fn(GemmEpilogue::STORE, false);
+    configure(fn, gemm_smem(GemmEpilogue::STORE));
+    for (int ks = std::min({kMaxKsplit, chunks, std::max(1, sms / mtiles)}); ks > 1; --ks) {
+        cudaLaunchConfig_t cfg{};
+        cfg.gridDim = dim3(mtiles, ks);
+        cfg.blockDim = dim3(kGThreads);
+        cfg.dynamicSmemBytes = gemm_smem(GemmEpilogue::STORE);
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeClusterDimension;
+        attr[0].val.clusterDim.x = 1;
+        attr[0].val.clusterDim.y = ks;
+        attr[0].val.clusterDim.z = 1;
+        cfg.attrs = attr;
+        cfg.numAttrs = 1;
+        int clusters = 0;
+        if (cudaOccupancyMaxActiveClusters(&clusters, fn, &cfg) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        if (clusters >= mtiles) return ks;
     }
-    const CUtensorMap* wm = tensor_map(w, n, k, kGM);
-    const CUtensorMap* xm = tensor_map(x, kXRows, k, kXRows);
-    GemmArgs a{part, n, batch, k / kGK, ksplit, err};
-    launch_kernel(gemm_bf16_kernel, dim3((n + kGM - 1) / kGM, ksplit), dim3(kGThreads), kGSmemBytes, stream, pdl, *wm, *xm,
-                  a);
+    return 1;
 }
 
-void launch_gemm_reduce(const float* part, int ksplit, int batch, int n, GemmEpilogue ep, float* out, __nv_bfloat16* outb,
-                        cudaStream_t stream, bool pdl) {
-    CLLM_CHECK(part && (out || outb) && batch >= 1 && batch <= kBatchMax && n >= 1 && ksplit >= 1,
-               "launch_gemm_reduce: bad arguments");
-    CLLM_CHECK(ep != GemmEpilogue::ADD || out, "launch_gemm_reduce: ADD needs out");
-    const size_t total = static_cast<size_t>(batch) * (ep == GemmEpilogue::SWIGLU ? n / 2 : n);
-    const int blocks = static_cast<int>(std::min<size_t>((total + 255) / 256, 148 * 8));
-    launch_kernel(gemm_reduce_kernel, dim3(blocks), dim3(256), 0, stream, pdl, part, ksplit, batch, n, static_cast<int>(ep), out,
-                  outb);
+void launch_gemm(const __nv_bfloat16* w, int n, int k, const __nv_bfloat16* x, int batch, int ksplit, const GemmEpi& epi,
+                 unsigned* err, cudaStream_t stream, bool pdl) {
+    CLLM_CHECK(w && x && err, "launch_gemm: null pointer");
+    CLLM_CHECK(batch >= 1 && batch <= kGN, "launch_gemm: batch must be 1..64");
+    CLLM_CHECK(n >= 1 && k >= kGK && k % kGK == 0 && ksplit >= 1 && ksplit <= std::min(kMaxKsplit, k / kGK),
+               "launch_gemm: k must be a multiple of 64 and ksplit in 1..min(16, k/64)");
+    CLLM_CHECK((reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(x) & 15) == 0,
+               "launch_gemm: operands must be 16-byte aligned");
+    CLLM_CHECK(!epi.ssq_in || (epi.ssq_count >= 1 && epi.ssq_count <= 16 && epi.norm_n >= 1),
+               "launch_gemm: bad RMSNorm statistics");
+    switch (epi.kind) {
+        case GemmEpilogue::STORE: CLLM_CHECK(epi.y, "launch_gemm: STORE needs y"); break;
+        case GemmEpilogue::LOGITS:
+            CLLM_CHECK(epi.y && epi.am_v && epi.am_i && ksplit == 1, "launch_gemm: LOGITS needs y, am_v, am_i and ksplit 1");
+            break;
+        case GemmEpilogue::ADD: CLLM_CHECK(epi.y && (!epi.planes || epi.gain), "launch_gemm: ADD needs y (and gain with planes)"); break;
+        case GemmEpilogue::SWIGLU:
+            CLLM_CHECK((epi.y || epi.planes) && n % kGM == 0, "launch_gemm: SWIGLU needs an output and n % 128 == 0");
+            break;
+        case GemmEpilogue::QKV_ROPE:
+            CLLM_CHECK(epi.q_out && epi.inv_freq && epi.k_cache && epi.v_cache && epi.pos && epi.nh > 0 && epi.nkv > 0 &&
+                           n == (epi.nh + 2 * epi.nkv) * 64 && n % kGM == 0 && epi.max_seq > 0,
+                       "launch_gemm: bad QKV_ROPE arguments");
+            break;
+    }
+    GemmFn fn = gemm_fn(epi.kind, epi.kv_bf16);
+    const int smem = gemm_smem(epi.kind);
+    configure(fn, smem);
+    const CUtensorMap* wm = tensor_map(w, n, k, kGM);
+    const CUtensorMap* xm = tensor_map(x, kXRows, k, kXRows);
+    const int mtiles = (n + kGM - 1) / kGM;
+    GemmArgs a{n, batch, k / kGK, ksplit, mtiles, err, epi};
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(mtiles, ksplit);
+    cfg.blockDim = dim3(kGThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    int na = 0;
+    if (ksplit > 1) {
+        attr[na].id = cudaLaunchAttributeClusterDimension;
+        attr[na].val.clusterDim.x = 1;
+        attr[na].val.clusterDim.y = ksplit;
+        attr[na].val.clusterDim.z = 1;
+        ++na;
+    }
+    if (pdl) {
+        attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        attr[na].val.programmaticStreamSerializationAllowed = 1;
+        ++na;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = na;
+    CLLM_CUDA(cudaLaunchKernelEx(&cfg, fn, *wm, *xm, a));
+}
+
+void interleave_gate_up(const __nv_bfloat16* src, __nv_bfloat16* dst, int inter, int k, cudaStream_t stream) {
+    CLLM_CHECK(src && dst && src != dst && inter % (kGM / 2) == 0 && k % 8 == 0, "interleave_gate_up: bad arguments");
+    interleave_gate_up_kernel<<<2 * inter, 256, 0, stream>>>(reinterpret_cast<const uint4*>(src), reinterpret_cast<uint4*>(dst),
+                                                          inter, k / 8);
+    CLLM_CUDA(cudaGetLastError());
 }
 
 }  // namespace cudallm
