@@ -75,6 +75,19 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
         ks_gu_ = gemm_pick_ksplit(2 * I, H);
         ks_down_ = gemm_pick_ksplit(H, I);
         lm_tiles_ = (V + kGemmTileRows - 1) / kGemmTileRows;
+        if (const char* env = std::getenv("CUDALLM_BATCH_KSPLIT")) {
+            // "qkv,wo,gate_up,down": explicit K splits (each 1..16 and at most k / 64).
+            int v[4] = {0, 0, 0, 0};
+            if (std::sscanf(env, "%d,%d,%d,%d", &v[0], &v[1], &v[2], &v[3]) != 4) throw ArgError("CUDALLM_BATCH_KSPLIT: want a,b,c,d");
+            const int kmax[4] = {H / 64, NH * D / 64, H / 64, I / 64};
+            for (int i = 0; i < 4; ++i) {
+                if (v[i] < 1 || v[i] > 16 || v[i] > kmax[i]) throw ArgError("CUDALLM_BATCH_KSPLIT: split out of range");
+            }
+            ks_qkv_ = v[0];
+            ks_wo_ = v[1];
+            ks_gu_ = v[2];
+            ks_down_ = v[3];
+        }
         if (std::getenv("CUDALLM_BATCH_VERBOSE")) {
             std::fprintf(stderr, "cudallm batch: K splits qkv %d wo %d gate/up %d down %d; attention %s; pdl %d\n", ks_qkv_, ks_wo_,
                          ks_gu_, ks_down_, attn_stream_ ? "stream" : "split", opts_.pdl ? 1 : 0);
