@@ -86,7 +86,8 @@ constexpr int stage_rows() {
     constexpr int halves = KIND == 2 ? 2 : 1;  // gate/up
     constexpr int rb = weight_row_bytes<WT>(KIND == 3 ? 4 * 2048 : 2048);  // down has K = 8192
     constexpr int fit = kStageBytes / halves / rb;
-    return (fit < kMaxTileRows ? fit : kMaxTileRows) * halves;
+    constexpr int cap = decode_step_tile_rows(WT);
+    return (fit < cap ? fit : cap) * halves;
 }
 
 struct WOp {
@@ -661,7 +662,8 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
     }
     constexpr int kN = stage_rows<WT, kQkv>(), kCpl = seg_chunks_per_lane<WT, kQkv>();
     constexpr int kNd = stage_rows<WT, kDown>(), kCpld = seg_chunks_per_lane<WT, kDown>();
-    static_assert(stage_rows<WT, kWo>() == kN && stage_rows<WT, kGu>() == kN, "shared tile shape");
+    constexpr int kNg = stage_rows<WT, kGu>();  // gate + up rows of one tile
+    static_assert(stage_rows<WT, kWo>() == kN && seg_chunks_per_lane<WT, kGu>() == kCpl, "shared tile shape");
     static_assert(seg_chunks_per_lane<WT, kWo>() == kCpl && seg_chunks_per_lane<WT, kGu>() == kCpl, "shared tile shape");
     float bv = -INFINITY;
     int bi = INT_MAX;
@@ -760,7 +762,8 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
         }
         if (c.tid == 0) trace_mark(p, top, 4);
         const bool ok = kind == kDown ? run_tiles<WT, kNd, kCpld>(c, o, kind, bv, bi, l)
-                                      : run_tiles<WT, kN, kCpl>(c, o, kind, bv, bi, l);
+                        : (kNg != kN && kind == kGu) ? run_tiles<WT, kNg, kCpl>(c, o, kind, bv, bi, l)
+                                                     : run_tiles<WT, kN, kCpl>(c, o, kind, bv, bi, l);
         if (!ok) return;
         if (kind != kLm && c.tid == 0) trace_mark(p, top, 2);  // run_tiles ended with a block barrier
     }

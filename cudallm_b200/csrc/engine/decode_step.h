@@ -22,6 +22,11 @@
 
 namespace cudallm {
 
+// Most weight rows in one tile of the persistent kernel. int4 tiles stop at 4 rows (a 4 KiB tile for a
+// 2048-column matrix): a tile is one warp's work, and 16 int4 rows (32k weights to dequantise) per warp
+// would leave most consumer warps idle on the small operations while one warp works through its tile.
+__host__ __device__ constexpr int decode_step_tile_rows(WeightType wt) { return wt == WeightType::INT4 ? 4 : kMaxTileRows; }
+
 struct StepLayer {
     const float* attn_norm;
     const void* wqkv;

@@ -142,9 +142,9 @@ Engine::Engine(const std::string& path, const EngineOptions& opts) : opts_(opts)
             if (const char* env = std::getenv("CUDALLM_WHOLE_HEAD_MAX_TILES")) p.whole_head_max_tiles = std::atoi(env);
             int trace_op = 64;  // lm_head; CUDALLM_TRACE_TILE_OP picks the weight operation whose tiles are stamped first
             if (const char* env = std::getenv("CUDALLM_TRACE_TILE_OP")) trace_op = std::atoi(env);
-            // The persistent kernel is compiled for the default tile shape (matvec_rpb selects the tile rows of
-            // the per-op kernels only; results do not depend on it).
-            const int rpb = 0;
+            // The persistent kernel is compiled for its own tile shape (decode_step_tile_rows; matvec_rpb
+            // selects the tile rows of the per-op kernels only; results do not depend on it).
+            const int rpb = decode_step_tile_rows(c.wtype);
             p.g_qkv = make_tile_geom(c.wtype, Epilogue::STORE, (c.n_heads + 2 * c.n_kv_heads) * c.head_dim, c.hidden, rpb);
             p.g_wo = make_tile_geom(c.wtype, Epilogue::ADD, c.hidden, c.hidden, rpb);
             p.g_gu = make_tile_geom(c.wtype, Epilogue::SWIGLU, 2 * c.inter, c.hidden, rpb);
