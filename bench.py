@@ -12,8 +12,8 @@ per GPU) every rank decodes its own sequence (replicas: the batch-1 path does no
 is N*K divided by the slowest rank's time.
 
 Also measured on every rank (unless --quick): batched decode of 64 sequences per GPU
-(512-token prompts, then timed greedy decode steps; tensor-core GEMMs), reported under "batched" as the
-whole-job tok/s over all ranks.
+(512-token prompts, then timed greedy decode steps; tensor-core GEMMs) with bf16 and with int4 weights,
+reported under "batched" ({"bf16": ..., "int4": ...}) as the whole-job tok/s over all ranks.
 
 Reported (one JSON line on rank 0): value = tok/s with weights resident; e2e = tok/s through the C ABI
 when every step takes its token from the host and returns the next token to the host; roofline of the
@@ -173,7 +173,7 @@ def time_e2e(eng, prompt: list[int], steps: int, torch, barrier) -> dict:
 BATCH_SEQS, BATCH_PROMPT, BATCH_GEN = 64, 512, 256  # BASELINE config 5, per GPU
 
 
-def time_batched(args, device: int, torch, barrier) -> dict:
+def time_batched(args, device: int, torch, barrier, dtype: str = "bf16") -> dict:
     """Batched decode (64 independent sequences on this GPU): every sequence steps a 512-token random
     prompt (untimed), then 256 greedy decode steps are timed with CUDA events on the engine's stream
     (positions 512..767, all 64 sequences per step); then 64 more steps through the C ABI with the tokens
@@ -181,7 +181,7 @@ def time_batched(args, device: int, torch, barrier) -> dict:
     import numpy as np
     from cudallm_b200 import synth
     from cudallm_b200.engine import BatchEngine
-    path, _ = synth.ensure_model("bf16", seed=0, max_seq_len=4096)
+    path, _ = synth.ensure_model(dtype, seed=0, max_seq_len=4096)
     rng = np.random.default_rng([0, device])
     prompts = rng.integers(0, 128256, (BATCH_PROMPT, BATCH_SEQS)).astype(np.int32)
     gen = min(BATCH_GEN, 1024 - BATCH_PROMPT - 64)
@@ -348,23 +348,25 @@ def run_ours(args) -> None:
                      "roofline_frac": (b / (kms * 1e-3) / 1e9) / peaks["hbm_gbs"],
                      "achieved_gbs": b / (kms * 1e-3) / 1e9, "ms_per_token": ms / args.steps}
 
-    batched = None
+    batched = {}
     if not args.quick:
-        b = time_batched(args, local_rank, torch, barrier)
-        b_ms = max_over_ranks(b["ms"])
-        b_e2e_ms = max_over_ranks(b["e2e_ms"])
-        avg_ctx_b = BATCH_PROMPT + (b["steps"] + 1) / 2
-        b_bytes = b["weight_bytes"] + BATCH_SEQS * KV_BYTES_PER_TOKEN * avg_ctx_b
-        b_gbs = b_bytes / (b_ms / b["steps"] * 1e-3) / 1e9
-        batched = {"metric": "batched decode aggregate tok/s (bf16 weights)",
-                   "value": world * BATCH_SEQS * b["steps"] / (b_ms * 1e-3), "unit": "tok/s",
-                   "per_gpu_tok_s": BATCH_SEQS * b["steps"] / (b_ms * 1e-3), "ms_per_step": b_ms / b["steps"],
-                   "sequences_per_gpu": BATCH_SEQS, "prompt": BATCH_PROMPT, "timed_decode_steps": b["steps"],
-                   "kv": args.kv, "bytes_per_step": int(b_bytes), "achieved_gbs": b_gbs,
-                   "roofline_frac": b_gbs / peaks["hbm_gbs"],
-                   "e2e": {"value": world * BATCH_SEQS * b["e2e_steps"] / (b_e2e_ms * 1e-3), "unit": "tok/s",
-                           "h2d_bytes_per_step": 4 * BATCH_SEQS, "d2h_bytes_per_step": 4 * BATCH_SEQS + 4},
-                   "scaling": "weak (64 sequences per GPU, no collective)"}
+        for bdt in ("bf16", "int4"):
+            b = time_batched(args, local_rank, torch, barrier, bdt)
+            b_ms = max_over_ranks(b["ms"])
+            b_e2e_ms = max_over_ranks(b["e2e_ms"])
+            avg_ctx_b = BATCH_PROMPT + (b["steps"] + 1) / 2
+            b_bytes = b["weight_bytes"] + BATCH_SEQS * KV_BYTES_PER_TOKEN * avg_ctx_b
+            b_gbs = b_bytes / (b_ms / b["steps"] * 1e-3) / 1e9
+            batched[bdt] = {
+                "metric": f"batched decode aggregate tok/s ({bdt} weights)",
+                "value": world * BATCH_SEQS * b["steps"] / (b_ms * 1e-3), "unit": "tok/s",
+                "per_gpu_tok_s": BATCH_SEQS * b["steps"] / (b_ms * 1e-3), "ms_per_step": b_ms / b["steps"],
+                "sequences_per_gpu": BATCH_SEQS, "prompt": BATCH_PROMPT, "timed_decode_steps": b["steps"],
+                "kv": args.kv, "bytes_per_step": int(b_bytes), "achieved_gbs": b_gbs,
+                "roofline_frac": b_gbs / peaks["hbm_gbs"],
+                "e2e": {"value": world * BATCH_SEQS * b["e2e_steps"] / (b_e2e_ms * 1e-3), "unit": "tok/s",
+                        "h2d_bytes_per_step": 4 * BATCH_SEQS, "d2h_bytes_per_step": 4 * BATCH_SEQS + 4},
+                "scaling": "weak (64 sequences per GPU, no collective)"}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -39,8 +39,9 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
     }
     if (opts_.max_seq_len > file.config.max_seq_len) throw ArgError("max_seq_len exceeds the file's max_seq_len");
     if (opts_.kv != KvType::F16 && opts_.kv != KvType::BF16) throw ArgError("kv_dtype must be 0 (fp16) or 1 (bf16)");
-    if (file.config.wtype != WeightType::BF16) {
-        throw ArgError(std::string("batched decode supports bf16 weights; the file holds ") + to_string(file.config.wtype));
+    if (file.config.wtype != WeightType::BF16 && file.config.wtype != WeightType::INT4) {
+        throw ArgError(std::string("batched decode supports bf16 and int4 weights; the file holds ") +
+                       to_string(file.config.wtype));
     }
     if (opts_.device >= 0) {
         int n = 0;
@@ -70,16 +71,20 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
         // One streaming CTA per (KV head, sequence) once that fills the SMs; fewer sequences split their
         // contexts over more CTAs.
         attn_stream_ = opts_.attn_mode == 1 || (opts_.attn_mode == 0 && opts_.n_seq * NKV >= sms);
-        ks_qkv_ = gemm_pick_ksplit(QKV, H);
-        ks_wo_ = gemm_pick_ksplit(H, NH * D);
-        ks_gu_ = gemm_pick_ksplit(2 * I, H);
-        ks_down_ = gemm_pick_ksplit(H, I);
+        int4_ = c.wtype == WeightType::INT4;
+        CLLM_CHECK(!int4_ || c.group_size == 128, "batched decode: int4 needs 128-column scale groups");
+        auto pick = [&](int n, int k) { return int4_ ? gemm_pick_ksplit_int4(n, k) : gemm_pick_ksplit(n, k); };
+        ks_qkv_ = pick(QKV, H);
+        ks_wo_ = pick(H, NH * D);
+        ks_gu_ = pick(2 * I, H);
+        ks_down_ = pick(H, I);
         lm_tiles_ = (V + kGemmTileRows - 1) / kGemmTileRows;
         if (const char* env = std::getenv("CUDALLM_BATCH_KSPLIT")) {
             // "qkv,wo,gate_up,down": explicit K splits (each 1..16 and at most k / 64).
             int v[4] = {0, 0, 0, 0};
             if (std::sscanf(env, "%d,%d,%d,%d", &v[0], &v[1], &v[2], &v[3]) != 4) throw ArgError("CUDALLM_BATCH_KSPLIT: want a,b,c,d");
-            const int kmax[4] = {H / 64, NH * D / 64, H / 64, I / 64};
+            const int unit = int4_ ? 128 : 64;  // int4 splits fall on 128-column groups
+            const int kmax[4] = {H / unit, NH * D / unit, H / unit, I / unit};
             for (int i = 0; i < 4; ++i) {
                 if (v[i] < 1 || v[i] > 16 || v[i] > kmax[i]) throw ArgError("CUDALLM_BATCH_KSPLIT: split out of range");
             }
@@ -118,16 +123,31 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
         alloc_zero(&err_, 1);
         CLLM_CUDA(cudaMemset(tok_in_, 0xff, B * sizeof(int)));  // -1: feed the previous argmax
         // The gate/up matrices are re-laid out in place so that each 128-row GEMM tile holds 64 gate rows and
-        // the 64 matching up rows (the SwiGLU epilogue needs both); this engine owns its copy of the weights.
+        // the 64 matching up rows (the SwiGLU epilogue needs both); int4 codes are also re-packed for the
+        // GEMM's converters (interleave_int4_codes). This engine owns its copy of the weights.
         {
-            const size_t gu_elems = static_cast<size_t>(2) * I * H;
-            __nv_bfloat16* tmp = nullptr;
-            CLLM_CUDA(cudaMalloc(&tmp, gu_elems * 2));
+            const size_t gu_bytes = static_cast<size_t>(2) * I * row_bytes(c.wtype, H);
+            void* tmp = nullptr;
+            CLLM_CUDA(cudaMalloc(&tmp, gu_bytes));
+            auto relayout = [&](const void* p, int row_b) {
+                void* w = const_cast<void*>(p);
+                interleave_gate_up_rows(w, tmp, I, row_b, stream_);
+                CLLM_CUDA(cudaMemcpyAsync(w, tmp, static_cast<size_t>(2) * I * row_b, cudaMemcpyDeviceToDevice, stream_));
+            };
+            auto repack = [&](const Linear& L) {
+                interleave_int4_codes(const_cast<void*>(L.w), static_cast<size_t>(L.rows) * L.cols / 2, stream_);
+            };
             for (const LayerWeights& L : weights_->layers) {
-                auto* w = const_cast<__nv_bfloat16*>(static_cast<const __nv_bfloat16*>(L.w_gate_up.w));
-                interleave_gate_up(w, tmp, I, H, stream_);
-                CLLM_CUDA(cudaMemcpyAsync(w, tmp, gu_elems * 2, cudaMemcpyDeviceToDevice, stream_));
+                relayout(L.w_gate_up.w, static_cast<int>(row_bytes(c.wtype, H)));
+                if (int4_) {
+                    relayout(L.w_gate_up.scales, H / 128 * 2);
+                    repack(L.wqkv);
+                    repack(L.wo);
+                    repack(L.w_gate_up);
+                    repack(L.w_down);
+                }
             }
+            if (int4_) repack(weights_->tok_embeddings);
             CLLM_CUDA(cudaStreamSynchronize(stream_));
             CLLM_CUDA(cudaFree(tmp));
         }
@@ -221,14 +241,21 @@ void BatchEngine::enqueue_layers(int tiles) {
     auto* pa = static_cast<__nv_bfloat16*>(pa_);
     auto* pb = static_cast<__nv_bfloat16*>(pb_);
     auto* act = static_cast<__nv_bfloat16*>(act_);
-    auto bf = [](const Linear& L) { return static_cast<const __nv_bfloat16*>(L.w); };
+    auto gemm = [&](const Linear& L, int n, int k, const __nv_bfloat16* x, int ks, const GemmEpi& epi) {
+        if (int4_) {
+            launch_gemm_int4(static_cast<const uint8_t*>(L.w), static_cast<const __half*>(L.scales), n, k, x, opts_.n_seq, ks, epi,
+                             err_, stream_, opts_.pdl);
+        } else {
+            launch_gemm(static_cast<const __nv_bfloat16*>(L.w), n, k, x, opts_.n_seq, ks, epi, err_, stream_, opts_.pdl);
+        }
+    };
     const bool pdl = opts_.pdl;
     const bool kv_bf16 = opts_.kv == KvType::BF16;
     cudaStream_t s = stream_;
     const int tiles_h = H / kGemmTileRows;
     // x, planes of x * attn_norm[0] and its statistics (one partial).
-    launch_embed_rows(static_cast<const uint16_t*>(W.tok_embeddings.w), tok_in_, tok_, W.layers[0].attn_norm, x_, pa, ssq_, B, H,
-                      s, pdl);
+    launch_embed_rows(W.tok_embeddings.w, int4_ ? static_cast<const __half*>(W.tok_embeddings.scales) : nullptr, tok_in_, tok_,
+                      W.layers[0].attn_norm, x_, pa, ssq_, B, H, s, pdl);
     int ssq_count = 1;
     for (int l = 0; l < c.n_layers; ++l) {
         const LayerWeights& L = W.layers[l];
@@ -250,7 +277,7 @@ void BatchEngine::enqueue_layers(int tiles) {
         q.nkv = NKV;
         q.max_seq = max_seq_;
         q.kv_bf16 = kv_bf16;
-        launch_gemm(bf(L.wqkv), QKV, H, pa, B, ks_qkv_, q, err_, s, pdl);
+        gemm(L.wqkv, QKV, H, pa, ks_qkv_, q);
         if (attn_stream_) {
             launch_attention_rows_stream<KV>(qkv_, kl, vl, seq_stride, dpos_, pb, B, NH, NKV, max_seq_, err_, s, pdl);
         } else {
@@ -263,7 +290,7 @@ void BatchEngine::enqueue_layers(int tiles) {
         o.planes = pa;
         o.gain = L.ffn_norm;
         o.ssq_out = ssq_;
-        launch_gemm(bf(L.wo), H, NH * D, pb, B, ks_wo_, o, err_, s, pdl);
+        gemm(L.wo, H, NH * D, pb, ks_wo_, o);
         GemmEpi g;
         g.kind = GemmEpilogue::SWIGLU;
         g.ssq_in = ssq_;
@@ -271,14 +298,14 @@ void BatchEngine::enqueue_layers(int tiles) {
         g.norm_n = H;
         g.eps = c.rms_eps;
         g.planes = act;
-        launch_gemm(bf(L.w_gate_up), 2 * I, H, pa, B, ks_gu_, g, err_, s, pdl);
+        gemm(L.w_gate_up, 2 * I, H, pa, ks_gu_, g);
         GemmEpi d;
         d.kind = GemmEpilogue::ADD;
         d.y = x_;
         d.planes = pa;
         d.gain = l + 1 < c.n_layers ? W.layers[l + 1].attn_norm : W.final_norm;
         d.ssq_out = ssq_;
-        launch_gemm(bf(L.w_down), H, I, act, B, ks_down_, d, err_, s, pdl);
+        gemm(L.w_down, H, I, act, ks_down_, d);
         ssq_count = tiles_h;
     }
     GemmEpi lm;
@@ -290,7 +317,7 @@ void BatchEngine::enqueue_layers(int tiles) {
     lm.y = logits_;
     lm.am_v = am_v_;
     lm.am_i = am_i_;
-    launch_gemm(bf(W.tok_embeddings), V, H, pa, B, 1, lm, err_, s, pdl);
+    gemm(W.tok_embeddings, V, H, pa, 1, lm);
     launch_argmax_tiles(am_v_, am_i_, lm_tiles_, tok_, dpos_, B, s, pdl);
 }
 

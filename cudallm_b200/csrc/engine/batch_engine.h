@@ -4,7 +4,9 @@
 // (src/engine/engine.cpp:181-237) on its own token, position and KV cache, so a row's logits match what
 // the batch-1 engine computes for that sequence up to fp32 summation order. The weight matvecs become
 // GEMMs on the tcgen05 tensor cores (every weight byte is read once per step for the whole batch);
-// RMSNorm, residual adds, RoPE with the KV-cache write, SwiGLU and the logits' argmax partials are fused
+// Weights: bf16, or int4 (dequantised to exact bf16 codes inside the GEMM, group scales applied to fp32
+// partial sums). RMSNorm, residual adds, RoPE with the KV-cache write, SwiGLU and the logits' argmax
+// partials are fused
 // into the GEMM epilogues; attention runs per row. Several GPUs run one engine each on their own
 // sequence groups (no collective).
 #pragma once
@@ -73,6 +75,7 @@ private:
     cudaGraphExec_t graph_exec_ = nullptr;
     int graph_tiles_ = 0;  // attention tiles the captured graph covers (split attention only)
     bool attn_stream_ = true;
+    bool int4_ = false;  // int4 weights (codes re-packed at creation), else bf16
 
     // Per-operation K splits (cluster sizes of the GEMMs), chosen to fill the SMs.
     int ks_qkv_ = 1, ks_wo_ = 1, ks_gu_ = 1, ks_down_ = 1;

@@ -22,10 +22,11 @@
 
 namespace cudallm {
 
-// Most weight rows in one tile of the persistent kernel. int4 tiles stop at 4 rows (a 4 KiB tile for a
-// 2048-column matrix): a tile is one warp's work, and 16 int4 rows (32k weights to dequantise) per warp
-// would leave most consumer warps idle on the small operations while one warp works through its tile.
-__host__ __device__ constexpr int decode_step_tile_rows(WeightType wt) { return wt == WeightType::INT4 ? 4 : kMaxTileRows; }
+// Most weight rows in one tile of the persistent kernel. A tile is one consumer warp's work; int4 tiles
+// stop at 2 rows (a 1 KiB tile of a 2048-column matrix), since dequantising 16 int4 rows (32k weights) per
+// warp leaves most consumer warps idle on the small operations while one warp works through its tile
+// (measured: 16 rows 1277 tok/s, 4 rows 1517, 2 rows 1562; int8 is fastest at the default 16).
+__host__ __device__ constexpr int decode_step_tile_rows(WeightType wt) { return wt == WeightType::INT4 ? 2 : kMaxTileRows; }
 
 struct StepLayer {
     const float* attn_norm;

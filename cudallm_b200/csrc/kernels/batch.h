@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -64,8 +65,21 @@ int gemm_pick_ksplit(int n, int k);
 void launch_gemm(const __nv_bfloat16* w, int n, int k, const __nv_bfloat16* x, int batch, int ksplit, const GemmEpi& epi,
                  unsigned* err, cudaStream_t stream, bool pdl = false);
 
+// The same GEMM over int4 weights in the .cudallm layout (codes [n][k/2], two per byte, value (u - 8) *
+// scale; fp16 scales [n][k/128]) after interleave_int4_codes has re-packed the codes. k % 128 == 0,
+// ksplit <= min(16, k / 128) (K splits fall on 128-column groups).
+void launch_gemm_int4(const uint8_t* codes, const __half* scales, int n, int k, const __nv_bfloat16* x, int batch, int ksplit,
+                      const GemmEpi& epi, unsigned* err, cudaStream_t stream, bool pdl = false);
+int gemm_pick_ksplit_int4(int n, int k);
+
+// In place, every 32-bit word of int4 codes: byte j = columns (2j, 2j+1) -> byte j = columns (j, j+4)
+// of the word's 8 columns (low nibble first). launch_gemm_int4 and the batched embedding read this form.
+void interleave_int4_codes(void* codes, size_t bytes, cudaStream_t stream);
+
 // dst = the gate/up matrix [2 * inter][k] (gate rows, then up rows) with rows reordered so that every
 // 128-row tile t holds gate rows 64t..64t+63 followed by up rows 64t..64t+63 (inter % 64 == 0).
 void interleave_gate_up(const __nv_bfloat16* src, __nv_bfloat16* dst, int inter, int k, cudaStream_t stream);
+// The same row order for any per-row data of row_bytes bytes (a multiple of 16): int4 codes, group scales.
+void interleave_gate_up_rows(const void* src, void* dst, int inter, int row_bytes, cudaStream_t stream);
 
 }  // namespace cudallm

@@ -34,10 +34,13 @@ struct PlaneDst {
 };
 
 // Token of row b: tok_in[b] when >= 0 (fed by the caller), else the previous step's argmax tok[b].
-// x[b][j] = emb[token][j] (bf16 weights); planes of x[b][j] * gain[j] (the first RMSNorm's input) and
-// ssq[b] = sum_j x[b][j]^2 (reduced in a fixed order), one 256-thread block per row.
-__global__ void __launch_bounds__(256) embed_rows_kernel(const uint16_t* __restrict__ emb, const int* __restrict__ tok_in,
-                                                         const int* tok, const float* __restrict__ gain, float* __restrict__ x,
+// x[b][j] = embedding row of the token: bf16 weights, or int4 codes re-packed by interleave_int4_codes
+// ((u - 8) * fp16 scale of the 128-column group, in fp32); planes of x[b][j] * gain[j] (the first RMSNorm's
+// input) and ssq[b] = sum_j x[b][j]^2 (reduced in a fixed order), one 256-thread block per row.
+template <bool INT4>
+__global__ void __launch_bounds__(256) embed_rows_kernel(const void* __restrict__ emb, const __half* __restrict__ emb_s,
+                                                         const int* __restrict__ tok_in, const int* tok,
+                                                         const float* __restrict__ gain, float* __restrict__ x,
                                                          __nv_bfloat16* __restrict__ planes, float* __restrict__ ssq,
                                                          int hidden) {
     grid_dep_launch();
@@ -45,10 +48,18 @@ __global__ void __launch_bounds__(256) embed_rows_kernel(const uint16_t* __restr
     __shared__ float red[8];
     const int b = blockIdx.x;
     const int t = tok_in[b] >= 0 ? tok_in[b] : tok[b];
-    const uint16_t* row = emb + static_cast<size_t>(t) * hidden;
     float ss = 0.f;
     for (int j = threadIdx.x; j < hidden; j += blockDim.x) {
-        const float v = __uint_as_float(static_cast<uint32_t>(row[j]) << 16);
+        float v;
+        if constexpr (INT4) {
+            const uint32_t* row = static_cast<const uint32_t*>(emb) + static_cast<size_t>(t) * (hidden / 8);
+            const int c = j & 7;
+            const uint32_t code = (row[j >> 3] >> (8 * (c & 3) + 4 * (c >> 2))) & 0xFu;
+            v = static_cast<float>(static_cast<int>(code) - 8) * __half2float(emb_s[static_cast<size_t>(t) * (hidden / 128) + j / 128]);
+        } else {
+            const uint16_t* row = static_cast<const uint16_t*>(emb) + static_cast<size_t>(t) * hidden;
+            v = __uint_as_float(static_cast<uint32_t>(row[j]) << 16);
+        }
         x[static_cast<size_t>(b) * hidden + j] = v;
         ss = fmaf(v, v, ss);
         store_planes(planes, static_cast<size_t>(kBatchMax) * hidden, static_cast<size_t>(b) * hidden + j, v * gain[j]);
@@ -484,11 +495,17 @@ void launch_argmax_tiles(const float* am_v, const int* am_i, int n_tiles, int* t
     launch_kernel(argmax_tiles_kernel, dim3(batch), dim3(256), 0, stream, pdl, am_v, am_i, n_tiles, tok, pos);
 }
 
-void launch_embed_rows(const uint16_t* emb, const int* tok_in, const int* tok, const float* gain, float* x,
-                       __nv_bfloat16* planes, float* ssq, int batch, int hidden, cudaStream_t stream, bool pdl) {
-    CLLM_CHECK(emb && tok_in && tok && gain && x && planes && ssq && batch >= 1 && batch <= kBatchMax,
+void launch_embed_rows(const void* emb, const __half* emb_scales, const int* tok_in, const int* tok, const float* gain,
+                       float* x, __nv_bfloat16* planes, float* ssq, int batch, int hidden, cudaStream_t stream, bool pdl) {
+    CLLM_CHECK(emb && tok_in && tok && gain && x && planes && ssq && batch >= 1 && batch <= kBatchMax && hidden % 128 == 0,
                "launch_embed_rows: bad arguments");
-    launch_kernel(embed_rows_kernel, dim3(batch), dim3(256), 0, stream, pdl, emb, tok_in, tok, gain, x, planes, ssq, hidden);
+    if (emb_scales) {
+        launch_kernel(embed_rows_kernel<true>, dim3(batch), dim3(256), 0, stream, pdl, emb, emb_scales, tok_in, tok, gain, x,
+                      planes, ssq, hidden);
+    } else {
+        launch_kernel(embed_rows_kernel<false>, dim3(batch), dim3(256), 0, stream, pdl, emb, emb_scales, tok_in, tok, gain, x,
+                      planes, ssq, hidden);
+    }
 }
 
 void launch_rmsnorm_rows(const float* x, const float* w, float eps, __nv_bfloat16* out, int batch, int n, cudaStream_t stream,

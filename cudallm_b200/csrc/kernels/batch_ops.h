@@ -4,6 +4,7 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <cstddef>
@@ -12,10 +13,12 @@
 namespace cudallm {
 
 // Row b's token t = tok_in[b] when >= 0, else tok[b] (the previous argmax); x[b][:] = embedding row t
-// (bf16 weights), planes of x[b][j] * gain[j] and ssq[b] = sum_j x[b][j]^2 (the first RMSNorm's input and
-// statistics, ssq as one [1][64] partial).
-void launch_embed_rows(const uint16_t* emb, const int* tok_in, const int* tok, const float* gain, float* x,
-                       __nv_bfloat16* planes, float* ssq, int batch, int hidden, cudaStream_t stream, bool pdl = false);
+// (bf16 weights, or with emb_scales int4 codes re-packed by interleave_int4_codes and fp16 group scales),
+// planes of x[b][j] * gain[j] and ssq[b] = sum_j x[b][j]^2 (the first RMSNorm's input and statistics, ssq
+// as one [1][64] partial).
+void launch_embed_rows(const void* emb, const __half* emb_scales, const int* tok_in, const int* tok, const float* gain,
+                       float* x, __nv_bfloat16* planes, float* ssq, int batch, int hidden, cudaStream_t stream,
+                       bool pdl = false);
 // tok[b] = the best of the per-tile argmax partials am_v / am_i [batch][n_tiles] of row b (lowest index on
 // ties), pos[b] += 1.
 void launch_argmax_tiles(const float* am_v, const int* am_i, int n_tiles, int* tok, int* pos, int batch, cudaStream_t stream,

@@ -229,9 +229,9 @@ def test_errors(bf16_path, model_path):
     with pytest.raises(CudaLLMError) as e:
         BatchEngine(bf16_path, max_seq_len=100)
     assert e.value.code == 1
-    int4_path, _ = model_path("int4")
+    int8_path, _ = model_path("int8")
     with pytest.raises(CudaLLMError) as e:
-        BatchEngine(int4_path, n_seq=2)
+        BatchEngine(int8_path, n_seq=2)
     assert e.value.code == 1
     with BatchEngine(bf16_path, n_seq=2, max_seq_len=128) as eng:
         with pytest.raises(CudaLLMError) as e:
@@ -255,3 +255,51 @@ def test_errors(bf16_path, model_path):
         eng.reset()
         nxt, _ = eng.step(np.array([1, 2], dtype=np.int32))
         assert all(0 <= t < 128256 for t in nxt)
+
+
+# ---- int4 weights (codes dequantised inside the tensor-core GEMM, group scales on fp32 partial sums) ----
+
+@pytest.fixture(scope="module")
+def int4_run(model_path, golden):
+    g = golden("full_int4_fp16")
+    path, digest = model_path("int4")
+    assert digest == str(g["digest"]), "synthetic weights differ from the ones the golden run used"
+    rng = np.random.default_rng(4321)
+    lens = [len(g["prompt"]), 9, 30]
+    prompts = [[int(t) for t in g["prompt"]]] + [[int(t) for t in rng.integers(0, 128256, n)] for n in lens[1:]]
+    with BatchEngine(path, n_seq=len(prompts), max_seq_len=256) as eng:
+        last, ids = _run_batch(eng, prompts, GEN)
+    return {"prompts": prompts, "last": last, "ids": ids, "golden": g, "path": path}
+
+
+def test_int4_row0_matches_reference(int4_run):
+    g = int4_run["golden"]
+    assert int4_run["ids"][0] == [int(t) for t in g["ids"][:GEN]]
+    got = int4_run["last"][0]
+    assert np.abs(got - g["logits_31"]).max() < REF_LOGIT_TOL
+    assert int(np.argmax(got)) == int(np.argmax(g["logits_31"]))
+
+
+@pytest.mark.parametrize("row", range(3))
+def test_int4_rows_match_batch1_engine(int4_run, row):
+    prompt = int4_run["prompts"][row]
+    last, ids, margins = _bs1(int4_run["path"], prompt, GEN, max_seq_len=256)
+    assert np.abs(int4_run["last"][row] - last).max() < LOGIT_TOL
+    n_cmp = next((i for i, m in enumerate(margins) if m < MARGIN), GEN)
+    assert int4_run["ids"][row][:n_cmp] == ids[:n_cmp]
+
+
+def test_int4_full_batch_sampled_rows(model_path):
+    """64 rows of int4 (the benchmark's batch, streaming attention): rows 0 and 63 against the batch-1
+    engine on the same tokens."""
+    path, _ = model_path("int4")
+    rng = np.random.default_rng(77)
+    toks = rng.integers(0, 128256, (20, 64)).astype(np.int32)
+    with BatchEngine(path, n_seq=64, max_seq_len=128) as eng:
+        for i in range(20):
+            _, lg = eng.step(toks[i], want_logits=(i == 19))
+    for r in (0, 63):
+        with Engine(path, max_seq_len=128) as one:
+            for i in range(20):
+                _, ref = one.step(int(toks[i, r]), want_logits=True)
+        assert np.abs(lg[r] - ref).max() < LOGIT_TOL
