@@ -1,7 +1,7 @@
 """Kernel timeline of the batched decode step, from CUPTI activity records (torch.profiler).
 
-    python -m cudallm_b200.batch_timeline [--n-seq 64] [--prompt 512] [--steps 4] [--max-seq 768]
-                                          [--kv fp16|bf16] [--plain]
+    python -m cudallm_b200.batch_timeline [--dtype bf16|int4] [--n-seq 64] [--prompt 512] [--steps 4]
+                                          [--max-seq 768] [--kv fp16|bf16] [--plain]
 
 Steps a seeded random prompt through a BatchEngine (untimed), then records `--steps` decode steps and
 prints, per kernel: launches per step and device time per step; the span of a step; and, for layers 0, 1
@@ -27,7 +27,7 @@ def run(args) -> None:
     from . import synth
     from .engine import BatchEngine
 
-    path, _ = synth.ensure_model("bf16", seed=0, max_seq_len=4096)
+    path, _ = synth.ensure_model(args.dtype, seed=0, max_seq_len=4096)
     rng = np.random.default_rng(0)
     toks = rng.integers(0, 128256, (args.prompt, args.n_seq)).astype(np.int32)
     torch.cuda.init()
@@ -55,7 +55,7 @@ def run(args) -> None:
         agg[e.name][0] += 1
         agg[e.name][1] += e.time_range.elapsed_us()
     span = (evs[-1].time_range.end - evs[0].time_range.start) / args.steps
-    print(f"batched step: {args.n_seq} sequences, context {args.prompt}..{args.prompt + args.steps}, "
+    print(f"batched step ({args.dtype} weights): {args.n_seq} sequences, context {args.prompt}..{args.prompt + args.steps}, "
           f"{per_step} launches, span {span:.1f} us per step")
     print("device time per step (includes programmatic-dependent-launch waits):")
     for name, (n, us) in sorted(agg.items(), key=lambda kv: -kv[1][1]):
@@ -81,6 +81,7 @@ def run(args) -> None:
 
 def main(argv: list[str] | None = None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--dtype", choices=("bf16", "int4"), default="bf16")
     ap.add_argument("--n-seq", type=int, default=64)
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--steps", type=int, default=4)
