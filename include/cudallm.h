@@ -140,7 +140,7 @@ int cudallm_debug_read_trace(cudallm_engine* e, unsigned long long* out, unsigne
 /* ---- batched decode (no counterpart in the reference, whose engine holds one sequence): up to 64
  * independent sequences decoded together on one GPU, one token each per step; every row runs the
  * reference engine's per-token sequence (src/engine/engine.cpp:181-237) on its own token, position and KV
- * cache, with the weight matvecs as tensor-core GEMMs (bf16 weights). Several GPUs: one batch engine per
+ * cache, with the weight matvecs as tensor-core GEMMs (bf16 or int4 weights). Several GPUs: one batch engine per
  * device (device field), each on its own sequences; no communication between them. */
 typedef struct cudallm_batch cudallm_batch;
 
@@ -156,7 +156,7 @@ typedef struct {
 
 /* Fills n_seq 64, max_seq_len 0, kv fp16, device -1, cuda_graph 1. */
 void cudallm_default_batch_options(cudallm_batch_options* out);
-/* Loads a .cudallm file (bf16 weights) for n_seq sequences; *out = NULL on failure. */
+/* Loads a .cudallm file (bf16 or int4 weights; int8 returns INVALID_ARG) for n_seq sequences; *out = NULL on failure. */
 int cudallm_batch_create(const char* path, const cudallm_batch_options* opts, cudallm_batch** out);
 /* NULL-safe. */
 void cudallm_batch_destroy(cudallm_batch* e);
