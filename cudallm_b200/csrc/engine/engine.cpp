@@ -43,8 +43,10 @@ constexpr unsigned long long kStepWaitLimitNs = 1000000000ull;  // 1 s per inter
 // Contexts up to this many 64-token tiles use the whole-head attention (one CTA per KV head); longer ones
 // spread (head, tile) items over all CTAs. CUDALLM_WHOLE_HEAD_MAX_TILES overrides it.
 constexpr int kDefaultWholeHeadMaxTiles = 2;
-// L2 prefetch distance (tiles of 16 KiB per SM) of the persistent step; CUDALLM_PREFETCH_TILES overrides it.
+// L2 prefetch distance (tiles per SM) of the persistent step; CUDALLM_PREFETCH_TILES overrides it. 24 tiles
+// of 16 KiB for bf16 / int8; int4 tiles hold 2 rows (1-8 KiB), so the same byte distance is ~8x the tiles.
 constexpr int kDefaultPrefetchTiles = 24;
+constexpr int kDefaultPrefetchTilesInt4 = 192;
 
 }  // namespace
 
@@ -134,7 +136,7 @@ Engine::Engine(const std::string& path, const EngineOptions& opts) : opts_(opts)
             p.eps = c.rms_eps;
             p.group_size = c.group_size;
             p.wait_limit_ns = kStepWaitLimitNs;
-            p.prefetch_tiles = kDefaultPrefetchTiles;
+            p.prefetch_tiles = c.wtype == WeightType::INT4 ? kDefaultPrefetchTilesInt4 : kDefaultPrefetchTiles;
             if (const char* env = std::getenv("CUDALLM_PREFETCH_TILES")) p.prefetch_tiles = std::max(0, std::atoi(env));
             p.prefetch_mode = 3;  // bulk L2 prefetches from the prefetch warp
             if (const char* env = std::getenv("CUDALLM_PREFETCH_MODE")) p.prefetch_mode = std::atoi(env);
