@@ -298,6 +298,11 @@ def config_block(args) -> dict:
 
 def run_ours(args) -> None:
     rank, world, local_rank = dist_info()
+    # Native libraries (NCCL prints its version banner at communicator creation) may write to file
+    # descriptor 1; until the result line, descriptor 1 points at stderr so stdout carries that line only.
+    sys.stdout.flush()
+    saved_stdout = os.dup(1)
+    os.dup2(2, 1)
     import torch
     import torch.distributed as dist
     torch.cuda.set_device(local_rank)
@@ -378,6 +383,9 @@ def run_ours(args) -> None:
 
     if world > 1:
         dist.barrier()
+    sys.stdout.flush()
+    os.dup2(saved_stdout, 1)
+    os.close(saved_stdout)
     if rank == 0:
         value = world * args.steps / (total_ms * 1e-3)
         line = {
