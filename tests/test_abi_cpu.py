@@ -176,3 +176,50 @@ def test_header_struct_offsets():
     raw = _header_bytes()
     assert len(raw) == 256
     assert struct.unpack_from("<Q", raw, 64)[0] == 256
+
+
+# ---- batched entry points (cudallm_batch_*): host-side checks, no GPU ----
+
+def _batch_create(lib, path, **overrides):
+    o = E.CudallmBatchOptions()
+    lib.cudallm_default_batch_options(ctypes.byref(o))
+    for k, v in overrides.items():
+        setattr(o, k, v)
+    h = ctypes.c_void_p()
+    rc = lib.cudallm_batch_create(str(path).encode(), ctypes.byref(o), ctypes.byref(h))
+    assert h.value is None  # nothing is created on failure
+    return rc, lib.cudallm_last_error().decode()
+
+
+def test_batch_options_layout_and_defaults(native_lib):
+    assert ctypes.sizeof(E.CudallmBatchOptions) == 40
+    o = E.CudallmBatchOptions()
+    native_lib.cudallm_default_batch_options(ctypes.byref(o))
+    assert (o.struct_size, o.n_seq, o.max_seq_len, o.kv_dtype, o.device, o.cuda_graph) == (40, 64, 0, 0, -1, 1)
+    native_lib.cudallm_default_batch_options(None)  # NULL-safe
+
+
+def test_batch_create_rejects_before_device_work(native_lib, model_path, tmp_path):
+    rc, _ = _batch_create(native_lib, tmp_path / "missing.cudallm")
+    assert rc == ERR_IO
+    path, _ = model_path("int8")
+    rc, msg = _batch_create(native_lib, path)
+    assert rc == ERR_INVALID_ARG and "bf16 and int4" in msg
+    for bad in ({"n_seq": 0}, {"n_seq": 65}, {"max_seq_len": 100}, {"max_seq_len": 8192}, {"kv_dtype": 2},
+                {"struct_size": 36}):
+        rc, msg = _batch_create(native_lib, path, **bad)
+        assert rc == ERR_INVALID_ARG, (bad, msg)
+
+
+def test_null_batch_engine_calls(native_lib):
+    assert native_lib.cudallm_batch_pos(None, 0) == -1
+    native_lib.cudallm_batch_destroy(None)
+    assert native_lib.cudallm_batch_reset(None, -1) == ERR_INVALID_ARG
+    assert native_lib.cudallm_batch_step(None, None, None, None) == ERR_INVALID_ARG
+    assert native_lib.cudallm_batch_synchronize(None) == ERR_INVALID_ARG
+    assert native_lib.cudallm_batch_stream(None) is None
+    info = E.CudallmConfigInfo()
+    assert native_lib.cudallm_batch_get_config(None, ctypes.byref(info)) == ERR_INVALID_ARG
+    o = E.CudallmBatchOptions()
+    native_lib.cudallm_default_batch_options(ctypes.byref(o))
+    assert native_lib.cudallm_batch_create(None, ctypes.byref(o), None) == ERR_INVALID_ARG
