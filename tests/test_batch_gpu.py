@@ -1,4 +1,4 @@
-"""GPU: batched decode (cudallm_batch_* entry points) on the seeded Llama-3.2-1B bf16 file.
+"""GPU: batched decode (cudallm_batch_* entry points) on the seeded Llama-3.2-1B bf16 and int4 files.
 
 Every row of the batch is one independent sequence. Each row is checked against what the batch-1 engine
 computes for the same sequence, and row 0 (fed the golden prompt) against wasiqnauman/cudallm's own
@@ -11,7 +11,9 @@ ReferenceModel run (golden_full_bf16_fp16.npz):
   * rows see only their own token, position and KV cache: equal inputs give bitwise-equal logits, a
     reset row reproduces its first run bitwise, and graph replay equals direct launches bitwise;
   * contexts crossing the 256-token boundaries at which the step's graph is captured again stay in
-    agreement with the batch-1 engine (teacher-forced on the same tokens).
+    agreement with the batch-1 engine (teacher-forced on the same tokens);
+  * int4 weights (golden_full_int4_fp16.npz): row 0 reproduces the reference's 64 greedy ids and logits,
+    every row's logits are within 2e-3 of the batch-1 int4 engine's, including rows of a 64-row batch.
 """
 from __future__ import annotations
 
