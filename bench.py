@@ -15,6 +15,13 @@ Also measured on every rank (unless --quick): batched decode 
 (512-token prompts, then timed greedy decode steps; tensor-core GEMMs) with bf16 and with int4 weights,
 reported under "batched" ({"bf16": ..., "int4": ...}) as the whole-job tok/s over all ranks.
 
+On one GPU (unless --quick) the line also carries the configured workloads whatever --steps is:
+  * "gen256": the headline precision over the configured 256 decode steps (positions 32..287);
+  * "precisions": bf16 / int8 / int4 over the same 256 steps (BASELINE configs 1-3);
+  * "long_context": BASELINE config 4, bf16 weights in a max_seq_len 32896 file: the KV cache is filled by
+    stepping seeded random tokens (untimed) to 4096 and then 32768 cached tokens, and 128 greedy decode steps
+    are timed at each context (bytes per token include the KV read at the step's context).
+
 Reported (one JSON line on rank 0): value = tok/s with weights resident; e2e = tok/s through the C ABI
 when every step takes its token from the host and returns the next token to the host; roofline of the
 persistent decode-step kernel (algorithmic bytes = weight bytes + KV bytes read at the step's context,
@@ -168,6 +175,54 @@ def time_e2e(eng, prompt: list[int], steps: int, torch, barrier) -> dict:
     wall = time.perf_counter() - t0
     barrier()
     return {"total_ms": start.elapsed_time(end), "wall_ms": wall * 1e3}
+
+
+CONFIG_GEN = 256                           # greedy decode of 256 tokens
+LONG_MAX_SEQ, LONG_CTX, LONG_GEN = 32896, (4096, 32768), 128
+
+
+def time_long_context(args, device: int, torch, peak_gbs: float) -> dict:
+    """BASELINE config 4 on the persistent path: one engine (bf16 weights, max_seq_len 32896) steps seeded
+    random tokens untimed until `ctx` tokens are cached, then 128 greedy decode steps are timed with per-launch
+    CUDA events on the engine's stream; first at 4096 cached tokens, then (continuing the same sequence) at
+    32768."""
+    from cudallm_b200 import synth
+    from cudallm_b200.engine import Engine
+    path, _ = synth.ensure_model("bf16", seed=0, max_seq_len=LONG_MAX_SEQ)
+    toks = synth.prompt_ids(max(LONG_CTX), seed=0)
+    out = {}
+    with Engine(path, kv_dtype=args.kv, device=device, max_seq_len=LONG_MAX_SEQ) as eng:
+        assert eng.decode_path == "persistent"
+        weight_bytes = eng.config["weight_bytes"]
+        stream = torch.cuda.ExternalStream(eng.stream_handle, device=torch.device("cuda", device))
+        pos = 0
+        for ctx in LONG_CTX:
+            t0 = time.perf_counter()
+            while pos < ctx:
+                eng.step_async(toks[pos])
+                pos += 1
+            eng.synchronize()
+            fill_s = time.perf_counter() - t0
+            starts = [torch.cuda.Event(enable_timing=True) for _ in range(LONG_GEN)]
+            ends = [torch.cuda.Event(enable_timing=True) for _ in range(LONG_GEN)]
+            torch.cuda.synchronize(device)
+            for i in range(LONG_GEN):
+                starts[i].record(stream)
+                eng.step_async(None)
+                ends[i].record(stream)
+            eng.synchronize()
+            torch.cuda.synchronize(device)
+            pos += LONG_GEN
+            total_ms = starts[0].elapsed_time(ends[-1])
+            kms = sum(s.elapsed_time(e) for s, e in zip(starts, ends)) / LONG_GEN
+            b = weight_bytes + KV_BYTES_PER_TOKEN * (ctx + (LONG_GEN + 1) / 2)
+            out[str(ctx)] = {"tok_s": LONG_GEN / (total_ms * 1e-3), "ms_per_token": total_ms / LONG_GEN,
+                             "positions": f"{ctx}..{ctx + LONG_GEN - 1}", "bytes_per_token": int(b),
+                             "achieved_gbs": b / (kms * 1e-3) / 1e9, "roofline_frac": b / (kms * 1e-3) / 1e9 / peak_gbs,
+                             "untimed_fill_s": fill_s}
+    out["note"] = ("bf16 weights, max_seq_len 32896; cache filled by stepping seeded random tokens one at a time "
+                   "(untimed); 128 greedy decode steps timed per context")
+    return out
 
 
 BATCH_SEQS, BATCH_PROMPT, BATCH_GEN = 64, 512, 256  # BASELINE config 5, per GPU
@@ -332,9 +387,11 @@ def run_ours(args) -> None:
                 clocks = clk.summary()
                 e = time_e2e(eng, prompt, args.steps, torch, barrier)
             else:
-                t = time_decode(eng, prompt, args.steps, args.warmup, torch, barrier)
-                e, clocks = None, None
-        results[dt] = {"t": t, "e": e, "clocks": clocks, "weight_bytes": weight_bytes}
+                t, e, clocks = None, None, None
+            # The configured workload (256 decode steps) on one GPU, whatever --steps is.
+            t256 = (t if args.steps == CONFIG_GEN else time_decode(eng, prompt, CONFIG_GEN, args.warmup, torch, lambda: None)) \
+                if world == 1 else None
+        results[dt] = {"t": t, "e": e, "clocks": clocks, "weight_bytes": weight_bytes, "t256": t256}
 
     head = results[args.dtype]
     total_ms = max_over_ranks(head["t"]["total_ms"])
@@ -344,14 +401,17 @@ def run_ours(args) -> None:
     avg_ctx = PROMPT_LEN + (args.steps + 1) / 2
     bytes_per_step = head["weight_bytes"] + KV_BYTES_PER_TOKEN * avg_ctx
     achieved = bytes_per_step / (avg_kernel_ms * 1e-3) / 1e9
-    extra = {}
-    for dt, r in results.items():
-        ms = r["t"]["total_ms"]
-        kms = sum(r["t"]["kernel_ms"]) / len(r["t"]["kernel_ms"])
-        b = r["weight_bytes"] + KV_BYTES_PER_TOKEN * avg_ctx
-        extra[dt] = {"tok_s": args.steps / (ms * 1e-3), "bytes_per_token": int(b),
-                     "roofline_frac": (b / (kms * 1e-3) / 1e9) / peaks["hbm_gbs"],
-                     "achieved_gbs": b / (kms * 1e-3) / 1e9, "ms_per_token": ms / args.steps}
+
+    def summarise(t: dict, weight_bytes: int, steps: int) -> dict:
+        kms = sum(t["kernel_ms"]) / len(t["kernel_ms"])
+        b = weight_bytes + KV_BYTES_PER_TOKEN * (PROMPT_LEN + (steps + 1) / 2)
+        return {"tok_s": steps / (t["total_ms"] * 1e-3), "bytes_per_token": int(b),
+                "roofline_frac": (b / (kms * 1e-3) / 1e9) / peaks["hbm_gbs"], "achieved_gbs": b / (kms * 1e-3) / 1e9,
+                "ms_per_token": t["total_ms"] / steps, "positions": f"{PROMPT_LEN}..{PROMPT_LEN + steps - 1}"}
+
+    extra = {dt: summarise(r["t256"], r["weight_bytes"], CONFIG_GEN) for dt, r in results.items() if r["t256"]}
+    gen256 = extra.get(args.dtype)
+    long_context = time_long_context(args, local_rank, torch, peaks["hbm_gbs"]) if (world == 1 and not args.quick) else None
 
     batched = {}
     if not args.quick:
@@ -402,7 +462,9 @@ def run_ours(args) -> None:
             "cpu_baseline": cpu,
             "gpu_launches": args.steps,
             "clocks": head["clocks"],
+            "gen256": gen256,
             "precisions": extra,
+            "long_context": long_context,
             "batched": batched,
         }
         print(json.dumps(line), flush=True)

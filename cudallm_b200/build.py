@@ -32,7 +32,7 @@ NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", "-Xc
               "-Xptxas", "-warn-spills", *ARCH]
 INCLUDES = [f"-I{CSRC}", f"-I{INCLUDE}"]
 
-# Library sources (everything except the tools' mains).
+# The command-line tools (each a main linked with the library's objects); every other source is the library.
 TOOLS = {
     "cudallm_bench": "tools/bench_main.cpp",
     "cudallm_kernelbench": "tools/kernelbench_main.cpp",
@@ -78,7 +78,7 @@ def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -
     all_files = [p for p in CSRC.rglob("*") if p.is_file()] + [p for p in INCLUDE.rglob("*.h")]
     stamp = _stamp(all_files)
     stamp_file = OBJ / "stamp"
-    tool_bins = [BIN_DIR / name for name in TOOLS]
+    tool_bins = [BIN_DIR / name for name, rel in TOOLS.items() if (CSRC / rel).exists()]
     if (not force and stamp_file.exists() and stamp_file.read_text() == stamp and LIB_PATH.exists()
             and all(b.exists() for b in tool_bins)):
         return LIB_PATH

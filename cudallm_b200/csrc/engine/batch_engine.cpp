@@ -5,7 +5,6 @@
 
 #include <algorithm>
 #include <cstdio>
-#include <cstdlib>
 #include <string>
 
 #include "common/check.h"
@@ -51,9 +50,11 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
     } else {
         CLLM_CUDA(cudaGetDevice(&device_));
     }
-    if (const char* env = std::getenv("CUDALLM_BATCH_PDL")) opts_.pdl = std::atoi(env) != 0;
-    if (const char* env = std::getenv("CUDALLM_BATCH_ATTN")) opts_.attn_mode = std::atoi(env);
     if (opts_.attn_mode < 0 || opts_.attn_mode > 2) throw ArgError("attention mode must be 0, 1 or 2");
+    ext_kv_ = opts_.ext_k_cache != nullptr || opts_.ext_v_cache != nullptr;
+    if (ext_kv_ && (opts_.ext_k_cache == nullptr || opts_.ext_v_cache == nullptr || opts_.n_seq != kBatchMax)) {
+        throw ArgError("a prefill engine needs both external caches and n_seq 64");
+    }
     DeviceGuard guard(device_);
     weights_ = std::make_unique<Weights>(file);
     const ModelConfig& c = weights_->config();
@@ -70,7 +71,7 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
                    "batched decode: unsupported model shape");
         // One streaming CTA per (KV head, sequence) once that fills the SMs; fewer sequences split their
         // contexts over more CTAs.
-        attn_stream_ = opts_.attn_mode == 1 || (opts_.attn_mode == 0 && opts_.n_seq * NKV >= sms);
+        attn_stream_ = ext_kv_ || opts_.attn_mode == 1 || (opts_.attn_mode == 0 && opts_.n_seq * NKV >= sms);
         int4_ = c.wtype == WeightType::INT4;
         CLLM_CHECK(!int4_ || c.group_size == 128, "batched decode: int4 needs 128-column scale groups");
         auto pick = [&](int n, int k) { return int4_ ? gemm_pick_ksplit_int4(n, k) : gemm_pick_ksplit(n, k); };
@@ -79,24 +80,6 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
         ks_gu_ = pick(2 * I, H);
         ks_down_ = pick(H, I);
         lm_tiles_ = (V + kGemmTileRows - 1) / kGemmTileRows;
-        if (const char* env = std::getenv("CUDALLM_BATCH_KSPLIT")) {
-            // "qkv,wo,gate_up,down": explicit K splits (each 1..16 and at most k / 64).
-            int v[4] = {0, 0, 0, 0};
-            if (std::sscanf(env, "%d,%d,%d,%d", &v[0], &v[1], &v[2], &v[3]) != 4) throw ArgError("CUDALLM_BATCH_KSPLIT: want a,b,c,d");
-            const int unit = int4_ ? 128 : 64;  // int4 splits fall on 128-column groups
-            const int kmax[4] = {H / unit, NH * D / unit, H / unit, I / unit};
-            for (int i = 0; i < 4; ++i) {
-                if (v[i] < 1 || v[i] > 16 || v[i] > kmax[i]) throw ArgError("CUDALLM_BATCH_KSPLIT: split out of range");
-            }
-            ks_qkv_ = v[0];
-            ks_wo_ = v[1];
-            ks_gu_ = v[2];
-            ks_down_ = v[3];
-        }
-        if (std::getenv("CUDALLM_BATCH_VERBOSE")) {
-            std::fprintf(stderr, "cudallm batch: K splits qkv %d wo %d gate/up %d down %d; attention %s; pdl %d\n", ks_qkv_, ks_wo_,
-                         ks_gu_, ks_down_, attn_stream_ ? "stream" : "split", opts_.pdl ? 1 : 0);
-        }
         const size_t B = kBatchMax;
         alloc_zero(&x_, B * H);
         alloc_zero(reinterpret_cast<__nv_bfloat16**>(&pa_), 2 * B * H);
@@ -107,11 +90,18 @@ BatchEngine::BatchEngine(const std::string& path, const BatchOptions& opts) : op
         alloc_zero(&logits_, B * V);
         alloc_zero(&am_v_, B * lm_tiles_);
         alloc_zero(&am_i_, B * lm_tiles_);
-        const size_t cache_elems = static_cast<size_t>(opts_.n_seq) * c.n_layers * NKV * max_seq_ * D;
-        CLLM_CUDA(cudaMalloc(&k_cache_, cache_elems * 2));
-        CLLM_CUDA(cudaMalloc(&v_cache_, cache_elems * 2));
-        CLLM_CUDA(cudaMemset(k_cache_, 0, cache_elems * 2));
-        CLLM_CUDA(cudaMemset(v_cache_, 0, cache_elems * 2));
+        if (ext_kv_) {
+            k_cache_ = opts_.ext_k_cache;
+            v_cache_ = opts_.ext_v_cache;
+        } else {
+            const size_t cache_elems = static_cast<size_t>(opts_.n_seq) * c.n_layers * NKV * max_seq_ * D;
+            CLLM_CUDA(cudaMalloc(&k_cache_, cache_elems * 2));
+            CLLM_CUDA(cudaMalloc(&v_cache_, cache_elems * 2));
+            CLLM_CUDA(cudaMemset(k_cache_, 0, cache_elems * 2));
+            CLLM_CUDA(cudaMemset(v_cache_, 0, cache_elems * 2));
+        }
+        alloc_zero(&tok_save_, static_cast<size_t>(kBatchMax) + 1);
+        alloc_zero(&last_logits_, static_cast<size_t>(V));
         if (!attn_stream_) {
             const size_t slots = static_cast<size_t>(max_seq_ / kAttnTile);
             alloc_zero(&att_o_, B * NH * slots * D);
@@ -166,11 +156,17 @@ void BatchEngine::free_all() noexcept {
     if (graph_) report(cudaGraphDestroy(graph_), "cudaGraphDestroy");
     graph_exec_ = nullptr;
     graph_ = nullptr;
-    void* bufs[] = {x_,    pa_,      pb_,      act_,   ssq_,    qkv_, logits_, am_v_, am_i_,
-                    k_cache_, v_cache_, att_o_, att_ml_, tok_in_, tok_, dpos_,   err_};
+    void* bufs[] = {x_,      pa_,   pb_,   act_,   ssq_,      qkv_,         logits_, am_v_, am_i_,
+                    att_o_,  att_ml_, tok_in_, tok_, dpos_, err_, tok_save_, last_logits_};
     for (void* b : bufs) {
         if (b) report(cudaFree(b), "cudaFree");
     }
+    if (!ext_kv_) {
+        if (k_cache_) report(cudaFree(k_cache_), "cudaFree");
+        if (v_cache_) report(cudaFree(v_cache_), "cudaFree");
+    }
+    tok_save_ = nullptr;
+    last_logits_ = nullptr;
     x_ = ssq_ = qkv_ = logits_ = am_v_ = att_o_ = att_ml_ = nullptr;
     pa_ = pb_ = act_ = k_cache_ = v_cache_ = nullptr;
     am_i_ = tok_in_ = tok_ = dpos_ = nullptr;
@@ -190,6 +186,51 @@ BatchEngine::~BatchEngine() {
     } catch (...) {
         std::fprintf(stderr, "cudallm: unknown exception in ~BatchEngine\n");
     }
+}
+
+void BatchEngine::set_knob(const std::string& name, long long value) {
+    const ModelConfig& c = config();
+    const int unit = int4_ ? 128 : 64;  // int4 K splits fall on 128-column scale groups
+    auto in = [&](long long lo, long long hi) {
+        if (value < lo || value > hi) {
+            throw ArgError("knob " + name + " must be in [" + std::to_string(lo) + ", " + std::to_string(hi) + "]");
+        }
+    };
+    if (name == "pdl") {
+        in(0, 1);
+        opts_.pdl = value != 0;
+    } else if (name == "ksplit_qkv") {
+        in(1, std::min(16, c.hidden / unit));
+        ks_qkv_ = static_cast<int>(value);
+    } else if (name == "ksplit_wo") {
+        in(1, std::min(16, c.n_heads * c.head_dim / unit));
+        ks_wo_ = static_cast<int>(value);
+    } else if (name == "ksplit_gate_up") {
+        in(1, std::min(16, c.hidden / unit));
+        ks_gu_ = static_cast<int>(value);
+    } else if (name == "ksplit_down") {
+        in(1, std::min(16, c.inter / unit));
+        ks_down_ = static_cast<int>(value);
+    } else {
+        throw ArgError("unknown knob '" + name + "' (pdl, ksplit_qkv, ksplit_wo, ksplit_gate_up, ksplit_down)");
+    }
+    // The captured step holds the old launch configuration: capture again at the next step.
+    synchronize();
+    DeviceGuard guard(device_);
+    if (graph_exec_) CLLM_CUDA(cudaGraphExecDestroy(graph_exec_));
+    if (graph_) CLLM_CUDA(cudaGraphDestroy(graph_));
+    graph_exec_ = nullptr;
+    graph_ = nullptr;
+}
+
+int BatchEngine::knob(const std::string& name) const {
+    if (name == "pdl") return opts_.pdl ? 1 : 0;
+    if (name == "ksplit_qkv") return ks_qkv_;
+    if (name == "ksplit_wo") return ks_wo_;
+    if (name == "ksplit_gate_up") return ks_gu_;
+    if (name == "ksplit_down") return ks_down_;
+    if (name == "attn_stream") return attn_stream_ ? 1 : 0;
+    throw ArgError("unknown knob '" + name + "'");
 }
 
 int BatchEngine::pos(int seq) const {
@@ -235,9 +276,12 @@ void BatchEngine::enqueue_layers(int tiles) {
     const int B = opts_.n_seq, H = c.hidden, I = c.inter, V = c.vocab, NH = c.n_heads, NKV = c.n_kv_heads, D = c.head_dim;
     const int QKV = (NH + 2 * NKV) * D;
     const size_t layer_elems = static_cast<size_t>(NKV) * max_seq_ * D;
-    const size_t seq_stride = layer_elems * c.n_layers;
-    KV* kc = static_cast<KV*>(k_cache_);
-    KV* vc = static_cast<KV*>(v_cache_);
+    // A prefill step points every row at sequence pf_seq_'s cache (stride 0); a decode step gives row b
+    // sequence b's cache.
+    const bool one_seq = pf_seq_ >= 0;
+    const size_t seq_stride = one_seq ? 0 : layer_elems * c.n_layers;
+    KV* kc = static_cast<KV*>(k_cache_) + (one_seq ? static_cast<size_t>(pf_seq_) * layer_elems * c.n_layers : 0);
+    KV* vc = static_cast<KV*>(v_cache_) + (one_seq ? static_cast<size_t>(pf_seq_) * layer_elems * c.n_layers : 0);
     auto* pa = static_cast<__nv_bfloat16*>(pa_);
     auto* pb = static_cast<__nv_bfloat16*>(pb_);
     auto* act = static_cast<__nv_bfloat16*>(act_);
@@ -279,7 +323,7 @@ void BatchEngine::enqueue_layers(int tiles) {
         q.kv_bf16 = kv_bf16;
         gemm(L.wqkv, QKV, H, pa, ks_qkv_, q);
         if (attn_stream_) {
-            launch_attention_rows_stream<KV>(qkv_, kl, vl, seq_stride, dpos_, pb, B, NH, NKV, max_seq_, err_, s, pdl);
+            launch_attention_rows_stream<KV>(qkv_, kl, vl, seq_stride, dpos_, pb, B, NH, NKV, max_seq_, err_, s, pdl, one_seq);
         } else {
             launch_attention_rows<KV>(qkv_, kl, vl, seq_stride, dpos_, tiles * kAttnTile, att_o_, att_ml_, pb, B, NH, NKV,
                                       max_seq_, s, pdl);
@@ -308,6 +352,7 @@ void BatchEngine::enqueue_layers(int tiles) {
         gemm(L.w_down, H, I, act, ks_down_, d);
         ssq_count = tiles_h;
     }
+    if (pf_skip_logits_) return;  // a prefill chunk that is not the last needs no logits
     GemmEpi lm;
     lm.kind = GemmEpilogue::LOGITS;
     lm.ssq_in = ssq_;
@@ -329,7 +374,76 @@ void BatchEngine::enqueue_step(int tiles) {
     }
 }
 
+void BatchEngine::set_position(int seq, int pos) {
+    CLLM_REQUIRE(seq >= 0 && seq < opts_.n_seq && pos >= 0 && pos <= max_seq_, "set_position: out of range");
+    synchronize();
+    DeviceGuard guard(device_);
+    CLLM_CUDA(cudaMemcpy(dpos_ + seq, &pos, sizeof(int), cudaMemcpyHostToDevice));
+    host_pos_[seq] = pos;
+}
+
+void BatchEngine::prefill(int seq, const int* tokens, int n, float* logits_out, int* next_out) {
+    CLLM_REQUIRE(seq >= 0 && seq < (ext_kv_ ? 1 : opts_.n_seq), "prefill: sequence index out of range");
+    CLLM_REQUIRE(tokens != nullptr && n >= 1, "prefill: need at least one token");
+    CLLM_REQUIRE(opts_.n_seq == kBatchMax, "prefill: needs an engine of 64 rows");
+    const int start = host_pos_[seq];
+    if (static_cast<long long>(start) + n > max_seq_) throw StateError("prefill: the tokens do not fit in max_seq_len");
+    for (int i = 0; i < n; ++i) CLLM_REQUIRE(tokens[i] >= 0 && tokens[i] < config().vocab, "prefill: token out of range");
+    synchronize();
+    DeviceGuard guard(device_);
+    const int B = kBatchMax;
+    // The rows' previous argmax (device state of every sequence) is kept aside; positions are restored from
+    // the host mirror afterwards.
+    CLLM_CUDA(cudaMemcpyAsync(tok_save_, tok_, sizeof(int) * B, cudaMemcpyDeviceToDevice, stream_));
+    pf_host_.resize(2 * B);
+    int last_row = 0;
+    pf_seq_ = seq;
+    try {
+        for (int i0 = 0; i0 < n; i0 += B) {
+            const int m = std::min(B, n - i0);
+            // Row b < m: token i0+b at position start+i0+b. Rows past m repeat the last one (same token and
+            // position, so they write the same cache values to the same slot).
+            for (int b = 0; b < B; ++b) {
+                const int i = std::min(b, m - 1);
+                pf_host_[b] = tokens[i0 + i];
+                pf_host_[B + b] = start + i0 + i;
+            }
+            CLLM_CUDA(cudaMemcpyAsync(tok_in_, pf_host_.data(), sizeof(int) * B, cudaMemcpyHostToDevice, stream_));
+            CLLM_CUDA(cudaMemcpyAsync(dpos_, pf_host_.data() + B, sizeof(int) * B, cudaMemcpyHostToDevice, stream_));
+            pf_skip_logits_ = i0 + m < n;
+            enqueue_step(max_seq_ / kAttnTile);
+            last_row = m - 1;
+        }
+    } catch (...) {
+        pf_seq_ = -1;
+        pf_skip_logits_ = false;
+        throw;
+    }
+    pf_seq_ = -1;
+    pf_skip_logits_ = false;
+    const int V = config().vocab;
+    CLLM_CUDA(cudaMemcpyAsync(last_logits_, logits_ + static_cast<size_t>(last_row) * V, sizeof(float) * V,
+                              cudaMemcpyDeviceToDevice, stream_));
+    CLLM_CUDA(cudaMemcpyAsync(tok_save_ + B, tok_ + last_row, sizeof(int), cudaMemcpyDeviceToDevice, stream_));
+    CLLM_CUDA(cudaMemcpyAsync(tok_save_ + seq, tok_ + last_row, sizeof(int), cudaMemcpyDeviceToDevice, stream_));
+    CLLM_CUDA(cudaMemcpyAsync(tok_, tok_save_, sizeof(int) * B, cudaMemcpyDeviceToDevice, stream_));
+    host_pos_[seq] = start + n;
+    std::vector<int> pos_now(B, 0);
+    for (int b = 0; b < opts_.n_seq; ++b) pos_now[b] = host_pos_[b];
+    CLLM_CUDA(cudaMemcpyAsync(dpos_, pos_now.data(), sizeof(int) * B, cudaMemcpyHostToDevice, stream_));
+    CLLM_CUDA(cudaMemsetAsync(tok_in_, 0xff, sizeof(int) * B, stream_));  // the next step feeds argmaxes
+    tok_in_fed_ = false;
+    if (logits_out != nullptr) {
+        CLLM_CUDA(cudaMemcpyAsync(logits_out, last_logits_, sizeof(float) * V, cudaMemcpyDeviceToHost, stream_));
+    }
+    int next = 0;
+    CLLM_CUDA(cudaMemcpyAsync(&next, tok_save_ + B, sizeof(int), cudaMemcpyDeviceToHost, stream_));
+    synchronize();
+    if (next_out != nullptr) *next_out = next;
+}
+
 void BatchEngine::step(const int* tokens, int* next_out, float* logits_out) {
+    if (ext_kv_) throw StateError("step: a prefill engine only runs prefill");
     const int B = opts_.n_seq;
     int longest = 0;
     for (int b = 0; b < B; ++b) {

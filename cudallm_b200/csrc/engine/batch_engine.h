@@ -18,6 +18,7 @@
 #include <vector>
 
 #include "common/dtype.h"
+#include "kernels/batch.h"
 #include "model/weights.h"
 
 namespace cudallm {
@@ -32,6 +33,11 @@ struct BatchOptions {
     // Attention kernel: 0 = choose by size, 1 = one CTA per (KV head, sequence) streaming the whole
     // context, 2 = split over 64-token tiles and merged by a second kernel (more CTAs for few sequences).
     int attn_mode = 0;
+    // Prefill engine of another engine's sequence: with both set (n_seq must be 64), the KV cache is this
+    // caller-owned pair ([layers][kv heads][max_seq][64] in the cache type, one sequence) and the engine
+    // only runs prefill(0, ...); it allocates no cache of its own.
+    void* ext_k_cache = nullptr;
+    void* ext_v_cache = nullptr;
 };
 
 class BatchEngine {
@@ -56,8 +62,27 @@ public:
     // -1. next_out: host [n_seq] or null; logits_out: host [n_seq][vocab] or null. With both outputs null
     // the call does not synchronise.
     void step(const int* tokens, int* next_out, float* logits_out);
+    // Prompt prefill of sequence seq: tokens[0..n) at positions pos(seq) .. pos(seq)+n-1, 64 per batched
+    // step. Every row of a step is one position of that sequence (its KV cache at stride 0, position
+    // increasing with the row), so the GEMMs compute 64 prompt tokens at once on the tensor cores and row b's
+    // attention covers the positions up to its own (causal). Equivalent to feeding the tokens one per step
+    // (up to fp32 summation order). Afterwards the sequence's position has advanced by n and its next token
+    // is the argmax after tokens[n-1]; next_out (host, or null) gets it and logits_out (host [vocab], or
+    // null) that step's logits. The other sequences keep their positions and previous argmax. Synchronises.
+    void prefill(int seq, const int* tokens, int n, float* logits_out, int* next_out);
+    // Prefill engines: the position their sequence continues from (host mirror and device word).
+    void set_position(int seq, int pos);
+    // Device copies of the last prefill's final logits row [vocab] and next token (valid until the next call).
+    const float* last_logits() const { return last_logits_; }
+    const int* last_token() const { return tok_save_ + kBatchMax; }
     // Waits for queued steps and reports a device-side failure (a timed-out wait in a GEMM).
     void synchronize();
+    // Validated tuning knobs, by name (ArgError when unknown or out of range): "pdl" (0/1, programmatic
+    // dependent launch between the step's kernels), "ksplit_qkv", "ksplit_wo", "ksplit_gate_up",
+    // "ksplit_down" (K split = cluster size of that GEMM, 1 .. min(16, k / 64), int4 k / 128). The next step
+    // captures its graph again. knob() reads them back, and "attn_stream" (1: streaming attention).
+    void set_knob(const std::string& name, long long value);
+    int knob(const std::string& name) const;
 
 private:
     template <typename KV>
@@ -99,6 +124,12 @@ private:
     int* dpos_ = nullptr;             // [64] position per sequence
     unsigned* err_ = nullptr;         // device error word
     bool tok_in_fed_ = false;         // tok_in_ holds fed tokens (not all -1)
+    bool ext_kv_ = false;             // prefill engine over a caller-owned cache (one sequence)
+    int pf_seq_ = -1;                 // sequence a prefill step writes (-1: ordinary decode step)
+    bool pf_skip_logits_ = false;     // prefill chunk before the last: no lm_head GEMM, no argmax
+    int* tok_save_ = nullptr;         // [64] rows' previous argmax kept across a prefill, then [1] its token
+    float* last_logits_ = nullptr;    // [vocab] logits after a prefill's last token
+    std::vector<int> pf_host_;        // host staging of a prefill step's tokens and positions
 };
 
 }  // namespace cudallm

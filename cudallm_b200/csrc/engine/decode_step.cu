@@ -144,21 +144,42 @@ __device__ __forceinline__ void fail(const StepParams& p, volatile Flags* fl, un
     atomicCAS(p.err + 1, 0u, id);
 }
 
-// Bounded wait on an mbarrier phase; also gives up when the CTA aborts (check_abort). With
-// `tile_word`, first waits until the producer has published tile `tile` into the stage (a parity wait
-// only distinguishes the barrier's current and previous phase; a consumer warp can be further ahead).
-__device__ bool wait_bar(const StepParams& p, uint64_t* bar, uint32_t parity, volatile Flags* fl, bool check_abort,
-                         unsigned id, const volatile int* tile_word = nullptr, int tile = 0) {
+// Bounded per-thread wait on an mbarrier phase (the producer lanes' drain of their last copies).
+__device__ bool wait_bar(const StepParams& p, uint64_t* bar, uint32_t parity, volatile Flags* fl, uint64_t limit_ns,
+                         unsigned id) {
     uint64_t t0 = 0;
     for (uint32_t it = 1;; ++it) {
-        if ((tile_word == nullptr || *tile_word == tile) && mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait(bar, parity)) return true;
         if ((it & 63) == 0) {
-            if (check_abort && fl->abort) return false;
             const uint64_t t = global_ns();
             if (t0 == 0) {
                 t0 = t;
-            } else if (t - t0 > p.wait_limit_ns) {
+            } else if (t - t0 > limit_ns) {
                 fail(p, fl, kErrWaitTimeout, id);
+                return false;
+            }
+        }
+    }
+}
+
+// Warp-collective bounded wait for tile `tile` in a ring stage (all 32 lanes of a consumer warp call it):
+// first until the producer has published that tile into the stage (a parity wait alone only tells the
+// barrier's current phase from the previous one, and a consumer warp can be further ahead), then for the
+// stage's phase. Every decision is a warp vote, so the lanes leave together with the same answer; gives
+// up when the CTA aborts or after the wait limit.
+__device__ bool wait_tile(const StepParams& p, uint64_t* bar, uint32_t parity, volatile Flags* fl, unsigned id,
+                          const volatile int* tile_word, int tile) {
+    uint64_t t0 = 0;
+    for (uint32_t it = 1;; ++it) {
+        const bool ready = *tile_word == tile && mbar_try_wait(bar, parity);
+        if (__all_sync(0xffffffffu, ready)) return true;
+        if ((it & 63) == 0) {
+            if (__any_sync(0xffffffffu, fl->abort != 0)) return false;
+            const uint64_t t = __shfl_sync(0xffffffffu, global_ns(), 0);
+            if (t0 == 0) {
+                t0 = t;
+            } else if (t - t0 > p.wait_limit_ns) {
+                if ((threadIdx.x & 31) == 0) fail(p, fl, kErrWaitTimeout, id);
                 return false;
             }
         }
@@ -275,8 +296,9 @@ __device__ void run_producer(const StepParams& p, uint8_t* ring, uint64_t* full,
         if (__any_sync(0xffffffffu, progressed)) {
             t_idle = 0;
         } else if ((it & 63) == 0) {
-            if (fl->abort) break;
-            const uint64_t now = global_ns();
+            // Warp-uniform decisions: every lane leaves the loop at the same iteration.
+            if (__any_sync(0xffffffffu, fl->abort != 0)) break;
+            const uint64_t now = __shfl_sync(0xffffffffu, global_ns(), 0);
             if (t_idle == 0) {
                 t_idle = now;
             } else if (now - t_idle > p.wait_limit_ns) {
@@ -285,8 +307,9 @@ __device__ void run_producer(const StepParams& p, uint8_t* ring, uint64_t* full,
             }
         }
     }
-    // Every copy issued lands before the CTA may exit.
-    if (lane < kStages && k > 0) wait_bar(p, &full[lane], (k - 1) & 1, fl, false, 2000u);
+    // Every copy issued lands before the CTA may exit. The drain has its own limit, independent of the
+    // (possibly short) dependency-wait limit: the copies are plain reads and always finish.
+    if (lane < kStages && k > 0) wait_bar(p, &full[lane], (k - 1) & 1, fl, p.drain_limit_ns, 2000u);
 }
 
 // Warp 1: L2 prefetch of the weight stream with ordinary prefetch instructions (load/store units,
@@ -528,10 +551,9 @@ __device__ bool load_input(ConsumerCtx& c, const unsigned long long* src, uint32
         }
         if ((it & 7) == 0 && !clk.keep_going(p, c.fl, id)) break;
     }
-    csync();
+    // One barrier that also agrees on the abort flag: every consumer thread takes the same branch.
+    const bool ok = !named_barrier_or(1, kCt, c.fl->abort != 0);
     if (c.tid == 0) trace_mark(p, top, 1);
-    const bool ok = c.fl->abort == 0;
-    csync();
     return ok;
 }
 
@@ -551,7 +573,7 @@ __device__ __forceinline__ bool group_dot(const ConsumerCtx& c, int t0, int r0, 
     for (int sg = 0; sg < g.n_seg; ++sg) {
         const int t = t0 + sg;
         const int s = t % kStages;
-        if (!wait_bar(p, &c.full[s], (t / kStages) & 1, c.fl, true, 3000u, &c.stage_tile[s], t)) return false;
+        if (!wait_tile(p, &c.full[s], (t / kStages) & 1, c.fl, 3000u, &c.stage_tile[s], t)) return false;
         if (c.lane == 0 && sg == 0) trace_tile(p, t0, 2);
         tile_dot<WT, N, CPL>(c.ring + s * kStageBytes, tr, g.seg_bytes, sg * (g.seg_bytes / 16), c.xp, nc, c.xc, op.s, g.cols,
                              acc, c.lane);
@@ -624,8 +646,7 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
     }
     if (!ok) c.fl->abort = 1;
     c.t_base += kr.nt;
-    csync();
-    return c.fl->abort == 0;
+    return !named_barrier_or(1, kCt, !ok || c.fl->abort != 0);
 }
 
 template <WeightType WT, typename KV>
@@ -738,7 +759,7 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
                 }
             }
             if (c.tid == 0) trace_mark(p, l * 5 + 1, 2);
-            if (c.fl->abort) return;
+            if (named_barrier_or(1, kCt, c.fl->abort != 0)) return;
             tsrc = p.t_att;
             tag = act_tag(p, l, kTagAtt);
         } else if (kind == kGu) {
@@ -755,6 +776,7 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
             snorm = p.final_norm;
         }
         if (c.tid == 0) trace_mark(p, top, 0);
+        if (o == p.stall_op && tsrc != nullptr) tag ^= 1u << 7;  // bit 7 is in no tag a writer produces
         {
             float4 v[kStagePer];
             if (!load_input<WT>(c, tsrc, tag, sK, tok, 10u + o, top, v)) return;
@@ -924,7 +946,7 @@ void launch_decode_step(const StepParams& p, WeightType wt, KvType kv, cudaStrea
             f16 ? launch_typed<WeightType::INT4, __half>(p, stream) : launch_typed<WeightType::INT4, __nv_bfloat16>(p, stream);
             return;
     }
-    throw std::runtime_error("decode step: unknown weight type");
+    throw InternalError("decode step: unknown weight type");
 }
 
 }  // namespace cudallm

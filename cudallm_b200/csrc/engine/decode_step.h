@@ -99,11 +99,14 @@ struct StepParams {
     int max_seq;
     float eps;
     int group_size;
-    unsigned long long wait_limit_ns;
+    unsigned long long wait_limit_ns;   // bound of every dependency wait (error + clean exit after it)
+    unsigned long long drain_limit_ns;  // bound of the producer's final wait for its copies in flight
     int prefetch_tiles;  // L2 prefetch distance of the weight stream, in tiles beyond the copies
     int prefetch_mode;   // 0 none, 2 prefetch warp (load/store-unit prefetch instructions), 3 same warp, bulk prefetches
     int whole_head_max_tiles;  // contexts up to this many 64-token tiles use one CTA per KV head for attention
     int trace_t0;        // first stamped tile (global index in CTA 0's tile stream)
+    int stall_op;        // test only, -1 = off: the consumers of weight operation k (k >= 1) wait for an input
+                         // tag that nothing writes, so every CTA's wait runs out after wait_limit_ns
     TileGeom g_qkv, g_wo, g_gu, g_down, g_lm;
 };
 

@@ -1,14 +1,21 @@
-// Batch-1 decode engine. Public surface of wasiqnauman/cudallm src/engine/engine.h:15-32 (create from
-// a .cudallm path, step / step_debug / reset / pos), re-designed for B200: the fused opt/opt path
-// runs each token as ONE persistent cooperative kernel (engine/decode_step.cu); every other option
-// combination runs the reference's per-operation sequence on sm_100a kernels, optionally replayed as
-// a CUDA graph. Position and token live on the device, so queued steps need no host round trip.
+// Batch-1 decode engine behind the reference's engine surface (wasiqnauman/cudallm
+// src/engine/engine.h:15-32: create from a .cudallm path; step, step_debug, reset, pos).
+//
+// Two execution paths share the weights, the KV cache and the device-resident (token, position) pair:
+//   * persistent (the default fused opt/opt configuration): each token is ONE cooperative launch of the
+//     decode-step kernel (engine/decode_step.cu);
+//   * per-op (every other option combination, and step_debug of them): a launch plan built once at
+//     creation, one record per kernel in the reference's operation order, replayed record by record or
+//     captured once as a CUDA graph.
+// All device memory of the engine (activations, KV cache, scratch, control words) is one allocation
+// carved into aligned regions; the weights are a second one (model/weights.h).
 #pragma once
 
 #include <cuda_runtime.h>
 
 #include <memory>
 #include <string>
+#include <vector>
 
 #include "common/dtype.h"
 #include "engine/decode_step.h"
@@ -17,24 +24,27 @@
 
 namespace cudallm {
 
+class BatchEngine;
+
 enum class MatvecImpl : int { NAIVE = 0, OPT = 1 };
 enum class AttnImpl : int { NAIVE = 0, OPT = 1 };
 enum class DecodePath : int { AUTO = 0, PERSISTENT = 1, PER_OP = 2 };
 
-// Options: reference src/engine/options.h:10-17 plus the additive kv / device / path fields.
+// Options of the reference (src/engine/options.h:10-17) plus the additive kv / device / path fields.
 struct EngineOptions {
     MatvecImpl matvec = MatvecImpl::OPT;
     AttnImpl attn = AttnImpl::OPT;
     bool fuse = true;
     bool cuda_graph = true;
-    int max_seq_len = 0;  // 0 = header value, else a multiple of 128 not above it
+    int max_seq_len = 0;  // 0 = header value, else a positive multiple of 128 not above it
     int matvec_rpb = 0;   // 0 = default, else 1, 2, 4 or 8
     KvType kv = KvType::F16;
     int device = -1;  // -1 = current device
     DecodePath path = DecodePath::AUTO;
 };
 
-void validate(const EngineOptions& o, WeightType wt);  // throws ArgError
+// Throws ArgError when an option (or combination) is invalid for weights of type wt.
+void validate(const EngineOptions& o, WeightType wt);
 
 class Engine {
 public:
@@ -53,66 +63,102 @@ public:
     cudaStream_t stream() const { return stream_; }
 
     void reset();
-    // token >= 0: feed it; -1: feed the previous argmax (already on the device). With both outputs
-    // null the call only enqueues work.
+    // token >= 0 is fed, -1 feeds the previous argmax (already on the device). With both outputs null the
+    // call only enqueues work.
     void step(int token, float* logits_out, int* next_token_out);
-    // Never graph-replayed; residuals_out: [(n_layers+1) * hidden].
+    // Never graph-replayed; residuals_out: host [(n_layers + 1) * hidden].
     void step_debug(int token, float* residuals_out, float* logits_out, int* next_token_out);
     // Waits for queued work and reports a device-side failure.
     void synchronize();
-    // Per-CTA timestamps of the persistent step (see decode_step.h kTraceSlots).
+    // Feeds tokens[0..n) at positions pos() .. pos()+n-1, as n steps would (results equal up to fp32
+    // summation order), but 64 tokens per launch sequence: a batched engine (tcgen05 GEMMs, created on first
+    // use with its own copy of the weights) writes this engine's KV cache directly. int8 weights have no
+    // batched GEMM and step the tokens through the decode path instead. Afterwards pos() has advanced by n;
+    // next_token_out / logits_out (host, or null) get the argmax and logits after tokens[n-1], and a step
+    // with token -1 continues from that argmax. Synchronises.
+    void prefill(const int* tokens, int n, float* logits_out, int* next_token_out);
+
+    // Step tracing of the persistent path (decode_step.h kTraceSlots).
     void set_trace(bool enable);
     int trace_grid() const;
     void read_trace(unsigned long long* out, size_t count);
+    // Validated tuning / test knobs of the persistent path, by name (ArgError when unknown or out of
+    // range): "wait_limit_ns" (bound of every inter-CTA wait, 1 .. 1e10), "prefetch_tiles" (L2 prefetch
+    // distance, 0 .. 1024), "whole_head_max_tiles" (attention form switch, 0 .. max_seq/64),
+    // "trace_tile_op" (weight operation whose tiles the trace stamps, 0 .. 64), "stall_op" (test only: the
+    // consumers of weight operation k wait for an input that is never written, so the step's waits run out
+    // and it fails with StateError; -1 = off, 1 .. 64).
+    void set_knob(const std::string& name, long long value);
 
-private:
+    // Device state read back with every synchronising step: the fed/argmax token, the position and the
+    // error words of the bounded in-kernel waits.
     struct DevState {
         int token;
         int pos;
         unsigned err[2];
     };
-    void enqueue_per_op(bool debug, float* residuals_out);
-    void launch_linear(const Linear& L, const float* x, float* y, Epilogue ep, const float* norm_w);
-    template <typename KV>
-    void enqueue_layers(bool debug, float* residuals_out);
-    void enqueue_persistent(int token, float* debug_res);
-    void finish_sync(float* logits_out, int* next_token_out);
-    void raise_if_device_error(const DevState& st);
-    void free_all() noexcept;
 
+private:
+    // One kernel launch of the per-op path.
+    enum class Op : uint8_t { EMBED, RMSNORM, MATVEC, ROPE, KV_WRITE, ROPE_KV, ATTN, ADD, SILU_MUL, ARGMAX, SNAPSHOT };
+    struct PlanStep {
+        Op op;
+        int layer = -1;              // KV-cache layer (ROPE / KV_WRITE / ROPE_KV / ATTN), residual slot (SNAPSHOT)
+        const Linear* w = nullptr;   // MATVEC
+        const float* in = nullptr;   // operand read
+        float* out = nullptr;        // operand written
+        const float* gain = nullptr; // RMSNorm gain (RMSNORM, or fused into MATVEC)
+        Epilogue ep = Epilogue::STORE;
+    };
+
+    template <typename Fn>
+    void for_each_region(Fn&& fn);
+    void build_plan();
+    template <typename KV>
+    void run_plan(float* residuals_out);
+    void run_plan_any(float* residuals_out);
+    void launch_step_kernel(int token, float* debug_res);
+    void collect(float* logits_out, int* next_token_out);
+    void check_device_state(const DevState& st);
+    void make_step_params();
+
+    std::string path_;
     std::unique_ptr<Weights> weights_;
+    std::unique_ptr<BatchEngine> prefiller_;  // made by the first prefill (bf16 / int4 weights)
     EngineOptions opts_;
     bool persistent_ = false;
     int device_ = 0;
     int max_seq_ = 0;
     int host_pos_ = 0;
     cudaStream_t stream_ = nullptr;
-    cudaGraph_t graph_ = nullptr;
-    cudaGraphExec_t graph_exec_ = nullptr;
-    StepParams step_params_{};
+    cudaGraphExec_t graph_ = nullptr;
+    std::vector<PlanStep> plan_;
 
-    float* x_ = nullptr;
-    float* xb_ = nullptr;
-    float* qkv_ = nullptr;
-    float* att_ = nullptr;
-    float* tmp_ = nullptr;
-    float* gu_ = nullptr;
-    float* act_ = nullptr;
-    float* logits_ = nullptr;
-    void* k_cache_ = nullptr;
-    void* v_cache_ = nullptr;
-    float* part_o_ = nullptr;
-    float* part_ml_ = nullptr;
-    float* am_v_ = nullptr;
+    // Regions of the engine's single device allocation (for_each_region lists them).
+    void* arena_ = nullptr;
+    float* x_ = nullptr;       // residual stream [hidden]
+    float* xb_ = nullptr;      // normalised input [hidden] (unfused)
+    float* qkv_ = nullptr;     // [q | k | v]
+    float* att_ = nullptr;     // attention output [heads * head_dim]
+    float* tmp_ = nullptr;     // projection output before the residual add (unfused) [hidden]
+    float* gu_ = nullptr;      // gate | up (unfused) [2 * inter]
+    float* act_ = nullptr;     // SwiGLU output [inter]
+    float* logits_ = nullptr;  // [vocab]
+    uint16_t* k_cache_ = nullptr;  // [layers][kv heads][max_seq][head_dim], fp16 or bf16 bits
+    uint16_t* v_cache_ = nullptr;
+    float* part_o_ = nullptr;   // split-K attention partials [heads][max_seq / 64][head_dim]
+    float* part_ml_ = nullptr;  // [heads][max_seq / 64][2]
+    float* am_v_ = nullptr;     // argmax partials
     int* am_i_ = nullptr;
-    DevState* state_ = nullptr;  // token, pos, error words
-    unsigned* sync_ = nullptr;
-    float* debug_res_ = nullptr;
-    // Persistent step: activations exchanged between CTAs as (value, tag) words; tag of the last launch.
-    unsigned long long* tagged_ = nullptr;
+    DevState* state_ = nullptr;
+    unsigned* sync_ = nullptr;  // persistent step: tickets
+    float* debug_res_ = nullptr;  // persistent step_debug: residuals [(layers + 1) * hidden]
+    unsigned long long* tagged_ = nullptr;  // persistent step: (value, tag) activation words
     size_t tagged_words_ = 0;
+
+    StepParams step_{};
     unsigned step_tag_ = 0;
-    unsigned long long* trace_ = nullptr;
+    unsigned long long* trace_ = nullptr;  // separate allocation, made when tracing is first enabled
     bool trace_on_ = false;
 };
 

@@ -187,7 +187,7 @@ __global__ void __launch_bounds__(kRowAttThreads) attention_rows_stream_kernel(c
                                                                                const KV* v_cache, size_t seq_stride,
                                                                                const int* __restrict__ pos_v,
                                                                                __nv_bfloat16* out, int nh, int nkv,
-                                                                               int max_seq, unsigned* err) {
+                                                                               int max_seq, unsigned* err, int one_seq) {
     using KV2 = typename Kv2<KV>::T;
     grid_dep_launch();
     // A direct cast keeps the shared address space visible to the compiler (shared loads, not generic);
@@ -202,8 +202,11 @@ __global__ void __launch_bounds__(kRowAttThreads) attention_rows_stream_kernel(c
     }
     __syncthreads();
     // pos and the cached tokens before pos were written by earlier steps, so tiles that end before pos
-    // are fetched before waiting for the kernel that produces q and the new token's k / v.
+    // are fetched before waiting for the kernel that produces q and the new token's k / v. When every row
+    // is one position of a single sequence (one_seq: a prefill chunk, row 0 at its first position), this
+    // step writes all positions from row 0's on, so only tiles ending before that one are fetched early.
     const int ctx = pos_v[b] + 1;
+    const int fresh = one_seq ? pos_v[0] : ctx - 1;
     const int n_tiles = (ctx + kAttnTile - 1) / kAttnTile;
     const KV* kg = k_cache + seq_stride * b + static_cast<size_t>(h) * max_seq * kHd;
     const KV* vg = v_cache + seq_stride * b + static_cast<size_t>(h) * max_seq * kHd;
@@ -216,7 +219,7 @@ __global__ void __launch_bounds__(kRowAttThreads) attention_rows_stream_kernel(c
         bulk_load(&sm.v[st][0][0], vg + static_cast<size_t>(t) * kAttnTile * kHd, bytes, &sm.full[st], pol);
     };
     const int first = min(kRowAttStages, n_tiles);
-    const int early = min(first, (ctx - 1) / kAttnTile);  // tiles wholly before pos
+    const int early = min(first, fresh / kAttnTile);  // tiles wholly before the first position written now
     if (tid == 0) {
         for (int t = 0; t < early; ++t) issue(t);
     }
@@ -540,7 +543,7 @@ void launch_attention_rows(const float* qkv, const KV* k_cache, const KV* v_cach
 template <typename KV>
 void launch_attention_rows_stream(const float* qkv, const KV* k_cache, const KV* v_cache, size_t seq_stride, const int* pos,
                                   __nv_bfloat16* out, int batch, int nh, int nkv, int max_seq, unsigned* err,
-                                  cudaStream_t stream, bool pdl) {
+                                  cudaStream_t stream, bool pdl, bool one_seq) {
     CLLM_CHECK(qkv && k_cache && v_cache && pos && out && err && batch >= 1 && batch <= kBatchMax,
                "launch_attention_rows_stream: bad arguments");
     CLLM_CHECK(nh == nkv * kGqa && max_seq % kAttnTile == 0, "launch_attention_rows_stream: unsupported shape");
@@ -556,7 +559,7 @@ void launch_attention_rows_stream(const float* qkv, const KV* k_cache, const KV*
         if (dev < 64) configured[dev] = true;
     }
     launch_kernel(attention_rows_stream_kernel<KV>, dim3(nkv, batch), dim3(kRowAttThreads), smem, stream, pdl, qkv, k_cache,
-                  v_cache, seq_stride, pos, out, nh, nkv, max_seq, err);
+                  v_cache, seq_stride, pos, out, nh, nkv, max_seq, err, one_seq ? 1 : 0);
 }
 
 void launch_argmax_rows(const float* logits, int n, float* scratch_v, int* scratch_i, unsigned* ticket, int* tok, int* pos,
@@ -573,9 +576,9 @@ template void launch_rope_kv_rows<__half>(float*, const float*, __half*, __half*
                                           cudaStream_t, bool);
 template void launch_attention_rows_stream<__nv_bfloat16>(const float*, const __nv_bfloat16*, const __nv_bfloat16*, size_t,
                                                           const int*, __nv_bfloat16*, int, int, int, int, unsigned*,
-                                                          cudaStream_t, bool);
+                                                          cudaStream_t, bool, bool);
 template void launch_attention_rows_stream<__half>(const float*, const __half*, const __half*, size_t, const int*,
-                                                   __nv_bfloat16*, int, int, int, int, unsigned*, cudaStream_t, bool);
+                                                   __nv_bfloat16*, int, int, int, int, unsigned*, cudaStream_t, bool, bool);
 template void launch_attention_rows<__nv_bfloat16>(const float*, const __nv_bfloat16*, const __nv_bfloat16*, size_t, const int*,
                                                    int, float*, float*, __nv_bfloat16*, int, int, int, int, cudaStream_t, bool);
 template void launch_attention_rows<__half>(const float*, const __half*, const __half*, size_t, const int*, int, float*, float*,

@@ -40,11 +40,13 @@ void launch_attention_rows(const float* qkv, const KV* k_cache, const KV* v_cach
                            int max_seq, cudaStream_t stream, bool pdl = false);
 // The same attention as launch_attention_rows, one CTA per (KV head, row) streaming the row's whole
 // context through shared memory (bulk async copies); no partials. err: device word, bit 1 set if a
-// bounded wait for a copy gave up. Caches 16-byte aligned.
+// bounded wait for a copy gave up. Caches 16-byte aligned. one_seq: every row is one position of the same
+// sequence (seq_stride 0, positions increasing from row 0: a prefill chunk), so a row reads the keys and
+// values its predecessors in the chunk wrote in this step.
 template <typename KV>
 void launch_attention_rows_stream(const float* qkv, const KV* k_cache, const KV* v_cache, size_t seq_stride, const int* pos,
                                   __nv_bfloat16* out, int batch, int nh, int nkv, int max_seq, unsigned* err,
-                                  cudaStream_t stream, bool pdl = false);
+                                  cudaStream_t stream, bool pdl = false, bool one_seq = false);
 // tok[b] = argmax of logits row b (lowest index on ties), pos[b] += 1. Each row is split over
 // kArgmaxSplit blocks; scratch_v / scratch_i hold [batch][kArgmaxSplit] slice results and ticket [batch]
 // counters that must be zero before the first launch (each launch leaves them zero).

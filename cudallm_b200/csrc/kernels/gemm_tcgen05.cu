@@ -811,16 +811,10 @@ __global__ void interleave_int4_codes_kernel(uint32_t* __restrict__ w, size_t wo
 
 using GemmFn = void (*)(CUtensorMap, CUtensorMap, GemmArgs);
 
-// Ring depth: 7 stages (one CTA per SM, the default; measured 2-3 % faster over a batched step) or 3
-// (two CTAs per SM; CUDALLM_GEMM_STAGES=3). The lm_head always uses 3: with 1002 tiles, two CTAs per SM
-// let one CTA's epilogue overlap the other's stream.
-int deep_ring() {
-    static const bool deep = [] {
-        const char* env = std::getenv("CUDALLM_GEMM_STAGES");
-        return !(env && std::atoi(env) == 3);
-    }();
-    return deep;
-}
+// Ring depth: 7 stages, one CTA per SM (measured 2-3 % faster over a batched step than 3 stages with two
+// CTAs per SM). The lm_head uses 3: with 1002 tiles, two CTAs per SM let one CTA's epilogue overlap the
+// other's stream.
+constexpr bool deep_ring() { return true; }
 
 template <int ST>
 GemmFn gemm_fn_st(GemmEpilogue kind, bool kv_bf16) {

@@ -83,8 +83,13 @@ void launch_set_token(int* d_token, int token, cudaStream_t);
 // Deterministic argmax (lowest index on ties); writes *d_token and increments *d_pos.
 void launch_argmax(const float* logits, int n, float* part_v, int* part_i, int* d_token, int* d_pos, cudaStream_t);
 
+// HBM bandwidth probes (kernels/hbm_probe.cu). sink: probe_grid() * 256 words for the plain probes,
+// num_sms() * 256 for the bulk read; err: a device word set when a bounded wait of the bulk read gave up.
+int probe_grid();
 void launch_bw_read(const uint4* src, size_t n_uint4, unsigned* sink, int grid, cudaStream_t);
 void launch_bw_write(uint4* dst, size_t n_uint4, int grid, cudaStream_t);
 void launch_bw_copy(const uint4* src, uint4* dst, size_t n_uint4, int grid, cudaStream_t);
+size_t bulk_probe_chunk_bytes();
+void launch_bw_bulk_read(const void* src, size_t bytes, unsigned* sink, unsigned* err, cudaStream_t);
 
 }  // namespace cudallm

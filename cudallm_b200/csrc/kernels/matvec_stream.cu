@@ -248,7 +248,7 @@ void dispatch_ep(Epilogue ep, bool norm, const MatvecArgs& a, const TileGeom& g,
         case Epilogue::ADD: dispatch_norm<WT, Epilogue::ADD>(norm, a, g, s, err); return;
         case Epilogue::SWIGLU: dispatch_norm<WT, Epilogue::SWIGLU>(norm, a, g, s, err); return;
     }
-    throw std::runtime_error("launch_matvec_stream: unknown epilogue");
+    throw InternalError("launch_matvec_stream: unknown epilogue");
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -318,7 +318,7 @@ void launch_matvec_stream(WeightType wt, Epilogue ep, bool fuse_norm, const Matv
         case WeightType::INT8: dispatch_ep<WeightType::INT8>(ep, fuse_norm, a, g, stream, err); return;
         case WeightType::INT4: dispatch_ep<WeightType::INT4>(ep, fuse_norm, a, g, stream, err); return;
     }
-    throw std::runtime_error("launch_matvec_stream: unknown weight type");
+    throw InternalError("launch_matvec_stream: unknown weight type");
 }
 
 void launch_matvec_naive(const MatvecArgs& a, cudaStream_t stream) {

@@ -279,40 +279,6 @@ __global__ void argmax_final_kernel(const float* __restrict__ part_v, const int*
 }
 
 // ---- DRAM bandwidth probes (reference src/kernels/bandwidth.cu:14-47) -------------------------
-__global__ void bw_read_kernel(const uint4* __restrict__ src, size_t n, unsigned* __restrict__ sink) {
-    unsigned acc = 0;
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const uint4 v = __ldcs(src + i);
-        acc ^= v.x ^ v.y ^ v.z ^ v.w;
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) acc ^= __shfl_xor_sync(0xffffffffu, acc, o);
-    __shared__ unsigned wacc[32];
-    if ((threadIdx.x & 31) == 0) wacc[threadIdx.x >> 5] = acc;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        unsigned r = 0;
-        for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) r ^= wacc[w];
-        sink[blockIdx.x] = r;
-    }
-}
-
-__global__ void bw_write_kernel(uint4* __restrict__ dst, size_t n) {
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        const unsigned u = static_cast<unsigned>(i);
-        __stcs(dst + i, make_uint4(u, u, u, u));
-    }
-}
-
-__global__ void bw_copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t n) {
-    for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
-         i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-        __stcs(dst + i, __ldcs(src + i));
-    }
-}
-
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
@@ -425,24 +391,6 @@ void launch_argmax(const float* logits, int n, float* part_v, int* part_i, int* 
     argmax_partial_kernel<<<kArgmaxBlocks, 256, 0, stream>>>(logits, n, part_v, part_i);
     CLLM_CUDA(cudaGetLastError());
     argmax_final_kernel<<<1, 256, 0, stream>>>(part_v, part_i, kArgmaxBlocks, d_token, d_pos);
-    CLLM_CUDA(cudaGetLastError());
-}
-
-void launch_bw_read(const uint4* src, size_t n_uint4, unsigned* sink, int grid, cudaStream_t stream) {
-    CLLM_CHECK(src && sink && n_uint4 > 0 && grid > 0, "launch_bw_read: bad arguments");
-    bw_read_kernel<<<grid, 256, 0, stream>>>(src, n_uint4, sink);
-    CLLM_CUDA(cudaGetLastError());
-}
-
-void launch_bw_write(uint4* dst, size_t n_uint4, int grid, cudaStream_t stream) {
-    CLLM_CHECK(dst && n_uint4 > 0 && grid > 0, "launch_bw_write: bad arguments");
-    bw_write_kernel<<<grid, 256, 0, stream>>>(dst, n_uint4);
-    CLLM_CUDA(cudaGetLastError());
-}
-
-void launch_bw_copy(const uint4* src, uint4* dst, size_t n_uint4, int grid, cudaStream_t stream) {
-    CLLM_CHECK(src && dst && n_uint4 > 0 && grid > 0, "launch_bw_copy: bad arguments");
-    bw_copy_kernel<<<grid, 256, 0, stream>>>(src, dst, n_uint4);
     CLLM_CUDA(cudaGetLastError());
 }
 

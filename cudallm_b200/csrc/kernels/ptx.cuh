@@ -102,6 +102,21 @@ __device__ __forceinline__ void named_barrier(int id, int threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
+// Named barrier that also ORs a predicate over its `threads` threads: every participant gets the same
+// answer, so a decision taken on it (e.g. "some thread saw the abort flag") is uniform.
+__device__ __forceinline__ bool named_barrier_or(int id, int threads, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "barrier.cta.red.or.pred q, %2, %3, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(threads)
+        : "memory");
+    return r != 0;
+}
+
 // Thread-block clusters: this CTA's rank and the cluster size; a full cluster barrier (all threads of
 // every CTA, release/acquire, so shared-memory writes before it are visible to peers after it); a peer
 // CTA's shared-memory address (distributed shared memory) and a 32-bit load from it.

@@ -54,7 +54,7 @@ ParsedFile parse_cudallm(const std::string& path);
 
 class Weights {
 public:
-    // Uploads a parsed file to the current device. Throws IoError / runtime_error("CUDA ...").
+    // Uploads a parsed file to the current device. Throws IoError / CudaError.
     explicit Weights(const ParsedFile& file);
     ~Weights();
     Weights(const Weights&) = delete;

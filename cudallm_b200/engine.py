@@ -1,241 +1,72 @@
-"""ctypes binding of libcudallm.so (include/cudallm.h).
+"""Python interface of libcudallm.so.
 
-Mirrors wasiqnauman/cudallm python/cudallm/engine.py:1-214: same class and function names
-(`Engine`, `CudaLLMError`, `kernel_matvec`, `kernel_rmsnorm`, `kernel_rope_kv`, `kernel_attention`,
-`kernel_silu_mul`, `kernel_argmax`), same argument meaning and the same error behaviour (every
-nonzero return code raises `CudaLLMError(code, message)`). Additions: `Engine(kv_dtype=..., device=...,
-path=...)` through `cudallm_create_ex`, `Engine.synchronize()` and `Engine.decode_path`.
+The public names and their arguments are those of wasiqnauman/cudallm's Python package
+(python/cudallm/engine.py): `Engine(path, matvec=, attn=, fuse=, cuda_graph=, max_seq_len=, matvec_rpb=)`
+with `step`, `step_debug`, `reset`, `pos`, `close`; the single-kernel hooks `kernel_matvec`,
+`kernel_rmsnorm`, `kernel_rope_kv`, `kernel_attention`, `kernel_silu_mul`, `kernel_argmax`; and
+`CudaLLMError(code, message)` for every nonzero return code. Code written against that package runs
+against this one. Everything is bound through `abi` (signatures generated from include/cudallm.h).
 
-There is no fallback: if the library cannot be loaded every call raises.
+Additions: `Engine(kv_dtype=, device=, path_kind=)` (cudallm_create_ex), `synchronize`, `step_async`,
+`decode_path`, `stream_handle`, `device`, tracing and knobs; `BatchEngine` (cudallm_batch_*);
+`kernel_gemm` (the batched path's tensor-core GEMM).
 """
 from __future__ import annotations
 
 import ctypes
-import functools
-from ctypes import POINTER, c_char_p, c_float, c_int, c_ulonglong, c_ushort, c_void_p
 from pathlib import Path
 
 import numpy as np
 
+from . import abi
+from .abi import CudaLLMError, addr, check, lib
 from .paths import LIB_PATH
 
-_IMPL = {"naive": 0, "opt": 1}
-_WTYPE = {"bf16": 1, "int8": 3, "int4": 4}
-_EPILOGUE = {"store": 0, "add": 1, "swiglu": 2}
-_KV = {"fp16": 0, "bf16": 1}
-_PATH = {"auto": 0, "persistent": 1, "per_op": 2}
+__all__ = ["BatchEngine", "CudaLLMError", "Engine", "LIB_PATH", "kernel_argmax", "kernel_attention", "kernel_gemm",
+           "kernel_matvec", "kernel_rmsnorm", "kernel_rope_kv", "kernel_silu_mul", "lib"]
+
+IMPLS = ("naive", "opt")
+WEIGHT_CODES = {"bf16": 1, "int8": 3, "int4": 4}
+EPILOGUES = ("store", "add", "swiglu")
+KV_DTYPES = ("fp16", "bf16")
+PATHS = ("auto", "persistent", "per_op")
+BATCH_ATTN = ("auto", "stream", "split")
 
 
-class CudallmOptions(ctypes.Structure):
-    _fields_ = [("matvec_impl", c_int), ("attn_impl", c_int), ("fuse", c_int), ("cuda_graph", c_int),
-                ("max_seq_len", c_int), ("matvec_rpb", c_int)]
-
-
-class CudallmOptionsEx(ctypes.Structure):
-    _fields_ = [("struct_size", c_int), ("kv_dtype", c_int), ("device", c_int), ("path", c_int),
-                ("reserved", c_int * 4)]
-
-
-class CudallmBatchOptions(ctypes.Structure):
-    _fields_ = [("struct_size", c_int), ("n_seq", c_int), ("max_seq_len", c_int), ("kv_dtype", c_int),
-                ("device", c_int), ("cuda_graph", c_int), ("reserved", c_int * 4)]
-
-
-class CudallmConfigInfo(ctypes.Structure):
-    _fields_ = [("weight_dtype", c_int), ("hidden", c_int), ("inter", c_int), ("n_layers", c_int),
-                ("n_heads", c_int), ("n_kv_heads", c_int), ("head_dim", c_int), ("vocab", c_int),
-                ("max_seq_len", c_int), ("group_size", c_int), ("rms_eps", c_float),
-                ("weight_bytes", c_ulonglong)]
-
-
-class CudaLLMError(RuntimeError):
-    def __init__(self, code: int, message: str):
-        super().__init__(f"cudallm error {code}: {message}")
-        self.code = code
-
-
-_FLOAT_P = POINTER(c_float)
-_INT_P = POINTER(c_int)
-_USHORT_P = POINTER(c_ushort)
-
-# Every symbol include/cudallm.h declares, with its ctypes signature.
-SIGNATURES = {
-    "cudallm_last_error": ([], c_char_p),
-    "cudallm_default_options": ([POINTER(CudallmOptions)], None),
-    "cudallm_create": ([c_char_p, POINTER(CudallmOptions), POINTER(c_void_p)], c_int),
-    "cudallm_destroy": ([c_void_p], None),
-    "cudallm_get_config": ([c_void_p, POINTER(CudallmConfigInfo)], c_int),
-    "cudallm_reset": ([c_void_p], c_int),
-    "cudallm_pos": ([c_void_p], c_int),
-    "cudallm_step": ([c_void_p, c_int, _FLOAT_P, _INT_P], c_int),
-    "cudallm_step_debug": ([c_void_p, c_int, _FLOAT_P, _FLOAT_P, _INT_P], c_int),
-    "cudallm_kernel_matvec": ([c_int, c_int, c_int, c_int, c_int, c_void_p, c_ulonglong, c_void_p, c_ulonglong,
-                               _FLOAT_P, _FLOAT_P, c_float, _FLOAT_P, c_int, c_int], c_int),
-    "cudallm_kernel_rmsnorm": ([_FLOAT_P, _FLOAT_P, c_float, _FLOAT_P, c_int], c_int),
-    "cudallm_kernel_rope_kv": ([c_int, _FLOAT_P, _FLOAT_P, c_int, _USHORT_P, _USHORT_P, c_int, c_int, c_int, c_int],
-                               c_int),
-    "cudallm_kernel_attention": ([c_int, _FLOAT_P, _USHORT_P, _USHORT_P, c_int, _FLOAT_P, c_int, c_int, c_int, c_int],
-                                 c_int),
-    "cudallm_kernel_silu_mul": ([_FLOAT_P, _FLOAT_P, c_int], c_int),
-    "cudallm_kernel_argmax": ([_FLOAT_P, c_int, _INT_P], c_int),
-    "cudallm_default_options_ex": ([POINTER(CudallmOptionsEx)], None),
-    "cudallm_create_ex": ([c_char_p, POINTER(CudallmOptions), POINTER(CudallmOptionsEx), POINTER(c_void_p)], c_int),
-    "cudallm_synchronize": ([c_void_p], c_int),
-    "cudallm_engine_path": ([c_void_p], c_int),
-    "cudallm_engine_stream": ([c_void_p], c_void_p),
-    "cudallm_engine_device": ([c_void_p], c_int),
-    "cudallm_debug_trace": ([c_void_p, c_int], c_int),
-    "cudallm_debug_read_trace": ([c_void_p, POINTER(c_ulonglong), c_ulonglong, _INT_P, _INT_P], c_int),
-    "cudallm_default_batch_options": ([POINTER(CudallmBatchOptions)], None),
-    "cudallm_batch_create": ([c_char_p, POINTER(CudallmBatchOptions), POINTER(c_void_p)], c_int),
-    "cudallm_batch_destroy": ([c_void_p], None),
-    "cudallm_batch_get_config": ([c_void_p, POINTER(CudallmConfigInfo)], c_int),
-    "cudallm_batch_reset": ([c_void_p, c_int], c_int),
-    "cudallm_batch_pos": ([c_void_p, c_int], c_int),
-    "cudallm_batch_step": ([c_void_p, _INT_P, _INT_P, _FLOAT_P], c_int),
-    "cudallm_batch_synchronize": ([c_void_p], c_int),
-    "cudallm_batch_stream": ([c_void_p], c_void_p),
-    "cudallm_kernel_gemm": ([_USHORT_P, _USHORT_P, _USHORT_P, _FLOAT_P, c_int, c_int, c_int, c_int, c_int], c_int),
-    # device pointers: q, k_cache, v_cache, ctx, out, nh, nkv, hd, max_seq, stream
-    "cudallm_attention_noalloc": ([c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_void_p],
-                                  c_int),
-}
-
-
-@functools.cache
-def _lib() -> ctypes.CDLL:
-    path = Path(LIB_PATH)
-    if not path.exists():
-        raise CudaLLMError(6, f"native library missing: {path} (build it with `python -m cudallm_b200.build`)")
-    lib = ctypes.CDLL(str(path))
-    for name, (argtypes, restype) in SIGNATURES.items():
-        fn = getattr(lib, name)
-        fn.argtypes = argtypes
-        fn.restype = restype
-    return lib
-
-
-def lib() -> ctypes.CDLL:
-    """The loaded library (raises CudaLLMError if it is missing)."""
-    return _lib()
-
-
-def _check(rc: int) -> None:
-    if rc != 0:
-        msg = _lib().cudallm_last_error()
-        raise CudaLLMError(rc, msg.decode("utf-8", "replace") if msg else "")
-
-
-def _fp(a: np.ndarray):
-    return a.ctypes.data_as(_FLOAT_P)
+def _index(names: tuple[str, ...], v) -> int:
+    """Position of a name in `names`, or an integer code passed through."""
+    return names.index(v) if isinstance(v, str) else int(v)
 
 
 def _f32(a) -> np.ndarray:
     return np.ascontiguousarray(a, dtype=np.float32)
 
 
-def _fp16_bits(a) -> np.ndarray:
+def _half_bits(a) -> np.ndarray:
+    """Own copy of fp16 data (given as float16 values or as their uint16 bits) as uint16 bits."""
     a = np.asarray(a)
-    if a.dtype == np.float16:
-        return np.ascontiguousarray(a).view(np.uint16).copy()
-    return np.ascontiguousarray(a, dtype=np.uint16).copy()
+    return np.array(a.view(np.uint16) if a.dtype == np.float16 else a, dtype=np.uint16, order="C", copy=True)
 
 
-def _code(table: dict[str, int], v: str | int) -> int:
-    return table[v] if isinstance(v, str) else int(v)
+class _Owned:
+    """A handle of the library, released by `close` (also on `with` exit and garbage collection)."""
 
+    _destroy = ""
 
-class Engine:
-    def __init__(self, path: Path | str, *, matvec: str = "opt", attn: str = "opt", fuse: bool = True,
-                 cuda_graph: bool = True, max_seq_len: int = 0, matvec_rpb: int = 0, kv_dtype: str = "fp16",
-                 device: int = -1, path_kind: str = "auto"):
-        self._h = None
-        lib_ = _lib()
-        opts = CudallmOptions(_IMPL[matvec], _IMPL[attn], int(bool(fuse)), int(bool(cuda_graph)), int(max_seq_len),
-                              int(matvec_rpb))
-        ex = CudallmOptionsEx()
-        lib_.cudallm_default_options_ex(ctypes.byref(ex))
-        ex.kv_dtype = _KV[kv_dtype]
-        ex.device = int(device)
-        ex.path = _PATH[path_kind]
-        h = c_void_p()
-        _check(lib_.cudallm_create_ex(str(path).encode(), ctypes.byref(opts), ctypes.byref(ex), ctypes.byref(h)))
-        self._h = h
-        info = CudallmConfigInfo()
-        _check(lib_.cudallm_get_config(self._h, ctypes.byref(info)))
-        self.config: dict = {name: getattr(info, name) for name, _ in CudallmConfigInfo._fields_}
-        self._vocab = info.vocab
-        self._rows = info.n_layers + 1
-        self._hidden = info.hidden
+    def __init__(self):
+        self._h: ctypes.c_void_p | None = None
 
-    def _handle(self) -> c_void_p:
+    def _handle(self) -> ctypes.c_void_p:
         if self._h is None:
-            raise CudaLLMError(5, "engine is closed")
+            raise CudaLLMError(5, f"{type(self).__name__} is closed")
         return self._h
 
-    @property
-    def pos(self) -> int:
-        return _lib().cudallm_pos(self._handle())
-
-    @property
-    def decode_path(self) -> str:
-        code = _lib().cudallm_engine_path(self._handle())
-        return {1: "persistent", 2: "per_op"}.get(code, "unknown")
-
-    @property
-    def stream_handle(self) -> int:
-        """The engine's cudaStream_t as an integer (e.g. for torch.cuda.ExternalStream)."""
-        return int(_lib().cudallm_engine_stream(self._handle()) or 0)
-
-    @property
-    def device(self) -> int:
-        return _lib().cudallm_engine_device(self._handle())
-
-    def reset(self) -> None:
-        _check(_lib().cudallm_reset(self._handle()))
-
-    def synchronize(self) -> None:
-        _check(_lib().cudallm_synchronize(self._handle()))
-
-    def trace(self, enable: bool = True) -> None:
-        """Per-CTA timestamps of each following step (persistent path only)."""
-        _check(_lib().cudallm_debug_trace(self._handle(), int(bool(enable))))
-
-    def read_trace(self, grid: int = 1024, slots: int = 82 * 6) -> tuple[np.ndarray, np.ndarray]:
-        """Last traced step: (uint64 [grid][ops][6] per-CTA stamps, uint64 [256][5] tile stamps of CTA 0),
-        nanoseconds (layout in csrc/engine/decode_step.h)."""
-        buf = np.zeros(grid * slots + 256 * 5, dtype=np.uint64)
-        g, sl = c_int(0), c_int(0)
-        _check(_lib().cudallm_debug_read_trace(self._handle(), buf.ctypes.data_as(POINTER(c_ulonglong)), buf.size,
-                                               ctypes.byref(g), ctypes.byref(sl)))
-        n = g.value * sl.value
-        return buf[:n].reshape(g.value, sl.value // 6, 6), buf[n:n + 256 * 5].reshape(256, 5)
-
-    def step(self, token: int | None = None, *, want_logits: bool = False) -> tuple[int, np.ndarray | None]:
-        nxt = c_int(0)
-        logits = np.empty(self._vocab, dtype=np.float32) if want_logits else None
-        _check(_lib().cudallm_step(self._handle(), -1 if token is None else int(token),
-                                   _fp(logits) if logits is not None else None, ctypes.byref(nxt)))
-        return nxt.value, logits
-
-    def step_async(self, token: int | None = None) -> None:
-        """Enqueues one step without waiting or copying anything back."""
-        _check(_lib().cudallm_step(self._handle(), -1 if token is None else int(token), None, None))
-
-    def step_debug(self, token: int | None = None) -> tuple[int, np.ndarray, np.ndarray]:
-        nxt = c_int(0)
-        logits = np.empty(self._vocab, dtype=np.float32)
-        residuals = np.empty((self._rows, self._hidden), dtype=np.float32)
-        _check(_lib().cudallm_step_debug(self._handle(), -1 if token is None else int(token), _fp(residuals),
-                                         _fp(logits), ctypes.byref(nxt)))
-        return nxt.value, logits, residuals
-
     def close(self) -> None:
-        if self._h is not None:
-            _lib().cudallm_destroy(self._h)
-            self._h = None
+        h, self._h = self._h, None
+        if h is not None:
+            getattr(lib(), self._destroy)(h)
 
-    def __enter__(self) -> "Engine":
+    def __enter__(self):
         return self
 
     def __exit__(self, *exc) -> None:
@@ -246,46 +77,144 @@ class Engine:
             self.close()
 
 
-class BatchEngine:
-    """Batched decode of up to 64 independent sequences on one GPU (cudallm_batch_* entry points)."""
+def _config_dict(info) -> dict:
+    return {name: getattr(info, name) for name, _ in info._fields_}
 
-    def __init__(self, path: Path | str, *, n_seq: int = 64, max_seq_len: int = 0, kv_dtype: str = "fp16",
-                 device: int = -1, cuda_graph: bool = True):
-        self._h = None
-        lib_ = _lib()
-        opts = CudallmBatchOptions()
-        lib_.cudallm_default_batch_options(ctypes.byref(opts))
-        opts.n_seq = int(n_seq)
-        opts.max_seq_len = int(max_seq_len)
-        opts.kv_dtype = _KV[kv_dtype]
-        opts.device = int(device)
-        opts.cuda_graph = int(bool(cuda_graph))
-        h = c_void_p()
-        _check(lib_.cudallm_batch_create(str(path).encode(), ctypes.byref(opts), ctypes.byref(h)))
+
+class Engine(_Owned):
+    """Batch-1 decode of one sequence (cudallm_create / cudallm_step ...)."""
+
+    _destroy = "cudallm_destroy"
+
+    def __init__(self, path: Path | str, *, matvec: str = "opt", attn: str = "opt", fuse: bool = True,
+                 cuda_graph: bool = True, max_seq_len: int = 0, matvec_rpb: int = 0, kv_dtype: str = "fp16",
+                 device: int = -1, path_kind: str = "auto"):
+        super().__init__()
+        L = lib()
+        opts = abi.struct("cudallm_options")(IMPLS.index(matvec), IMPLS.index(attn), int(bool(fuse)),
+                                             int(bool(cuda_graph)), int(max_seq_len), int(matvec_rpb))
+        ex = abi.struct("cudallm_options_ex")()
+        L.cudallm_default_options_ex(ctypes.byref(ex))
+        ex.kv_dtype, ex.device, ex.path = KV_DTYPES.index(kv_dtype), int(device), PATHS.index(path_kind)
+        h = ctypes.c_void_p()
+        check(L.cudallm_create_ex(str(path).encode(), ctypes.byref(opts), ctypes.byref(ex), ctypes.byref(h)))
         self._h = h
-        info = CudallmConfigInfo()
-        _check(lib_.cudallm_batch_get_config(self._h, ctypes.byref(info)))
-        self.config: dict = {name: getattr(info, name) for name, _ in CudallmConfigInfo._fields_}
-        self.n_seq = int(n_seq)
-        self._vocab = info.vocab
+        info = abi.struct("cudallm_config_info")()
+        check(L.cudallm_get_config(h, ctypes.byref(info)))
+        self.config = _config_dict(info)
 
-    def _handle(self) -> c_void_p:
-        if self._h is None:
-            raise CudaLLMError(5, "engine is closed")
-        return self._h
+    @property
+    def pos(self) -> int:
+        return lib().cudallm_pos(self._handle())
 
-    def pos(self, seq: int) -> int:
-        return _lib().cudallm_batch_pos(self._handle(), int(seq))
+    @property
+    def decode_path(self) -> str:
+        return {1: "persistent", 2: "per_op"}.get(lib().cudallm_engine_path(self._handle()), "unknown")
 
     @property
     def stream_handle(self) -> int:
-        return int(_lib().cudallm_batch_stream(self._handle()) or 0)
+        """The engine's cudaStream_t as an integer (for torch.cuda.ExternalStream)."""
+        return lib().cudallm_engine_stream(self._handle()) or 0
 
-    def reset(self, seq: int = -1) -> None:
-        _check(_lib().cudallm_batch_reset(self._handle(), int(seq)))
+    @property
+    def device(self) -> int:
+        return lib().cudallm_engine_device(self._handle())
+
+    def reset(self) -> None:
+        check(lib().cudallm_reset(self._handle()))
 
     def synchronize(self) -> None:
-        _check(_lib().cudallm_batch_synchronize(self._handle()))
+        check(lib().cudallm_synchronize(self._handle()))
+
+    def step(self, token: int | None = None, *, want_logits: bool = False) -> tuple[int, np.ndarray | None]:
+        """Feeds `token` (None: the previous argmax); returns (next token, logits if asked)."""
+        nxt = np.zeros(1, dtype=np.int32)
+        logits = np.empty(self.config["vocab"], dtype=np.float32) if want_logits else None
+        check(lib().cudallm_step(self._handle(), -1 if token is None else int(token), addr(logits), addr(nxt)))
+        return int(nxt[0]), logits
+
+    def step_async(self, token: int | None = None) -> None:
+        """Enqueues one step; nothing is waited for or copied back."""
+        check(lib().cudallm_step(self._handle(), -1 if token is None else int(token), None, None))
+
+    def prefill(self, tokens, *, want_logits: bool = False) -> tuple[int, np.ndarray | None]:
+        """Feeds a prompt 64 tokens per batched step (cudallm_prefill): (argmax after the last token, its
+        logits if asked); a following step(None) continues from that argmax."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        nxt = np.zeros(1, dtype=np.int32)
+        logits = np.empty(self.config["vocab"], dtype=np.float32) if want_logits else None
+        check(lib().cudallm_prefill(self._handle(), addr(t), t.size, addr(logits), addr(nxt)))
+        return int(nxt[0]), logits
+
+    def step_debug(self, token: int | None = None) -> tuple[int, np.ndarray, np.ndarray]:
+        """One step without graph replay: (next token, logits, residuals [n_layers + 1][hidden])."""
+        c = self.config
+        nxt = np.zeros(1, dtype=np.int32)
+        logits = np.empty(c["vocab"], dtype=np.float32)
+        residuals = np.empty((c["n_layers"] + 1, c["hidden"]), dtype=np.float32)
+        check(lib().cudallm_step_debug(self._handle(), -1 if token is None else int(token), addr(residuals),
+                                       addr(logits), addr(nxt)))
+        return int(nxt[0]), logits, residuals
+
+    def set_knob(self, name: str, value: int) -> None:
+        """Tuning / test knob of the persistent step (cudallm_debug_set)."""
+        check(lib().cudallm_debug_set(self._handle(), name.encode(), int(value)))
+
+    def trace(self, enable: bool = True) -> None:
+        """Per-CTA timestamps of each following step (persistent path only)."""
+        check(lib().cudallm_debug_trace(self._handle(), int(bool(enable))))
+
+    def read_trace(self, grid: int = 1024, slots: int = 82 * 6) -> tuple[np.ndarray, np.ndarray]:
+        """Last traced step: (uint64 [grid][ops][6] per-CTA stamps, uint64 [256][5] tile stamps of CTA 0),
+        nanoseconds (layout in csrc/engine/decode_step.h)."""
+        buf = np.zeros(grid * slots + 256 * 5, dtype=np.uint64)
+        shape = np.zeros(2, dtype=np.int32)
+        check(lib().cudallm_debug_read_trace(self._handle(), addr(buf), buf.size, addr(shape), addr(shape) + 4))
+        n = int(shape[0]) * int(shape[1])
+        return buf[:n].reshape(int(shape[0]), int(shape[1]) // 6, 6), buf[n:n + 256 * 5].reshape(256, 5)
+
+
+class BatchEngine(_Owned):
+    """Batched decode of up to 64 independent sequences on one GPU (cudallm_batch_*)."""
+
+    _destroy = "cudallm_batch_destroy"
+
+    def __init__(self, path: Path | str, *, n_seq: int = 64, max_seq_len: int = 0, kv_dtype: str = "fp16",
+                 device: int = -1, cuda_graph: bool = True, attn: str = "auto"):
+        super().__init__()
+        L = lib()
+        opts = abi.struct("cudallm_batch_options")()
+        L.cudallm_default_batch_options(ctypes.byref(opts))
+        opts.n_seq, opts.max_seq_len, opts.kv_dtype = int(n_seq), int(max_seq_len), KV_DTYPES.index(kv_dtype)
+        opts.device, opts.cuda_graph, opts.attn_mode = int(device), int(bool(cuda_graph)), BATCH_ATTN.index(attn)
+        h = ctypes.c_void_p()
+        check(L.cudallm_batch_create(str(path).encode(), ctypes.byref(opts), ctypes.byref(h)))
+        self._h = h
+        info = abi.struct("cudallm_config_info")()
+        check(L.cudallm_batch_get_config(h, ctypes.byref(info)))
+        self.config = _config_dict(info)
+        self.n_seq = int(n_seq)
+
+    def pos(self, seq: int) -> int:
+        return lib().cudallm_batch_pos(self._handle(), int(seq))
+
+    @property
+    def stream_handle(self) -> int:
+        return lib().cudallm_batch_stream(self._handle()) or 0
+
+    def reset(self, seq: int = -1) -> None:
+        check(lib().cudallm_batch_reset(self._handle(), int(seq)))
+
+    def synchronize(self) -> None:
+        check(lib().cudallm_batch_synchronize(self._handle()))
+
+    def set_knob(self, name: str, value: int) -> None:
+        check(lib().cudallm_batch_debug_set(self._handle(), name.encode(), int(value)))
+
+    def knob(self, name: str) -> int:
+        out = np.zeros(1, dtype=np.int64)
+        check(lib().cudallm_batch_debug_get(self._handle(), name.encode(), addr(out)))
+        return int(out[0])
 
     def _tokens(self, tokens) -> np.ndarray | None:
         if tokens is None:
@@ -296,117 +225,103 @@ class BatchEngine:
         return t
 
     def step(self, tokens=None, *, want_logits: bool = False) -> tuple[np.ndarray, np.ndarray | None]:
-        """One step of every sequence: tokens [n_seq] (-1 = the sequence's previous argmax; None = all -1)
+        """One step of every sequence: tokens [n_seq] (-1 = that sequence's previous argmax; None = all -1)
         -> (next token per sequence, logits [n_seq][vocab] if asked)."""
         t = self._tokens(tokens)
         nxt = np.empty(self.n_seq, dtype=np.int32)
-        logits = np.empty((self.n_seq, self._vocab), dtype=np.float32) if want_logits else None
-        _check(_lib().cudallm_batch_step(self._handle(), t.ctypes.data_as(_INT_P) if t is not None else None,
-                                         nxt.ctypes.data_as(_INT_P), _fp(logits) if logits is not None else None))
+        logits = np.empty((self.n_seq, self.config["vocab"]), dtype=np.float32) if want_logits else None
+        check(lib().cudallm_batch_step(self._handle(), addr(t), addr(nxt), addr(logits)))
         return nxt, logits
 
     def step_async(self, tokens=None) -> None:
-        """Enqueues one step without waiting or copying anything back."""
-        t = self._tokens(tokens)
-        _check(_lib().cudallm_batch_step(self._handle(), t.ctypes.data_as(_INT_P) if t is not None else None, None,
-                                         None))
+        """Enqueues one step; nothing is waited for or copied back."""
+        check(lib().cudallm_batch_step(self._handle(), addr(self._tokens(tokens)), None, None))
 
-    def close(self) -> None:
-        if self._h is not None:
-            _lib().cudallm_batch_destroy(self._h)
-            self._h = None
-
-    def __enter__(self) -> "BatchEngine":
-        return self
-
-    def __exit__(self, *exc) -> None:
-        self.close()
-
-    def __del__(self) -> None:
-        if getattr(self, "_h", None) is not None:
-            self.close()
+    def prefill(self, seq: int, tokens, *, want_logits: bool = False) -> tuple[int, np.ndarray | None]:
+        """Prompt prefill of one sequence, 64 of its tokens per batched step (cudallm_batch_prefill)."""
+        t = np.ascontiguousarray(tokens, dtype=np.int32).reshape(-1)
+        nxt = np.zeros(1, dtype=np.int32)
+        logits = np.empty(self.config["vocab"], dtype=np.float32) if want_logits else None
+        check(lib().cudallm_batch_prefill(self._handle(), int(seq), addr(t), t.size, addr(logits), addr(nxt)))
+        return int(nxt[0]), logits
 
 
 def kernel_matvec(impl: str | int, wtype: str | int, epilogue: str | int, fuse_norm: bool | int, rpb: int,
                   w: np.ndarray, scales: np.ndarray | None, x: np.ndarray, norm_w: np.ndarray | None, eps: float,
                   y_init: np.ndarray | None, rows: int, cols: int) -> np.ndarray:
-    ep = _code(_EPILOGUE, epilogue)
-    out_rows = rows // 2 if ep == 2 else rows
-    w = np.ascontiguousarray(w)
-    s = np.ascontiguousarray(scales) if scales is not None else None
-    x = _f32(x)
-    n = _f32(norm_w) if norm_w is not None else None
-    y = _f32(y_init).copy() if y_init is not None else np.zeros(out_rows, dtype=np.float32)
-    assert y.shape == (out_rows,)
-    _check(_lib().cudallm_kernel_matvec(_code(_IMPL, impl), _code(_WTYPE, wtype), ep, int(bool(fuse_norm)), int(rpb),
-                                        w.ctypes.data, w.nbytes, s.ctypes.data if s is not None else None,
-                                        s.nbytes if s is not None else 0, _fp(x), _fp(n) if n is not None else None,
-                                        float(eps), _fp(y), int(rows), int(cols)))
+    """y = W x with the epilogue (store / add onto y_init / swiglu -> rows/2 outputs), optional fused RMSNorm."""
+    ep = _index(EPILOGUES, epilogue)
+    n_out = rows // 2 if ep == 2 else rows
+    wb = np.ascontiguousarray(w)
+    sb = None if scales is None else np.ascontiguousarray(scales)
+    y = np.zeros(n_out, dtype=np.float32) if y_init is None else np.array(y_init, dtype=np.float32, copy=True)
+    if y.shape != (n_out,):
+        raise ValueError(f"y_init must have shape ({n_out},)")
+    xv = _f32(x)
+    nv = None if norm_w is None else _f32(norm_w)
+    wcode = WEIGHT_CODES[wtype] if isinstance(wtype, str) else int(wtype)
+    check(lib().cudallm_kernel_matvec(_index(IMPLS, impl), wcode, ep, int(bool(fuse_norm)), int(rpb), addr(wb), wb.nbytes,
+                                      addr(sb), 0 if sb is None else sb.nbytes, addr(xv), addr(nv), float(eps), addr(y),
+                                      int(rows), int(cols)))
     return y
 
 
 def kernel_rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
-    x, w = _f32(x), _f32(w)
-    y = np.empty_like(x)
-    _check(_lib().cudallm_kernel_rmsnorm(_fp(x), _fp(w), float(eps), _fp(y), x.size))
+    xv, wv = _f32(x), _f32(w)
+    y = np.empty_like(xv)
+    check(lib().cudallm_kernel_rmsnorm(addr(xv), addr(wv), float(eps), addr(y), xv.size))
     return y
 
 
 def kernel_rope_kv(fused: bool | int, qkv: np.ndarray, inv_freq: np.ndarray, pos: int, k_cache: np.ndarray,
                    v_cache: np.ndarray, nh: int, nkv: int, hd: int,
                    max_seq: int) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
-    qkv = _f32(qkv).copy()
-    inv = _f32(inv_freq)
-    k = _fp16_bits(k_cache)
-    v = _fp16_bits(v_cache)
-    _check(_lib().cudallm_kernel_rope_kv(int(bool(fused)), _fp(qkv), _fp(inv), int(pos), k.ctypes.data_as(_USHORT_P),
-                                         v.ctypes.data_as(_USHORT_P), nh, nkv, hd, max_seq))
-    return qkv, k.view(np.float16), v.view(np.float16)
+    """RoPE on q and k, k/v written at `pos` of the fp16 caches: returns (qkv, k_cache, v_cache) (new arrays)."""
+    q = np.array(qkv, dtype=np.float32, copy=True)
+    f = _f32(inv_freq)
+    k, v = _half_bits(k_cache), _half_bits(v_cache)
+    check(lib().cudallm_kernel_rope_kv(int(bool(fused)), addr(q), addr(f), int(pos), addr(k), addr(v), nh, nkv, hd,
+                                       max_seq))
+    return q, k.view(np.float16), v.view(np.float16)
 
 
 def kernel_attention(impl: str | int, q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, ctx: int, nh: int,
                      nkv: int, hd: int, max_seq: int) -> np.ndarray:
-    q = _f32(q)
-    k = _fp16_bits(k_cache)
-    v = _fp16_bits(v_cache)
+    """Decode attention of nh query heads over the first ctx cached positions (fp16 caches [nkv][max_seq][hd])."""
+    qv = _f32(q)
+    k, v = _half_bits(k_cache), _half_bits(v_cache)
     out = np.empty(nh * hd, dtype=np.float32)
-    _check(_lib().cudallm_kernel_attention(_code(_IMPL, impl), _fp(q), k.ctypes.data_as(_USHORT_P),
-                                           v.ctypes.data_as(_USHORT_P), int(ctx), _fp(out), nh, nkv, hd, max_seq))
-    return out
-
-
-def kernel_gemm(w_bits: np.ndarray, x_bits: np.ndarray, *, x_lo_bits: np.ndarray | None = None, ksplit: int = 1,
-                epilogue: str = "store", y: np.ndarray | None = None) -> np.ndarray:
-    """Batched-path GEMM hook: w_bits [n][k], x_bits (and optionally x_lo_bits, added to x) [batch][k] bf16
-    bits (uint16) -> fp32 [batch][n] (store / add onto y) or [batch][n/2] (swiglu)."""
-    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
-    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
-    n, k = w.shape
-    batch = x.shape[0]
-    lo = None
-    if x_lo_bits is not None:
-        lo = np.ascontiguousarray(x_lo_bits, dtype=np.uint16)
-        if lo.shape != x.shape:
-            raise ValueError("x_lo_bits must have the shape of x_bits")
-    ep = _EPILOGUE[epilogue]
-    n_out = n // 2 if epilogue == "swiglu" else n
-    out = np.zeros((batch, n_out), dtype=np.float32) if y is None else np.ascontiguousarray(y, dtype=np.float32).copy()
-    _check(_lib().cudallm_kernel_gemm(w.ctypes.data_as(_USHORT_P), x.ctypes.data_as(_USHORT_P),
-                                      lo.ctypes.data_as(_USHORT_P) if lo is not None else None, _fp(out), n, k, batch,
-                                      int(ksplit), ep))
+    check(lib().cudallm_kernel_attention(_index(IMPLS, impl), addr(qv), addr(k), addr(v), int(ctx), addr(out), nh, nkv,
+                                         hd, max_seq))
     return out
 
 
 def kernel_silu_mul(gu: np.ndarray) -> np.ndarray:
-    gu = _f32(gu)
-    inter = gu.size // 2
-    act = np.empty(inter, dtype=np.float32)
-    _check(_lib().cudallm_kernel_silu_mul(_fp(gu), _fp(act), inter))
+    g = _f32(gu)
+    act = np.empty(g.size // 2, dtype=np.float32)
+    check(lib().cudallm_kernel_silu_mul(addr(g), addr(act), act.size))
     return act
 
 
 def kernel_argmax(logits: np.ndarray) -> int:
-    logits = _f32(logits)
-    idx = c_int(-1)
-    _check(_lib().cudallm_kernel_argmax(_fp(logits), logits.size, ctypes.byref(idx)))
-    return idx.value
+    lg = _f32(logits)
+    idx = np.full(1, -1, dtype=np.int32)
+    check(lib().cudallm_kernel_argmax(addr(lg), lg.size, addr(idx)))
+    return int(idx[0])
+
+
+def kernel_gemm(w_bits: np.ndarray, x_bits: np.ndarray, *, x_lo_bits: np.ndarray | None = None, ksplit: int = 1,
+                epilogue: str = "store", y: np.ndarray | None = None) -> np.ndarray:
+    """Batched-path GEMM hook: w_bits [n][k], x_bits (plus optional x_lo_bits, added to x) [batch][k] bf16 bits
+    (uint16) -> fp32 [batch][n] (store / add onto y) or [batch][n/2] (swiglu)."""
+    w = np.ascontiguousarray(w_bits, dtype=np.uint16)
+    x = np.ascontiguousarray(x_bits, dtype=np.uint16)
+    lo = None if x_lo_bits is None else np.ascontiguousarray(x_lo_bits, dtype=np.uint16)
+    if lo is not None and lo.shape != x.shape:
+        raise ValueError("x_lo_bits must have the shape of x_bits")
+    n, k = w.shape
+    ep = EPILOGUES.index(epilogue)
+    shape = (x.shape[0], n // 2 if ep == 2 else n)
+    out = np.zeros(shape, dtype=np.float32) if y is None else np.array(y, dtype=np.float32, copy=True)
+    check(lib().cudallm_kernel_gemm(addr(w), addr(x), addr(lo), addr(out), n, k, x.shape[0], int(ksplit), ep))
+    return out

@@ -16,7 +16,6 @@ Times are microseconds from the start of the step. Stamp layout: csrc/engine/dec
 from __future__ import annotations
 
 import argparse
-import os
 
 import numpy as np
 
@@ -31,12 +30,12 @@ def op_names() -> list[str]:
 
 
 def capture(dtype: str, kv: str, prompt: int, tile_op: int | None) -> tuple[np.ndarray, np.ndarray]:
-    if tile_op is not None:
-        os.environ["CUDALLM_TRACE_TILE_OP"] = str(tile_op)  # read when the engine is created
     from . import synth
     from .engine import Engine
     path, _ = synth.ensure_model(dtype)
     with Engine(path, kv_dtype=kv) as eng:
+        if tile_op is not None:
+            eng.set_knob("trace_tile_op", tile_op)
         for t in synth.prompt_ids(prompt):
             eng.step_async(t)
         for _ in range(4):

@@ -120,6 +120,14 @@ void cudallm_default_options_ex(cudallm_options_ex* out);
 int cudallm_create_ex(const char* path, const cudallm_options* opts, const cudallm_options_ex* ex, cudallm_engine** out);
 /* Waits for every queued step; reports a device-side failure (e.g. a timed-out inter-block wait). */
 int cudallm_synchronize(cudallm_engine* e);
+/* Prompt prefill: feeds tokens[0..n) (host) at positions pos .. pos+n-1, with the results of n calls of
+ * cudallm_step(e, tokens[i], NULL, NULL) up to fp32 summation order, 64 tokens per batched tensor-core step
+ * (a batched engine with its own copy of the weights is created on the first call and writes this engine's
+ * KV cache; int8 weights step the tokens through the decode path). Afterwards cudallm_pos advanced by n,
+ * *next_token_out (or NULL) is the argmax after tokens[n-1], logits_out (host [vocab], or NULL) its logits,
+ * and cudallm_step(e, -1, ...) continues from that argmax. n must fit in max_seq_len (else STATE).
+ * Synchronises. No counterpart in the reference, which feeds prompts one cudallm_step at a time. */
+int cudallm_prefill(cudallm_engine* e, const int* tokens, int n, float* logits_out, int* next_token_out);
 /* Which decode path the engine runs: CUDALLM_PATH_PERSISTENT or CUDALLM_PATH_PER_OP. */
 int cudallm_engine_path(cudallm_engine* e);
 /* The engine's CUDA stream (a cudaStream_t) and device, so callers can order or time work against the
@@ -131,11 +139,20 @@ int cudallm_engine_device(cudallm_engine* e);
  * producer warp starts streaming its weights; 0 turns it off. */
 int cudallm_debug_trace(cudallm_engine* e, int enable);
 /* Copies the last traced step: grid x slots per-CTA values followed by 256 x 5 stamps of 256 consecutive
- * tiles of CTA 0 (from the lm_head's first tile unless CUDALLM_TRACE_TILE_OP named another weight operation
- * when the engine was created); count >= grid*slots + 1280. *grid_out, *slots_out get the shape. Waits
- * for queued work. */
+ * tiles of CTA 0 (from the first tile of the weight operation the "trace_tile_op" knob names, by default the
+ * lm_head); count >= grid*slots + 1280. *grid_out, *slots_out get the shape. Waits for queued work. */
 int cudallm_debug_read_trace(cudallm_engine* e, unsigned long long* out, unsigned long long count, int* grid_out,
                              int* slots_out);
+/* Sets a tuning or test knob of the persistent decode path by name; CUDALLM_ERR_INVALID_ARG for an unknown
+ * name, a value out of range, or a per-op engine. Knobs: "wait_limit_ns" (bound of every inter-block wait of
+ * the step, 1 .. 1e10; default 1e9; a step whose wait runs out returns CUDALLM_ERR_STATE and leaves the
+ * position unchanged), "prefetch_tiles" (L2 prefetch distance of the weight stream, 0 .. 1024),
+ * "whole_head_max_tiles" (contexts up to this many 64-token tiles attend with one block per KV head, 0 ..
+ * max_seq_len/64; default 2), "trace_tile_op" (weight operation whose tiles the trace stamps, 0 .. 64),
+ * "stall_op" (for tests of the failure path: the blocks computing weight operation k, 1 .. 64, wait for an
+ * input that is never written, so every such wait runs out after wait_limit_ns and the step fails with
+ * CUDALLM_ERR_STATE; -1 = off, the default). */
+int cudallm_debug_set(cudallm_engine* e, const char* knob, long long value);
 
 /* ---- batched decode (no counterpart in the reference, whose engine holds one sequence): up to 64
  * independent sequences decoded together on one GPU, one token each per step; every row runs the
@@ -151,10 +168,12 @@ typedef struct {
     int kv_dtype;    /* CUDALLM_KV_FP16 or CUDALLM_KV_BF16 */
     int device;      /* CUDA device ordinal; -1 = the calling thread's current device */
     int cuda_graph;  /* 1: replay the step as a CUDA graph */
-    int reserved[4];
+    int attn_mode;   /* 0 choose by size; 1 one block per (KV head, sequence) streaming the context;
+                        2 split over 64-token tiles, merged by a second kernel */
+    int reserved[3];
 } cudallm_batch_options;
 
-/* Fills n_seq 64, max_seq_len 0, kv fp16, device -1, cuda_graph 1. */
+/* Fills n_seq 64, max_seq_len 0, kv fp16, device -1, cuda_graph 1, attn_mode 0. */
 void cudallm_default_batch_options(cudallm_batch_options* out);
 /* Loads a .cudallm file (bf16 or int4 weights; int8 returns INVALID_ARG) for n_seq sequences; *out = NULL on failure. */
 int cudallm_batch_create(const char* path, const cudallm_batch_options* opts, cudallm_batch** out);
@@ -173,8 +192,19 @@ int cudallm_batch_pos(cudallm_batch* e, int seq);
 int cudallm_batch_step(cudallm_batch* e, const int* tokens, int* next_out, float* logits_out);
 /* Waits for every queued step; reports a device-side failure. */
 int cudallm_batch_synchronize(cudallm_batch* e);
+/* Prompt prefill of sequence seq (engines of n_seq 64): tokens[0..n) at that sequence's positions pos ..
+ * pos+n-1, 64 per batched step, every row of a step one position of that sequence. The other sequences keep
+ * their positions and previous argmax. next_token_out / logits_out (host, or NULL) as in cudallm_prefill.
+ * Synchronises. */
+int cudallm_batch_prefill(cudallm_batch* e, int seq, const int* tokens, int n, float* logits_out, int* next_token_out);
 /* The engine's CUDA stream (a cudaStream_t); NULL for a NULL engine. */
 void* cudallm_batch_stream(cudallm_batch* e);
+/* Tuning knobs of the batched step by name (CUDALLM_ERR_INVALID_ARG when unknown or out of range): "pdl"
+ * (0/1: programmatic dependent launch between the step's kernels), "ksplit_qkv", "ksplit_wo",
+ * "ksplit_gate_up", "ksplit_down" (K split of that GEMM, 1 .. min(16, k/64); int4 k/128). The next step
+ * captures its graph again. _get reads them back, and "attn_stream" (1 = streaming attention in use). */
+int cudallm_batch_debug_set(cudallm_batch* e, const char* knob, long long value);
+int cudallm_batch_debug_get(cudallm_batch* e, const char* knob, long long* value_out);
 
 /* Test hook of the batched path (no counterpart in the reference): tensor-core GEMM y[b][j] (+)= sum_k
  * (x[b][k] + x_lo[b][k]) * w[j][k] for b < batch (1..64), w [n][k], x and x_lo [batch][k] bf16 bits (x_lo
@@ -197,7 +227,9 @@ int cudallm_kernel_gemm(const unsigned short* w, const unsigned short* x, const 
  * return CUDALLM_ERR_INVALID_ARG. All calls share that array and it keeps the last call's contents, so
  * calls whose GPU work overlaps (other streams or threads, same device) race: order them on one stream.
  * The first call on each device, with that device current, looks up the array's device address
- * (cudaGetSymbolAddress); make that first call before any stream capture that includes this function. */
+ * (cudaGetSymbolAddress) and keeps it for the life of the process; make that first call before any stream
+ * capture that includes this function. A cudaDeviceReset of that device invalidates the kept address:
+ * call this function no more on a device that was reset while the library stayed loaded. */
 int cudallm_attention_noalloc(const float* q, const unsigned short* k_cache, const unsigned short* v_cache, int ctx,
                               float* out, int nh, int nkv, int hd, int max_seq, void* stream);
 

@@ -13,6 +13,8 @@ Parts (each writes one .npz):
           quantiser re-applied to sampled blocks; ReferenceModel on the 32-token seeded prompt for
           32 + 63 steps: greedy ids, per-step top-2 margin and logit statistics, full logits at the last
           prompt step and residuals at two steps -> golden_full_<config>.npz
+  long    the seeded bf16 weights in a max_seq_len 32896 file; ReferenceModel (bf16 KV) on a 4096-token
+          seeded prompt + 8 greedy tokens -> golden_long_bf16_bf16.npz (about half an hour of CPU)
 """
 from __future__ import annotations
 
@@ -165,11 +167,35 @@ def part_full(configs: list[str]) -> None:
         np.savez_compressed(HERE / f"golden_full_{cfg}.npz", **out)
 
 
+LONG_PROMPT_LEN = 4096
+LONG_NEW = 8
+LONG_MAX_SEQ = 32896  # 32768 + 128: the long-context file serves both the 4096 and the 32768 contexts
+
+
+def part_long() -> None:
+    """ReferenceModel (bf16 KV) on the seeded bf16 weights in a max_seq_len 32896 file, prompted with 4096
+    seeded random tokens, then 8 greedy tokens: ids, per-step top-8 over the last 64 prompt steps and the
+    generated steps, full logits and residuals at the last prompt step -> golden_long_bf16_bf16.npz."""
+    prompt = synth.prompt_ids(LONG_PROMPT_LEN, seed=0)
+    path, digest = synth.ensure_model("bf16", seed=0, max_seq_len=LONG_MAX_SEQ)
+    out = {"digest": np.array(digest), "prompt": np.array(prompt, dtype=np.int32), "max_seq_len": np.array(LONG_MAX_SEQ)}
+    r = run_reference(path, prompt, LONG_NEW, torch.bfloat16, keep_logits_at=(LONG_PROMPT_LEN - 1,),
+                      keep_res_at=(LONG_PROMPT_LEN - 1,))
+    first = LONG_PROMPT_LEN - 64  # keep the per-step statistics of the tail only (the file stays small)
+    for k in ("margin", "lsum", "lsq", "top8_i", "top8_v"):
+        r[k] = r[k][first:]
+    r["stats_first_step"] = np.array(first)
+    out.update(r)
+    np.savez_compressed(HERE / "golden_long_bf16_bf16.npz", **out)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--parts", nargs="+", default=["quant", "format", "tiny"])
     ap.add_argument("--full-configs", nargs="+", default=["bf16_fp16", "int8_fp16", "int4_fp16", "bf16_bf16"])
     args = ap.parse_args()
+    if "long" in args.parts:
+        part_long()
     if "quant" in args.parts:
         part_quant()
     if "format" in args.parts:

@@ -11,6 +11,7 @@ from pathlib import Path
 import numpy as np
 import pytest
 
+from cudallm_b200 import abi
 from cudallm_b200 import engine as E
 from cudallm_b200 import format as fmt
 
@@ -39,27 +40,39 @@ def test_library_exports_every_declared_symbol(native_lib):
     exported = {line.split()[-1] for line in out.stdout.splitlines() if line.strip()}
     missing = [n for n in declared_functions() if n not in exported]
     assert not missing, f"declared but not exported: {missing}"
-    assert set(E.SIGNATURES) == set(declared_functions())
+    assert set(abi.declarations()[1]) == set(declared_functions())
 
 
 def test_struct_layouts():
-    assert ctypes.sizeof(E.CudallmOptions) == 24
-    assert ctypes.sizeof(E.CudallmConfigInfo) == 56
-    assert ctypes.sizeof(E.CudallmOptionsEx) == 32
+    """The structs generated from the header have the reference's sizes (cudallm.h:18-32) and the additive ones."""
+    assert ctypes.sizeof(abi.struct("cudallm_options")) == 24
+    assert ctypes.sizeof(abi.struct("cudallm_config_info")) == 56
+    assert ctypes.sizeof(abi.struct("cudallm_options_ex")) == 32
+    assert ctypes.sizeof(abi.struct("cudallm_batch_options")) == 40
+
+
+def test_signatures_follow_the_header():
+    _, funcs = abi.declarations()
+    args, ret = funcs["cudallm_kernel_matvec"]
+    assert len(args) == 15 and ret is ctypes.c_int
+    assert args[6] is ctypes.c_ulonglong and args[11] is ctypes.c_float
+    assert funcs["cudallm_last_error"] == ([], ctypes.c_char_p)
+    assert funcs["cudallm_create"][0][2] is ctypes.POINTER(ctypes.c_void_p)
+    assert funcs["cudallm_debug_set"][0] == [ctypes.c_void_p, ctypes.c_char_p, ctypes.c_longlong]
 
 
 def test_default_options(native_lib):
-    o = E.CudallmOptions()
+    o = abi.struct("cudallm_options")()
     native_lib.cudallm_default_options(ctypes.byref(o))
     assert (o.matvec_impl, o.attn_impl, o.fuse, o.cuda_graph, o.max_seq_len, o.matvec_rpb) == (1, 1, 1, 1, 0, 0)
     native_lib.cudallm_default_options(None)  # NULL-safe
-    ex = E.CudallmOptionsEx()
+    ex = abi.struct("cudallm_options_ex")()
     native_lib.cudallm_default_options_ex(ctypes.byref(ex))
     assert (ex.struct_size, ex.kv_dtype, ex.device, ex.path) == (32, 0, -1, 0)
 
 
 def _create(native_lib, path, **over) -> tuple[int, str]:
-    o = E.CudallmOptions()
+    o = abi.struct("cudallm_options")()
     native_lib.cudallm_default_options(ctypes.byref(o))
     for k, v in over.items():
         setattr(o, k, v)
@@ -137,7 +150,7 @@ def test_null_engine_calls(native_lib):
     assert native_lib.cudallm_reset(None) == ERR_INVALID_ARG
     assert native_lib.cudallm_step(None, 0, None, None) == ERR_INVALID_ARG
     assert native_lib.cudallm_synchronize(None) == ERR_INVALID_ARG
-    info = E.CudallmConfigInfo()
+    info = abi.struct("cudallm_config_info")()
     assert native_lib.cudallm_get_config(None, ctypes.byref(info)) == ERR_INVALID_ARG
 
 
@@ -181,7 +194,7 @@ def test_header_struct_offsets():
 # ---- batched entry points (cudallm_batch_*): host-side checks, no GPU ----
 
 def _batch_create(lib, path, **overrides):
-    o = E.CudallmBatchOptions()
+    o = abi.struct("cudallm_batch_options")()
     lib.cudallm_default_batch_options(ctypes.byref(o))
     for k, v in overrides.items():
         setattr(o, k, v)
@@ -192,10 +205,9 @@ def _batch_create(lib, path, **overrides):
 
 
 def test_batch_options_layout_and_defaults(native_lib):
-    assert ctypes.sizeof(E.CudallmBatchOptions) == 40
-    o = E.CudallmBatchOptions()
+    o = abi.struct("cudallm_batch_options")()
     native_lib.cudallm_default_batch_options(ctypes.byref(o))
-    assert (o.struct_size, o.n_seq, o.max_seq_len, o.kv_dtype, o.device, o.cuda_graph) == (40, 64, 0, 0, -1, 1)
+    assert (o.struct_size, o.n_seq, o.max_seq_len, o.kv_dtype, o.device, o.cuda_graph, o.attn_mode) == (40, 64, 0, 0, -1, 1, 0)
     native_lib.cudallm_default_batch_options(None)  # NULL-safe
 
 
@@ -206,7 +218,7 @@ def test_batch_create_rejects_before_device_work(native_lib, model_path, tmp_pat
     rc, msg = _batch_create(native_lib, path)
     assert rc == ERR_INVALID_ARG and "bf16 and int4" in msg
     for bad in ({"n_seq": 0}, {"n_seq": 65}, {"max_seq_len": 100}, {"max_seq_len": 8192}, {"kv_dtype": 2},
-                {"struct_size": 36}):
+                {"struct_size": 36}, {"attn_mode": 3}):
         rc, msg = _batch_create(native_lib, path, **bad)
         assert rc == ERR_INVALID_ARG, (bad, msg)
 
@@ -218,8 +230,19 @@ def test_null_batch_engine_calls(native_lib):
     assert native_lib.cudallm_batch_step(None, None, None, None) == ERR_INVALID_ARG
     assert native_lib.cudallm_batch_synchronize(None) == ERR_INVALID_ARG
     assert native_lib.cudallm_batch_stream(None) is None
-    info = E.CudallmConfigInfo()
+    info = abi.struct("cudallm_config_info")()
     assert native_lib.cudallm_batch_get_config(None, ctypes.byref(info)) == ERR_INVALID_ARG
-    o = E.CudallmBatchOptions()
+    o = abi.struct("cudallm_batch_options")()
     native_lib.cudallm_default_batch_options(ctypes.byref(o))
     assert native_lib.cudallm_batch_create(None, ctypes.byref(o), None) == ERR_INVALID_ARG
+    assert native_lib.cudallm_batch_debug_set(None, b"pdl", 1) == ERR_INVALID_ARG
+    v = ctypes.c_longlong(0)
+    assert native_lib.cudallm_batch_debug_get(None, b"pdl", ctypes.byref(v)) == ERR_INVALID_ARG
+
+
+def test_null_engine_knobs(native_lib):
+    assert native_lib.cudallm_debug_set(None, b"wait_limit_ns", 1000) == ERR_INVALID_ARG
+    assert b"null or destroyed" in native_lib.cudallm_last_error()
+    assert native_lib.cudallm_engine_path(None) == -1
+    assert native_lib.cudallm_engine_device(None) == -1
+    assert native_lib.cudallm_engine_stream(None) is None

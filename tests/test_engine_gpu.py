@@ -20,7 +20,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from cudallm_b200.engine import Engine
+from cudallm_b200.engine import CudaLLMError, Engine
 
 pytestmark = pytest.mark.gpu
 
@@ -186,8 +186,8 @@ def test_sequence_full_and_bad_token(model_path):
 
 @pytest.mark.parametrize("kv", ["fp16", "bf16"])
 def test_long_context_persistent_matches_per_op(model_path, kv):
-    """Past 1024 tokens the persistent kernel switches from whole-head attention to split-K across CTAs
-    with an ordered merge; it must agree with the per-op path (split-K kernels + separate RoPE/KV write,
+    """Past 128 tokens (two 64-token tiles) the persistent kernel switches from whole-head attention to
+    split-K across CTAs with an ordered merge; it must agree with the per-op path (split-K kernels + separate RoPE/KV write,
     themselves checked against float64 by the kernel tests) on the same token stream."""
     path, _ = model_path("int4")
     rng = np.random.default_rng(3)
@@ -202,3 +202,56 @@ def test_long_context_persistent_matches_per_op(model_path, kv):
     for a, b in zip(out["persistent"], out["per_op"]):
         assert np.max(np.abs(a - b)) < 2e-2
         assert int(np.argmax(a)) == int(np.argmax(b))
+
+
+def test_wait_expiry_reports_state_and_engine_recovers(model_path, golden):
+    """Every inter-block wait of the persistent step is bounded. The stall_op test knob makes the blocks of
+    one weight operation (layer 0's O projection) wait for an input that nothing writes; with the bound at
+    20 ms those waits run out: the kernel records the failure and returns, the call reports
+    CUDALLM_ERR_STATE (5) and the position stays where it was. With the knob off and the default bound, the
+    same engine, reset, reproduces the reference's logits at the last prompt step and its first greedy ids."""
+    g = golden("full_bf16_fp16")
+    path, digest = model_path("bf16")
+    assert digest == str(g["digest"])
+    prompt = [int(t) for t in g["prompt"]]
+    with Engine(path) as eng:
+        assert eng.decode_path == "persistent"
+        eng.set_knob("wait_limit_ns", 20_000_000)
+        eng.set_knob("stall_op", 1)
+        with pytest.raises(CudaLLMError) as e:
+            eng.step(prompt[0], want_logits=True)
+        assert e.value.code == 5 and "gave up" in str(e.value)
+        assert eng.pos == 0
+        with pytest.raises(CudaLLMError) as e:  # queued steps that fail report it at the next synchronisation
+            eng.step_async(prompt[0])
+            eng.step_async(prompt[1])
+            eng.synchronize()
+        assert e.value.code == 5
+        assert eng.pos == 0
+        eng.set_knob("stall_op", -1)
+        eng.set_knob("wait_limit_ns", 10**9)
+        eng.reset()
+        for t in prompt[:-1]:
+            eng.step_async(t)
+        nxt, lg = eng.step(prompt[-1], want_logits=True)
+        ref = g[f"logits_{len(prompt) - 1}"]
+        assert np.max(np.abs(lg - ref)) < 2e-2
+        ids = [nxt]
+        for _ in range(7):
+            ids.append(eng.step(None)[0])
+        assert ids == [int(t) for t in g["ids"][:8]]
+
+
+def test_knobs_are_validated(model_path):
+    path, _ = model_path("bf16")
+    with Engine(path) as eng:
+        for name, bad in (("wait_limit_ns", 0), ("prefetch_tiles", -1), ("prefetch_tiles", 4096),
+                          ("whole_head_max_tiles", 10**6), ("trace_tile_op", 65), ("stall_op", 0), ("stall_op", 65),
+                          ("no_such_knob", 1)):
+            with pytest.raises(CudaLLMError) as e:
+                eng.set_knob(name, bad)
+            assert e.value.code == 1, (name, bad)
+    with Engine(path, path_kind="per_op") as eng:
+        with pytest.raises(CudaLLMError) as e:
+            eng.set_knob("wait_limit_ns", 10**9)
+        assert e.value.code == 1

@@ -2,8 +2,9 @@
 memory (their memory belongs to another runtime's pool, or their loop must stay out of the driver's
 allocator). It works on caller-owned device buffers and keeps its partials in a fixed 1.03 MiB device
 array, so it is checked here against the allocating entry point cudallm_kernel_attention (same kernels,
-host buffers) with the attention tolerance of the kernel tests (rtol = atol = 1e-4), on calls made back
-to back so that a call which read the previous call's leftovers in the shared array would show.
+host buffers) and against the float64 oracle (oracle.kernels64.attention64), with the attention tolerance
+of the kernel tests (rtol = atol = 1e-4), on calls made back to back so that a call which read the previous
+call's leftovers in the shared array would show; and once on a stream of its own, read back on that stream.
 
 Named to be collected last: if it fails, a run that stops at the first failure has run everything else.
 """
@@ -16,6 +17,7 @@ import pytest
 import torch
 
 from cudallm_b200 import engine as E
+from oracle import kernels64 as K
 
 pytestmark = pytest.mark.gpu
 
@@ -31,18 +33,24 @@ def _case(seed: int, max_seq: int):
     return q, k, v
 
 
-def _noalloc(lib, q, k, v, ctx: int, max_seq: int, nh: int = NH, nkv: int = NKV) -> tuple[int, np.ndarray]:
-    """One call on device buffers the test owns (the test may allocate; the entry point does not)."""
+def _noalloc(lib, q, k, v, ctx: int, max_seq: int, nh: int = NH, nkv: int = NKV,
+             own_stream: bool = False) -> tuple[int, np.ndarray]:
+    """One call on device buffers the test owns (the test may allocate; the entry point does not). With
+    own_stream the call runs on a fresh stream and the output is read back on that stream without a device
+    synchronisation in between."""
     dev = torch.device("cuda:0")
     dq = torch.from_numpy(q).to(dev)
     dk = torch.from_numpy(k.view(np.uint16).view(np.int16)).to(dev)
     dv = torch.from_numpy(v.view(np.uint16).view(np.int16)).to(dev)
     dout = torch.full((nh * HD,), float("nan"), dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    torch.cuda.synchronize(dev)
+    stream = torch.cuda.Stream(dev) if own_stream else torch.cuda.current_stream(dev)
     rc = lib.cudallm_attention_noalloc(dq.data_ptr(), dk.data_ptr(), dv.data_ptr(), ctx, dout.data_ptr(), nh, nkv, HD,
                                        max_seq, ctypes.c_void_p(stream.cuda_stream))
-    torch.cuda.synchronize(dev)
-    return rc, dout.cpu().numpy()
+    with torch.cuda.stream(stream):
+        host = dout.to("cpu", non_blocking=False)
+    stream.synchronize()
+    return rc, host.numpy()
 
 
 @pytest.fixture(scope="module")
@@ -63,8 +71,16 @@ def test_two_calls_in_a_row_match_allocating_entry_point(lib):
         ref = E.kernel_attention("opt", q, k, v, ctx, NH, NKV, HD, max_seq)
         assert np.all(np.isfinite(out))
         assert np.allclose(out, ref, **TOL), (seed, max_seq, ctx)
+        assert np.allclose(out, K.attention64(q, k, v, ctx, NH, NKV), **TOL), (seed, max_seq, ctx)
         outs.append(out)
     assert np.allclose(outs[0], outs[2], **TOL)
+
+
+def test_on_a_stream_of_its_own(lib):
+    q, k, v = _case(4, 2048)
+    rc, out = _noalloc(lib, q, k, v, 1500, 2048, own_stream=True)
+    assert rc == 0, lib.cudallm_last_error()
+    assert np.allclose(out, K.attention64(q, k, v, 1500, NH, NKV), **TOL)
 
 
 def test_full_capacity(lib):
@@ -72,6 +88,7 @@ def test_full_capacity(lib):
     rc, out = _noalloc(lib, q, k, v, 8192, 8192)
     assert rc == 0, lib.cudallm_last_error()
     assert np.allclose(out, E.kernel_attention("opt", q, k, v, 8192, NH, NKV, HD, 8192), **TOL)
+    assert np.allclose(out, K.attention64(q, k, v, 8192, NH, NKV), **TOL)
 
 
 @pytest.mark.parametrize("nh, nkv, max_seq", [(32, 8, 8320), (64, 16, 128)], ids=["max_seq", "heads"])
