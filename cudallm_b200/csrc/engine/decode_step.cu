@@ -438,7 +438,10 @@ __device__ __forceinline__ void csync() { named_barrier(1, kCt); }
 // with it. The tag names the launch (step_tag), the layer and the vector, so a reader needs no counter,
 // no release and no second round trip: it polls the data until the tags are current. A slot is
 // rewritten only after every CTA has passed a later all-to-all dependency, hence after all its readers.
-enum TagKind : uint32_t { kTagQkv = 1, kTagAtt = 2, kTagXmid = 3, kTagXout = 4, kTagAct = 5 };
+enum TagKind : uint32_t { kTagQkv = 1, kTagAtt = 2, kTagXmid = 3, kTagXout = 4, kTagAct = 5, kTagPart = 6 };
+__device__ __forceinline__ void st_release_gpu(unsigned* p, unsigned v) {
+    asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 __device__ __forceinline__ uint32_t act_tag(const StepParams& p, int layer, uint32_t kind) {
     return (p.step_tag << 8) | (static_cast<uint32_t>(layer) << 3) | kind;
 }
@@ -504,6 +507,94 @@ struct TaggedDst {
     uint32_t tag;
     __device__ __forceinline__ void operator()(int i, float x) const { st_tagged(v + i, x, tag); }
 };
+
+// Ranges per KV head for the attention of a context of n_tiles 64-token tiles (n_pass 128-token passes):
+// 1 = one CTA per head over the whole context; else S ranges plus one merging CTA per head.
+__device__ __forceinline__ int attn_splits(const StepParams& p, int n_tiles, int n_pass) {
+    if (n_tiles <= p.whole_head_max_tiles) return 1;
+    const int s = min(min(kAttnMaxSplits, (static_cast<int>(gridDim.x) - kNkv) / kNkv), n_pass);
+    return s > 1 ? s : 1;
+}
+
+// This CTA's attention work for a context of ctx tokens (the same in every layer; recomputed where it is
+// used so that none of it stays live across the weight operations): KV head `head` (-1: none) over the
+// 128-token passes [p0, p1), or, when the context is split (S > 1), merging head `merge`'s S ranges.
+struct AttnRole {
+    int S, n_pass, head, split, p0, p1, merge;
+};
+__device__ __forceinline__ AttnRole attn_role(const StepParams& p, int ctx) {
+    AttnRole r;
+    const int n_tiles = (ctx + kAttnTile - 1) / kAttnTile;
+    r.n_pass = (ctx + kHeadPassTokens - 1) / kHeadPassTokens;
+    r.S = attn_splits(p, n_tiles, r.n_pass);
+    r.head = -1;
+    r.split = 0;
+    r.p0 = 0;
+    r.p1 = 0;
+    r.merge = -1;
+    const int b = blockIdx.x;
+    if (r.S == 1) {
+        const int stride = gridDim.x / kNkv;
+        if (b % stride == 0 && b / stride < kNkv) {
+            r.head = b / stride;
+            r.p1 = r.n_pass;
+        }
+    } else if (b < kNkv * r.S) {
+        r.head = b / r.S;
+        r.split = b % r.S;
+        r.p0 = r.split * r.n_pass / r.S;
+        r.p1 = (r.split + 1) * r.n_pass / r.S;
+    } else if (b < kNkv * r.S + kNkv) {
+        r.merge = b - kNkv * r.S;
+    }
+    return r;
+}
+
+// Merges the S partials of KV head h in range order and writes the 4 query heads' outputs. Threads 0..S-1
+// each acquire one range's flag (bounded polls); one barrier, which also agrees on an abort, then makes the
+// partials visible to every thread. The (M, L) pairs are staged in shared memory by one load per thread;
+// thread (g, d) issues the loads of all S partial outputs of query head 4h + g, dim d at once and merges them
+// in range order. Returns false (all threads) if the CTA gave up.
+template <typename Dst>
+__device__ bool combine_splits(const ConsumerCtx& c, int h, int S, int n_slots, uint32_t tag, Dst out, unsigned id) {
+    const StepParams& p = *c.p;
+    if (c.tid < S) {
+        const unsigned* flag = p.sync + kSyncFlags + 32 * h + c.tid;
+        PollClock clk;
+        for (uint32_t it = 1; ld_acquire_gpu(flag) != tag; ++it) {
+            __nanosleep(64);
+            if ((it & 7) == 0 && !clk.keep_going(p, c.fl, id)) break;
+        }
+    }
+    if (named_barrier_or(1, kCt, c.fl->abort != 0)) return false;
+    float2* ml = reinterpret_cast<float2*>(c.xp);  // [4][S]
+    if (c.tid < kGqa * S) {
+        const int g = c.tid / S, sp = c.tid % S;
+        ml[c.tid] = __ldcg(reinterpret_cast<const float2*>(p.part_ml) + static_cast<size_t>(h * kGqa + g) * n_slots + sp);
+    }
+    csync();
+    const int g = c.tid >> 6, d = c.tid & 63;
+    const float* po = p.part_o + static_cast<size_t>(h * kGqa + g) * n_slots * kHd + d;
+    float ov[kAttnMaxSplits];
+#pragma unroll
+    for (int sp = 0; sp < kAttnMaxSplits; ++sp) ov[sp] = sp < S ? __ldcg(po + static_cast<size_t>(sp) * kHd) : 0.f;
+    float M = -INFINITY, L = 0.f, acc = 0.f;
+#pragma unroll
+    for (int sp = 0; sp < kAttnMaxSplits; ++sp) {
+        if (sp < S) {
+            const float2 m_l = ml[g * S + sp];
+            const float o = ov[sp];
+            const float mn = fmaxf(M, m_l.x);
+            const float a = expf(M - mn), b = expf(m_l.x - mn);
+            L = L * a + m_l.y * b;
+            acc = acc * a + o * b;
+            M = mn;
+        }
+    }
+    out((h * kGqa + g) * kHd + d, acc / L);
+    csync();
+    return true;
+}
 
 // Loads the input vector of an operation into v[i] (columns 4q..4q+3, q = tid + i * kCt): the
 // embedding row for the first QKV projection (src == null), else a tagged vector, where every thread
@@ -649,7 +740,24 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
     return !named_barrier_or(1, kCt, !ok || c.fl->abort != 0);
 }
 
-template <WeightType WT, typename KV>
+// The cached K/V rows of this CTA's range (split contexts) into L2, before the layer's attention needs them.
+template <typename KV>
+__device__ __forceinline__ void prefetch_split_kv(const ConsumerCtx& c, size_t layer_bytes, int ctx) {
+    const StepParams& p = *c.p;
+    const AttnRole ar = attn_role(p, ctx);
+    if (ar.head < 0) return;
+    const int n_tiles = (ctx + kAttnTile - 1) / kAttnTile;
+    const int t0 = 2 * ar.p0, t1 = min(n_tiles, 2 * ar.p1);
+    for (int q = c.tid; q < 2 * (t1 - t0); q += kCt) {
+        const int tile = t0 + (q >> 1);
+        const int n = min(kAttnTile, ctx - tile * kAttnTile);
+        const size_t off = (static_cast<size_t>(ar.head) * p.max_seq + tile * kAttnTile) * kHd * sizeof(KV);
+        const uint8_t* base = static_cast<const uint8_t*>((q & 1) ? p.v_cache : p.k_cache);
+        bulk_prefetch_l2(base + layer_bytes + off, static_cast<uint32_t>(n * kHd * sizeof(KV)));
+    }
+}
+
+template <WeightType WT, typename KV, bool SPLIT>
 __device__ void run_consumers(ConsumerCtx& c, float* cs) {
     const StepParams& p = *c.p;
     const int G = gridDim.x;
@@ -657,8 +765,9 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
     const int ctx = pos + 1;
     const int tok = p.token_override >= 0 ? p.token_override : *p.d_token;
     const int n_tiles = (ctx + kAttnTile - 1) / kAttnTile;
-    const int n_slots = p.max_seq / kAttnTile;
-    const bool whole_head = n_tiles <= p.whole_head_max_tiles;
+    // SPLIT: the instantiation launched for contexts past whole_head_max_tiles (ranges of the context over
+    // many CTAs, merged per head); the other runs every head on one CTA. Each is correct at any length.
+    const bool whole_head = SPLIT ? attn_splits(p, n_tiles, (ctx + kHeadPassTokens - 1) / kHeadPassTokens) == 1 : true;
     const int head_stride = G / kNkv;
     rope_table(p.inv_freq, pos, cs, c.tid);
     if (c.tid == 0) {
@@ -703,15 +812,19 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
             const size_t layer_bytes = static_cast<size_t>(l) * kNkv * p.max_seq * kHd * sizeof(KV);
             // The cached K/V rows this CTA's attention will read do not depend on this step: pull them
             // into L2 now (the same assignment as the attention below).
-            for (int q = c.tid; q < 2 * kNkv * n_tiles; q += kCt) {
-                const int i = q >> 1;
-                const int h = i / n_tiles, tile = i % n_tiles;
-                const bool mine = whole_head ? (blockIdx.x == h * head_stride) : (i % G == static_cast<int>(blockIdx.x));
-                if (!mine) continue;
-                const int n = min(kAttnTile, ctx - tile * kAttnTile);
-                const size_t off = (static_cast<size_t>(h) * p.max_seq + tile * kAttnTile) * kHd * sizeof(KV);
-                const uint8_t* base = static_cast<const uint8_t*>((q & 1) ? p.v_cache : p.k_cache);
-                bulk_prefetch_l2(base + layer_bytes + off, static_cast<uint32_t>(n * kHd * sizeof(KV)));
+            if (whole_head) {
+                if (blockIdx.x % head_stride == 0 && blockIdx.x / head_stride < kNkv) {
+                    const int h = blockIdx.x / head_stride;
+                    for (int q = c.tid; q < 2 * n_tiles; q += kCt) {
+                        const int tile = q >> 1;
+                        const int n = min(kAttnTile, ctx - tile * kAttnTile);
+                        const size_t off = (static_cast<size_t>(h) * p.max_seq + tile * kAttnTile) * kHd * sizeof(KV);
+                        const uint8_t* base = static_cast<const uint8_t*>((q & 1) ? p.v_cache : p.k_cache);
+                        bulk_prefetch_l2(base + layer_bytes + off, static_cast<uint32_t>(n * kHd * sizeof(KV)));
+                    }
+                }
+            } else if constexpr (SPLIT) {
+                prefetch_split_kv<KV>(c, layer_bytes, ctx);
             }
             if (l > 0) {
                 tsrc = p.t_xout;
@@ -724,13 +837,13 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
                 trace_mark(p, l * 5 + 1, 0);
                 trace_mark(p, l * 5 + 1, 1);
             }
-            const size_t layer_off = static_cast<size_t>(l) * kNkv * p.max_seq * kHd;
-            KV* kc = static_cast<KV*>(p.k_cache) + layer_off;
-            KV* vc = static_cast<KV*>(p.v_cache) + layer_off;
-            const TaggedSrc qkv_src{&p, c.fl, p.t_qkv, act_tag(p, l, kTagQkv), 30u + l};
-            const TaggedDst att_dst{p.t_att, act_tag(p, l, kTagAtt)};
             if (whole_head) {
                 if (blockIdx.x % head_stride == 0 && blockIdx.x / head_stride < kNkv) {
+                    const size_t layer_off = static_cast<size_t>(l) * kNkv * p.max_seq * kHd;
+                    KV* kc = static_cast<KV*>(p.k_cache) + layer_off;
+                    KV* vc = static_cast<KV*>(p.v_cache) + layer_off;
+                    const TaggedSrc qkv_src{&p, c.fl, p.t_qkv, act_tag(p, l, kTagQkv), 30u + l};
+                    const TaggedDst att_dst{p.t_att, act_tag(p, l, kTagAtt)};
                     const int h = blockIdx.x / head_stride;
                     uint4 hk[4];  // cached keys of the first pass: independent of this step's projections
                     if (kHeadWarpTokens * c.cw < ctx) head_load_keys<KV>(kc, p.max_seq, h, pos, 0, c.cw, c.lane, hk);
@@ -739,23 +852,35 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
                                          [] { csync(); });
                     csync();
                 }
-            } else {
-                AttSmem<KV>& sm = *reinterpret_cast<AttSmem<KV>*>(c.xp);
-                for (int i = blockIdx.x; i < kNkv * n_tiles; i += G) {
-                    const int h = i / n_tiles, tile = i % n_tiles;
-                    attend_tile<KV, true>(qkv_src, kNh, kNkv, cs, kc, vc, p.max_seq, h, tile, ctx, n_slots, p.part_o,
-                                          p.part_ml, sm, c.tid, [] { csync(); });
-                    if (c.tid == 0) {
-                        const unsigned old = atom_acq_rel_gpu_add(p.sync + kSyncTicket + l * kNkv + h, 1u);
-                        c.fl->role = (old == static_cast<unsigned>(n_tiles - 1)) ? 1 : 0;
+            } else if constexpr (SPLIT) {
+                const size_t layer_off = static_cast<size_t>(l) * kNkv * p.max_seq * kHd;
+                KV* kc = static_cast<KV*>(p.k_cache) + layer_off;
+                KV* vc = static_cast<KV*>(p.v_cache) + layer_off;
+                const TaggedSrc qkv_src{&p, c.fl, p.t_qkv, act_tag(p, l, kTagQkv), 30u + l};
+                const TaggedDst att_dst{p.t_att, act_tag(p, l, kTagAtt)};
+                const AttnRole ar = attn_role(p, ctx);
+                const int n_slots = p.max_seq / kAttnTile;  // partial slots per query head (>= any S)
+                if (ar.head >= 0) {
+                    const int h = ar.head, sp = ar.split;
+                    uint4 hk[4];  // cached keys of the range's first pass: independent of this step's projections
+                    if (ar.p0 * kHeadPassTokens + kHeadWarpTokens * c.cw < ctx) {
+                        head_load_keys<KV>(kc, p.max_seq, h, pos, ar.p0, c.cw, c.lane, hk);
                     }
+                    HeadPassSmem<KV>& sm = *reinterpret_cast<HeadPassSmem<KV>*>(c.xp);
+                    // The range that holds pos inserts the new token. Partials go to slot = range; after a
+                    // barrier (all of the CTA's stores done) one release store of the step's tag publishes them.
+                    attend_head_span<KV>(
+                        qkv_src, kNh, kNkv, cs, kc, vc, p.max_seq, h, ctx, ar.p0, ar.p1, ar.p1 == ar.n_pass,
+                        [&](int hq, int d, float O, float M, float L) {
+                            const size_t slot = static_cast<size_t>(hq) * n_slots + sp;
+                            __stcg(p.part_o + slot * kHd + d, O);
+                            if (d == 0) __stcg(reinterpret_cast<float2*>(p.part_ml) + slot, make_float2(M, L));
+                        },
+                        sm, c.tid, hk, [] { csync(); });
                     csync();
-                    const bool combiner = c.fl->role != 0;
-                    csync();
-                    if (combiner) {
-                        combine_head(p.part_o, p.part_ml, h, n_tiles, n_slots, att_dst, c.tid);
-                        csync();
-                    }
+                    if (c.tid == 0) st_release_gpu(p.sync + kSyncFlags + 32 * h + sp, act_tag(p, l, kTagPart));
+                } else if (ar.merge >= 0) {
+                    combine_splits(c, ar.merge, ar.S, n_slots, act_tag(p, l, kTagPart), att_dst, 50u + l);
                 }
             }
             if (c.tid == 0) trace_mark(p, l * 5 + 1, 2);
@@ -851,7 +976,7 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
     }
 }
 
-template <WeightType WT, typename KV>
+template <WeightType WT, typename KV, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kOffBars);
@@ -899,13 +1024,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     c.cw = c.tid >> 5;
     c.lane = c.tid & 31;
     c.t_base = 0;
-    run_consumers<WT, KV>(c, reinterpret_cast<float*>(smem + kOffCs));
+    run_consumers<WT, KV, SPLIT>(c, reinterpret_cast<float*>(smem + kOffCs));
     if (fl->abort) atomicOr(p.err, kErrAborted);
 }
 
-template <WeightType WT, typename KV>
+template <WeightType WT, typename KV, bool SPLIT>
 void launch_typed(const StepParams& p, cudaStream_t stream) {
-    auto kernel = decode_step_kernel<WT, KV>;
+    auto kernel = decode_step_kernel<WT, KV, SPLIT>;
     static bool configured[64] = {};
     int dev = 0;
     CLLM_CUDA(cudaGetDevice(&dev));
@@ -924,26 +1049,35 @@ void launch_typed(const StepParams& p, cudaStream_t stream) {
                                           kSmemBytes, stream));
 }
 
+template <WeightType WT, typename KV>
+void launch_kv(const StepParams& p, bool split, cudaStream_t stream) {
+    if (split) {
+        launch_typed<WT, KV, true>(p, stream);
+    } else {
+        launch_typed<WT, KV, false>(p, stream);
+    }
+}
+
 }  // namespace
 
 int decode_step_smem_bytes() { return kSmemBytes; }
 
 int decode_step_grid() { return num_sms(); }
 
-void launch_decode_step(const StepParams& p, WeightType wt, KvType kv, cudaStream_t stream) {
+void launch_decode_step(const StepParams& p, WeightType wt, KvType kv, bool split, cudaStream_t stream) {
     CLLM_CHECK(p.max_seq % kAttnTile == 0, "decode step: max_seq must be a multiple of 64");
     CLLM_CHECK((kH + decode_step_grid() - 1) / decode_step_grid() <= kMaxResRows,
                "decode step: too few SMs for the on-chip residual rows");
     const bool f16 = kv == KvType::F16;
     switch (wt) {
         case WeightType::BF16:
-            f16 ? launch_typed<WeightType::BF16, __half>(p, stream) : launch_typed<WeightType::BF16, __nv_bfloat16>(p, stream);
+            f16 ? launch_kv<WeightType::BF16, __half>(p, split, stream) : launch_kv<WeightType::BF16, __nv_bfloat16>(p, split, stream);
             return;
         case WeightType::INT8:
-            f16 ? launch_typed<WeightType::INT8, __half>(p, stream) : launch_typed<WeightType::INT8, __nv_bfloat16>(p, stream);
+            f16 ? launch_kv<WeightType::INT8, __half>(p, split, stream) : launch_kv<WeightType::INT8, __nv_bfloat16>(p, split, stream);
             return;
         case WeightType::INT4:
-            f16 ? launch_typed<WeightType::INT4, __half>(p, stream) : launch_typed<WeightType::INT4, __nv_bfloat16>(p, stream);
+            f16 ? launch_kv<WeightType::INT4, __half>(p, split, stream) : launch_kv<WeightType::INT4, __nv_bfloat16>(p, split, stream);
             return;
     }
     throw InternalError("decode step: unknown weight type");

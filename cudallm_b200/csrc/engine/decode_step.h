@@ -63,10 +63,17 @@ inline constexpr size_t trace_words(int grid) {
 constexpr unsigned kErrWaitTimeout = 1u;
 constexpr unsigned kErrAborted = 2u;
 
-// Counters the step uses (zeroed at creation, after an error and by the step itself at its end): the
-// split attention's per-(layer, KV head) tickets and the lm_head ticket. Activations between operations
+// Attention past whole_head_max_tiles: every KV head's context is cut into S <= kAttnMaxSplits ranges of
+// 128-token passes, one CTA per (head, range), and one further CTA per head merges the S partials
+// (O[64], M, L per query head, in part_o / part_ml at slot = range) in range order. A range CTA publishes
+// its partials by a release store of this step's tag into its flag word (sync[kSyncFlags + 32 h + range]);
+// the merging CTA acquires the S flags, then reads the partials.
+constexpr int kAttnMaxSplits = 17;
+
+// Words the step uses (zeroed at creation, after an error and by the step itself at its end): the split
+// attention's per-(KV head, range) flags and the lm_head ticket. Activations between operations
 // are synchronised through their tags, not counters.
-constexpr int kSyncTicket = 0, kSyncLm = 16 * 8, kSyncWords = 256;
+constexpr int kSyncFlags = 0, kSyncLm = 8 * 32, kSyncWords = 512;
 
 struct StepParams {
     StepLayer layers[kStepLayers];
@@ -113,8 +120,10 @@ struct StepParams {
 // Shared memory bytes of one CTA of the persistent kernel.
 int decode_step_smem_bytes();
 // Prepares (once per device) and launches one step on `stream` as a cooperative launch with one CTA
-// per SM. Throws if the device cannot hold the grid.
-void launch_decode_step(const StepParams& p, WeightType wt, KvType kv, cudaStream_t stream);
+// per SM. Throws if the device cannot hold the grid. split: launch the instantiation whose attention cuts
+// a context into ranges over many CTAs (for contexts past whole_head_max_tiles tiles); the other gives each
+// KV head one CTA. Both compute every context length correctly; the choice only affects speed.
+void launch_decode_step(const StepParams& p, WeightType wt, KvType kv, bool split, cudaStream_t stream);
 // Grid size the launch uses (the number of SMs).
 int decode_step_grid();
 

@@ -34,9 +34,11 @@ namespace {
 constexpr size_t kRegionAlign = 256;
 constexpr unsigned long long kWaitLimitNs = 1000000000ull;   // each inter-CTA wait of the persistent step
 constexpr unsigned long long kDrainLimitNs = 1000000000ull;  // its final wait for copies still in flight
-// Contexts up to this many 64-token tiles attend with one CTA per KV head; longer ones spread (head, tile)
-// items over all CTAs (the measured cross-over of the two forms).
-constexpr int kWholeHeadMaxTiles = 2;
+// Contexts up to this many 64-token tiles attend with one CTA per KV head; longer ones cut each head's
+// context into ranges over many CTAs (the split instantiation of the step). The measured cross-over of the
+// two forms on B200: ~384 tokens for bf16 / int8 weights, ~512 for int4 (whose step is shorter).
+constexpr int kWholeHeadMaxTiles = 6;
+constexpr int kWholeHeadMaxTilesInt4 = 8;
 // L2 prefetch distance of the persistent weight stream, in tiles: 24 tiles of 16 KiB for bf16 / int8; int4
 // tiles hold 2 rows, so the same byte distance is ~8x as many tiles.
 constexpr int kPrefetchTiles = 24;
@@ -183,7 +185,7 @@ void Engine::make_step_params() {
     p.drain_limit_ns = kDrainLimitNs;
     p.prefetch_tiles = c.wtype == WeightType::INT4 ? kPrefetchTilesInt4 : kPrefetchTiles;
     p.prefetch_mode = 3;  // bulk L2 prefetches from the prefetch warp
-    p.whole_head_max_tiles = kWholeHeadMaxTiles;
+    p.whole_head_max_tiles = c.wtype == WeightType::INT4 ? kWholeHeadMaxTilesInt4 : kWholeHeadMaxTiles;
     p.stall_op = -1;
     // The persistent kernel has its own compile-time tile shape (matvec_rpb applies to the per-op kernels;
     // results do not depend on either).
@@ -246,7 +248,9 @@ void Engine::launch_step_kernel(int token, float* debug_res) {
     p.token_override = token;
     p.debug_res = debug_res;
     p.trace = trace_on_ ? trace_ : nullptr;
-    launch_decode_step(p, config().wtype, opts_.kv, stream_);
+    // The step's context is host_pos_ + 1 tokens (the host mirror is exact for the persistent path).
+    const int tiles = (host_pos_ + 1 + kAttnTile - 1) / kAttnTile;
+    launch_decode_step(p, config().wtype, opts_.kv, tiles > p.whole_head_max_tiles, stream_);
 }
 
 void Engine::set_trace(bool enable) {

@@ -151,7 +151,7 @@ private:
     float* am_v_ = nullptr;     // argmax partials
     int* am_i_ = nullptr;
     DevState* state_ = nullptr;
-    unsigned* sync_ = nullptr;  // persistent step: tickets
+    unsigned* sync_ = nullptr;  // persistent step: split-attention flags and the lm_head ticket
     float* debug_res_ = nullptr;  // persistent step_debug: residuals [(layers + 1) * hidden]
     unsigned long long* tagged_ = nullptr;  // persistent step: (value, tag) activation words
     size_t tagged_words_ = 0;

@@ -274,6 +274,138 @@ __device__ __forceinline__ void head_load_values(const KV* v_cache, int max_seq,
     }
 }
 
+// Attention of KV head h for context ctx (= pos + 1) over the 128-token passes [pass_lo, pass_hi): rotates
+// the 4 query heads (cs = rope table of pos). The range that holds pos (insert_new) also rotates the new key,
+// rounds k and v to the cache type, writes them to the cache and uses the rounded values; every other range
+// only reads cached tokens below pos. k holds the keys of pass pass_lo (head_load_keys, issued by the caller
+// before it waited for the QKV projection: they do not depend on this step); later passes load their keys
+// at the pass start, and every pass loads its values after the scores (their latency overlaps the softmax).
+// The caller prefetches the range's cached rows into L2 when the layer starts. The 8 warps' running softmax states are merged in warp order and handed to
+// emit(hq, d, O, M, L) for query head hq = 4h + 0..3 and dim d (thread tid = 64 (hq - 4h) + d): O = sum of
+// exp(s - M) v over the range, L = sum of exp(s - M). `sync()` is a barrier over the 256 participating threads.
+template <typename KV, typename Sync, typename Src, typename Emit>
+__device__ __forceinline__ void attend_head_span(Src qkv, int nh, int nkv, const float* cs, KV* k_cache, KV* v_cache,
+                                                 int max_seq, int h, int ctx, int pass_lo, int pass_hi, bool insert_new,
+                                                 Emit emit, HeadPassSmem<KV>& sm, int tid, uint4 (&k)[4], Sync sync) {
+    using KV2 = typename Kv2<KV>::T;
+    const int pos = ctx - 1;
+    const int w = tid >> 5, lane = tid & 31;
+    if (tid < kGqa * kHd / 2) {
+        const int g = tid >> 5, i = tid & 31;
+        const int q = (h * kGqa + g) * kHd;
+        const float x0 = qkv(q + i), x1 = qkv(q + i + kHd / 2);
+        const float c = cs[i], s = cs[kHd / 2 + i];
+        sm.qs[g][i] = x0 * c - x1 * s;
+        sm.qs[g][i + kHd / 2] = x1 * c + x0 * s;
+    } else if (insert_new && tid < kGqa * kHd / 2 + kHd / 2) {
+        const int i = tid - kGqa * kHd / 2;
+        const int kp = (nh + h) * kHd;
+        const float x0 = qkv(kp + i), x1 = qkv(kp + i + kHd / 2);
+        const float c = cs[i], s = cs[kHd / 2 + i];
+        const KV k0 = to_kv<KV>(x0 * c - x1 * s), k1 = to_kv<KV>(x1 * c + x0 * s);
+        sm.kn[i] = k0;
+        sm.kn[i + kHd / 2] = k1;
+        KV* kdst = k_cache + (static_cast<size_t>(h) * max_seq + pos) * kHd;
+        kdst[i] = k0;
+        kdst[i + kHd / 2] = k1;
+    } else if (insert_new && tid < kGqa * kHd / 2 + kHd / 2 + kHd) {
+        const int d = tid - kGqa * kHd / 2 - kHd / 2;
+        const KV vv = to_kv<KV>(qkv((nh + nkv + h) * kHd + d));
+        sm.vn[d] = vv;
+        v_cache[(static_cast<size_t>(h) * max_seq + pos) * kHd + d] = vv;
+    }
+    sync();
+    float m_run[kGqa], l_run[kGqa], o[kGqa][2];
+#pragma unroll
+    for (int hq = 0; hq < kGqa; ++hq) {
+        m_run[hq] = -INFINITY;
+        l_run[hq] = 0.f;
+        o[hq][0] = o[hq][1] = 0.f;
+    }
+    for (int pass = pass_lo; pass < pass_hi; ++pass) {
+        const int base = pass * kHeadPassTokens + kHeadWarpTokens * w;
+        if (base >= ctx) break;  // warp-uniform: no token of this warp is in the context
+        if (pass > pass_lo) head_load_keys<KV>(k_cache, max_seq, h, pos, pass, w, lane, k);
+        const int j = base + (lane >> 1), half = lane & 1;
+        if (j == pos) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) k[c] = reinterpret_cast<const uint4*>(sm.kn)[4 * half + c];
+        }
+        float dot[kGqa] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            float kf[8];
+            unpack8<KV>(k[c], kf);
+#pragma unroll
+            for (int hq = 0; hq < kGqa; ++hq) {
+#pragma unroll
+                for (int e = 0; e < 8; ++e) dot[hq] = fmaf(kf[e], sm.qs[hq][32 * half + 8 * c + e], dot[hq]);
+            }
+        }
+        // Values: loaded once the key registers are free; their latency overlaps the softmax.
+        uint32_t v[kHeadWarpTokens];
+        head_load_values<KV>(v_cache, max_seq, h, pos, pass, w, lane, v);
+        if (pos >= base && pos < base + kHeadWarpTokens) {
+#pragma unroll
+            for (int i = 0; i < kHeadWarpTokens; ++i) {
+                if (base + i == pos) v[i] = reinterpret_cast<const uint32_t*>(sm.vn)[lane];
+            }
+        }
+        float pj[kGqa];
+#pragma unroll
+        for (int hq = 0; hq < kGqa; ++hq) {
+            const float d = dot[hq] + __shfl_xor_sync(0xffffffffu, dot[hq], 1);  // both halves of the row
+            const float sc = j < ctx ? 0.125f * d : -INFINITY;
+            const float mn = fmaxf(m_run[hq], warp_max(sc));  // finite: the warp's first token is in the context
+            const float a = expf(m_run[hq] - mn);
+            pj[hq] = expf(sc - mn);
+            l_run[hq] = l_run[hq] * a + 0.5f * warp_sum(pj[hq]);  // every token is counted by its two lanes
+            o[hq][0] *= a;
+            o[hq][1] *= a;
+            m_run[hq] = mn;
+        }
+        if (half == 0) sm.ps[w][lane >> 1] = make_float4(pj[0], pj[1], pj[2], pj[3]);
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < kHeadWarpTokens; ++i) {
+            const float4 p4 = sm.ps[w][i];
+            const float2 vf = kv2_to_float2(*reinterpret_cast<const KV2*>(&v[i]));
+            o[0][0] = fmaf(p4.x, vf.x, o[0][0]);
+            o[0][1] = fmaf(p4.x, vf.y, o[0][1]);
+            o[1][0] = fmaf(p4.y, vf.x, o[1][0]);
+            o[1][1] = fmaf(p4.y, vf.y, o[1][1]);
+            o[2][0] = fmaf(p4.z, vf.x, o[2][0]);
+            o[2][1] = fmaf(p4.z, vf.y, o[2][1]);
+            o[3][0] = fmaf(p4.w, vf.x, o[3][0]);
+            o[3][1] = fmaf(p4.w, vf.y, o[3][1]);
+        }
+        __syncwarp();
+    }
+#pragma unroll
+    for (int hq = 0; hq < kGqa; ++hq) {
+        *reinterpret_cast<float2*>(&sm.wo[w][hq][2 * lane]) = make_float2(o[hq][0], o[hq][1]);
+        if (lane == 0) {
+            sm.wm[w][hq] = m_run[hq];
+            sm.wl[w][hq] = l_run[hq];
+        }
+    }
+    sync();
+    {
+        const int g = tid >> 6, d = tid & 63;
+        float M = -INFINITY;
+#pragma unroll
+        for (int ww = 0; ww < 8; ++ww) M = fmaxf(M, sm.wm[ww][g]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int ww = 0; ww < 8; ++ww) {
+            const float e = expf(sm.wm[ww][g] - M);  // 0 for a warp that had no token
+            L = fmaf(sm.wl[ww][g], e, L);
+            O = fmaf(sm.wo[ww][g][d], e, O);
+        }
+        emit(h * kGqa + g, d, O, M, L);
+    }
+}
+
 // Attention of KV head h for context ctx (= pos + 1): rotates the 4 query heads and the new key
 // (cs = rope table of pos), rounds k and v to the cache type, writes them to the cache and uses the
 // rounded values. out receives [4][64] at query head 4h. k holds the keys of pass 0 (head_load_keys,

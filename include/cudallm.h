@@ -147,8 +147,8 @@ int cudallm_debug_read_trace(cudallm_engine* e, unsigned long long* out, unsigne
  * name, a value out of range, or a per-op engine. Knobs: "wait_limit_ns" (bound of every inter-block wait of
  * the step, 1 .. 1e10; default 1e9; a step whose wait runs out returns CUDALLM_ERR_STATE and leaves the
  * position unchanged), "prefetch_tiles" (L2 prefetch distance of the weight stream, 0 .. 1024),
- * "whole_head_max_tiles" (contexts up to this many 64-token tiles attend with one block per KV head, 0 ..
- * max_seq_len/64; default 2), "trace_tile_op" (weight operation whose tiles the trace stamps, 0 .. 64),
+ * "whole_head_max_tiles" (contexts up to this many 64-token tiles attend with one block per KV head, longer
+ * ones split each head's context over many blocks, 0 .. max_seq_len/64; default 6, int4 weights 8), "trace_tile_op" (weight operation whose tiles the trace stamps, 0 .. 64),
  * "stall_op" (for tests of the failure path: the blocks computing weight operation k, 1 .. 64, wait for an
  * input that is never written, so every such wait runs out after wait_limit_ns and the step fails with
  * CUDALLM_ERR_STATE; -1 = off, the default). */

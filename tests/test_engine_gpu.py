@@ -186,8 +186,8 @@ def test_sequence_full_and_bad_token(model_path):
 
 @pytest.mark.parametrize("kv", ["fp16", "bf16"])
 def test_long_context_persistent_matches_per_op(model_path, kv):
-    """Past 128 tokens (two 64-token tiles) the persistent kernel switches from whole-head attention to
-    split-K across CTAs with an ordered merge; it must agree with the per-op path (split-K kernels + separate RoPE/KV write,
+    """Past whole_head_max_tiles 64-token tiles (8 for int4) the persistent kernel cuts each KV head's context
+    into ranges over many CTAs and merges their partials in range order; it must agree with the per-op path (split-K kernels + separate RoPE/KV write,
     themselves checked against float64 by the kernel tests) on the same token stream."""
     path, _ = model_path("int4")
     rng = np.random.default_rng(3)
