@@ -29,8 +29,17 @@ constexpr int kLaunchRegs = 168;  // 65536 / 384 rounded down to a multiple of 8
 constexpr int kProducerRegs = 88;
 constexpr int kConsumerRegs = 208;
 static_assert(kProducerRegs * 128 + kConsumerRegs * kCt == kLaunchRegs * kThreads, "register split must use the launch pool");
+// Weight ring: kStages stages of 16 KiB in the short-context kernel; the split-attention kernel keeps
+// kSplitStages of them and gives the rest to its K/V tile ring (kAttRingSlots slots of one 64-token K tile +
+// V tile each). Barrier and tile-word arrays are laid out for kStages.
 constexpr int kStages = 12;
+constexpr int kSplitStages = 8;
+constexpr int kAttRingSlots = 4;
 static_assert(kStages <= 32, "one producer lane per stage");
+template <bool SPLIT>
+constexpr int ring_stages() {
+    return SPLIT ? kSplitStages : kStages;
+}
 constexpr int kMaxK = 8192;
 constexpr int kOpsPerLayer = 4;
 constexpr int kWeightOps = kStepLayers * kOpsPerLayer + 1;  // + tied lm_head
@@ -63,6 +72,9 @@ constexpr int kOffXp = 3072;
 constexpr int kOffRing = kOffXp + kMaxK * 4;  // 35840
 constexpr int kSmemBytes = kOffRing + kStages * kStageBytes;
 static_assert(kOffTiles + kStages * 4 <= kOffFlags, "barriers overflow");
+constexpr int kOffAttBars = 352;  // kAttRingSlots mbarriers of the split kernel's K/V ring
+static_assert(kOffAttBars % 8 == 0 && kOffAttBars + kAttRingSlots * 8 <= kOffRed, "attention barriers overflow");
+static_assert((kStages - kSplitStages) * kStageBytes >= kAttRingSlots * 2 * kAttnTile * 64 * 2, "K/V ring must fit");
 static_assert(kOffAm + kCw * 8 <= kOffRes && kOffRes + kMaxResRows * 4 <= kOffXc, "argmax / residual scratch overflow");
 static_assert(kOffXc + (kMaxK / 32) * 4 <= kOffXp, "chunk sums overflow");
 static_assert(sizeof(AttSmem<__half>) <= kMaxK * 4, "attention scratch must fit in the vector area");
@@ -89,6 +101,21 @@ constexpr int stage_rows() {
     constexpr int cap = decode_step_tile_rows(WT);
     return (fit < cap ? fit : cap) * halves;
 }
+
+// How the consumer warps share the stages of one operation kind: kRows stage rows (both halves for the
+// gate/up operation), kWps warps per stage (1: one warp consumes a whole stage; >1: the stage's rows are
+// split over kWps warps and kCw / kWps warp groups take stages in turn), kNw rows per warp, kHalf of them
+// per half, kCpl 16-byte chunks per lane of a row. int4 shares stages; bf16 and int8 do not.
+template <WeightType WT, int KIND>
+struct StageShape {
+    static constexpr int kHalves = KIND == 2 ? 2 : 1;
+    static constexpr int kRows = stage_rows<WT, KIND>();
+    static constexpr int kWps = WT == WeightType::INT4 ? (KIND == 3 ? 4 : 8) : 1;
+    static constexpr int kNw = kRows / kWps;
+    static constexpr int kHalf = kNw / kHalves;
+    static constexpr int kCpl = seg_chunks_per_lane<WT, KIND>();
+    static_assert(kRows % kWps == 0 && kNw % kHalves == 0 && kNw <= 32, "stage rows must split evenly over the warps");
+};
 
 struct WOp {
     const uint8_t* w;
@@ -196,7 +223,7 @@ __device__ __forceinline__ uint8_t* smem_base() {
 struct KindRows {
     int lo, hi, nt;
 };
-static_assert(kOffKinds + 5 * sizeof(KindRows) <= kOffRed, "kind table overflow");
+static_assert(kOffKinds + 5 * sizeof(KindRows) <= kOffAttBars, "kind table overflow");
 __device__ __forceinline__ KindRows kind_rows(const TileGeom& g) {
     KindRows r;
     split_rows(g.out_rows, r.lo, r.hi);
@@ -267,6 +294,7 @@ __device__ __forceinline__ void issue_tile(const WOp& op, int lo, int hi, int i,
 // order) into it, issuing each copy as soon as the stage is released. The lanes poll their stages with
 // non-blocking tests in one converged loop, so a stage that is still in use never holds back another
 // lane's copy. Lane 0 publishes the lowest tile index not yet issued for the prefetch warp.
+template <int ST>
 __device__ void run_producer(const StepParams& p, uint8_t* ring, uint64_t* full, uint64_t* empty, volatile int* stage_tile,
                              volatile Flags* fl) {
     const int lane = threadIdx.x & 31;
@@ -275,7 +303,7 @@ __device__ void run_producer(const StepParams& p, uint8_t* ring, uint64_t* full,
     cur.init();
     cur.advance(lane);
     int t = lane, k = 0;  // next tile of this lane; copies issued into its stage so far
-    bool more = lane < kStages && cur.valid();
+    bool more = lane < ST && cur.valid();
     uint64_t t_idle = 0;
     for (uint32_t it = 1;; ++it) {
         bool progressed = false;
@@ -285,8 +313,8 @@ __device__ void run_producer(const StepParams& p, uint8_t* ring, uint64_t* full,
             trace_tile(p, t, 0);
             issue_tile(weight_op(p, cur.o), cur.lo, cur.hi, cur.i, ring + lane * kStageBytes, &full[lane], pol);
             ++k;
-            t += kStages;
-            cur.advance(kStages);
+            t += ST;
+            cur.advance(ST);
             more = cur.valid();
             progressed = true;
         }
@@ -309,7 +337,7 @@ __device__ void run_producer(const StepParams& p, uint8_t* ring, uint64_t* full,
     }
     // Every copy issued lands before the CTA may exit. The drain has its own limit, independent of the
     // (possibly short) dependency-wait limit: the copies are plain reads and always finish.
-    if (lane < kStages && k > 0) wait_bar(p, &full[lane], (k - 1) & 1, fl, p.drain_limit_ns, 2000u);
+    if (lane < ST && k > 0) wait_bar(p, &full[lane], (k - 1) & 1, fl, p.drain_limit_ns, 2000u);
 }
 
 // Warp 1: L2 prefetch of the weight stream with ordinary prefetch instructions (load/store units,
@@ -336,7 +364,8 @@ __device__ void run_prefetcher(const StepParams& p, volatile Flags* fl) {
         const int r0 = pf.lo + pf.i * op.g.rows_per_tile;
         const int bytes = min(op.g.rows_per_tile, pf.hi - r0) * op.g.row_bytes;
         for (int h = 0; h < op.g.halves; ++h) {
-            const uint8_t* a = op.w + (static_cast<size_t>(r0) + static_cast<size_t>(h) * op.g.out_rows) * op.g.row_bytes;
+            const size_t row = static_cast<size_t>(r0) + static_cast<size_t>(h) * op.g.out_rows;
+            const uint8_t* a = op.w + row * op.g.row_bytes;
             if (p.prefetch_mode == 3) {
                 if (lane == 0) bulk_prefetch_l2(a, static_cast<uint32_t>(bytes));  // one request per half (bulk engine)
             } else {
@@ -550,6 +579,251 @@ __device__ __forceinline__ AttnRole attn_role(const StepParams& p, int ctx) {
     return r;
 }
 
+// ---- Range attention of the split kernel: K/V tiles through a ring of bulk copies -------------------
+// One CTA computes the 4 query heads of KV head h over the 64-token tiles [T0, T1) of the context. Its two
+// warp halves take alternate tiles (half f: tiles T0 + f, T0 + f + 2, ...); each tile's K and V rows
+// (8 KiB each, contiguous in the cache) arrive in one of kAttRingSlots shared-memory slots by bulk copies
+// completing on the slot's mbarrier, so up to four tiles (64 KiB) stream while one per half is computed.
+// Per tile and half (128 threads, the layout of the batched streaming attention): thread (token j, dims
+// 8c..8c+7) forms partial dots for the 4 heads, a butterfly over the token's 8 lanes completes them; warp g
+// advances head g's running (max, sum); p.V by token groups with per-head rescaling. The halves' states are
+// merged at the end and handed to emit(hq, d, O, M, L). The range that holds pos rotates the new key,
+// rounds k and v to the cache type, writes them to the cache and patches them into its last tile. Every
+// wait is bounded; a CTA that gives up lets its issued copies land before it goes on.
+template <typename KV>
+struct RangeAttnSmem {
+    float qs[kGqa][kHd];
+    alignas(16) KV kn[kHd];
+    alignas(16) KV vn[kHd];
+    float s[2][kAttnTile][kGqa];  // per half: scores, then probabilities, of the tile
+    float alpha[2][kGqa];
+    float mh[2][kGqa], lh[2][kGqa];
+    int ok[2];
+};
+static_assert(sizeof(RangeAttnSmem<__half>) <= kMaxK * 4, "range attention scratch must fit in the vector area");
+
+template <typename KV, typename Src, typename Emit>
+__device__ void attend_range_stream(const ConsumerCtx& c, int layer, int h, int T0, int T1, int ctx, bool insert_new,
+                                    const float* cs, KV* k_cache, KV* v_cache, Src qkv, Emit emit) {
+    using KV2 = typename Kv2<KV>::T;
+    constexpr int kTileBytes = kAttnTile * kHd * static_cast<int>(sizeof(KV));
+    const StepParams& p = *c.p;
+    const int pos = ctx - 1;
+    const int tid = c.tid, hf = tid >> 7, th = tid & 127, warp = th >> 5, lane = c.lane, c8 = th & 7;
+    RangeAttnSmem<KV>& sm = *reinterpret_cast<RangeAttnSmem<KV>*>(c.xp);
+    uint8_t* ring = smem_base() + kOffRing + kSplitStages * kStageBytes;
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_base() + kOffAttBars);
+    const int n = T1 - T0;
+    auto slot_k = [&](int sl) { return reinterpret_cast<KV*>(ring + sl * 2 * kTileBytes); };
+    auto slot_v = [&](int sl) { return reinterpret_cast<KV*>(ring + sl * 2 * kTileBytes + kTileBytes); };
+    // Every layer of a step uses each slot the same number of times, so tile i's phase parity follows.
+    auto parity = [&](int i) {
+        const int sl = i % kAttRingSlots;
+        const int per_layer = sl < n ? (n - sl + kAttRingSlots - 1) / kAttRingSlots : 0;
+        return static_cast<uint32_t>((layer * per_layer + i / kAttRingSlots) & 1);
+    };
+    const uint64_t pol = l2_policy_evict_first();
+    const KV* kg = k_cache + static_cast<size_t>(h) * p.max_seq * kHd;
+    const KV* vg = v_cache + static_cast<size_t>(h) * p.max_seq * kHd;
+    auto issue = [&](int i) {
+        const int t = T0 + i, sl = i % kAttRingSlots;
+        const uint32_t bytes = static_cast<uint32_t>(min(kAttnTile, ctx - t * kAttnTile) * kHd * sizeof(KV));
+        mbar_arrive_expect_tx(&bars[sl], 2 * bytes);
+        bulk_load(slot_k(sl), kg + static_cast<size_t>(t) * kAttnTile * kHd, bytes, &bars[sl], pol);
+        bulk_load(slot_v(sl), vg + static_cast<size_t>(t) * kAttnTile * kHd, bytes, &bars[sl], pol);
+    };
+    // Cached tiles do not depend on this step: their copies start before q is waited for.
+    if (tid == 0) {
+        for (int i = 0; i < min(kAttRingSlots, n); ++i) issue(i);
+    }
+    if (tid < kGqa * kHd / 2) {
+        const int g = tid >> 5, i = tid & 31;
+        const int q = (h * kGqa + g) * kHd;
+        const float x0 = qkv(q + i), x1 = qkv(q + i + kHd / 2);
+        const float cz = cs[i], sz = cs[kHd / 2 + i];
+        sm.qs[g][i] = x0 * cz - x1 * sz;
+        sm.qs[g][i + kHd / 2] = x1 * cz + x0 * sz;
+    } else if (insert_new && tid < kGqa * kHd / 2 + kHd / 2) {
+        const int i = tid - kGqa * kHd / 2;
+        const int kp = (kNh + h) * kHd;
+        const float x0 = qkv(kp + i), x1 = qkv(kp + i + kHd / 2);
+        const float cz = cs[i], sz = cs[kHd / 2 + i];
+        const KV k0 = to_kv<KV>(x0 * cz - x1 * sz), k1 = to_kv<KV>(x1 * cz + x0 * sz);
+        sm.kn[i] = k0;
+        sm.kn[i + kHd / 2] = k1;
+        KV* kdst = k_cache + (static_cast<size_t>(h) * p.max_seq + pos) * kHd;
+        kdst[i] = k0;
+        kdst[i + kHd / 2] = k1;
+    } else if (insert_new && tid < kGqa * kHd / 2 + kHd / 2 + kHd) {
+        const int d = tid - kGqa * kHd / 2 - kHd / 2;
+        const KV vv = to_kv<KV>(qkv((kNh + kNkv + h) * kHd + d));
+        sm.vn[d] = vv;
+        v_cache[(static_cast<size_t>(h) * p.max_seq + pos) * kHd + d] = vv;
+    }
+    csync();
+    float2 q[kGqa][4];
+#pragma unroll
+    for (int g = 0; g < kGqa; ++g) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) q[g][e] = make_float2(sm.qs[g][8 * c8 + 2 * e], sm.qs[g][8 * c8 + 2 * e + 1]);
+    }
+    float2 acc[kGqa][4];
+#pragma unroll
+    for (int g = 0; g < kGqa; ++g) {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[g][e] = make_float2(0.f, 0.f);
+    }
+    float m_run = -INFINITY, l_run = 0.f;  // head `warp`'s running softmax of this half (warps 0..3)
+    const bool hi4 = (lane & 4) != 0, hi2 = (lane & 2) != 0;
+    const int my_head = (hi4 ? 2 : 0) + (hi2 ? 1 : 0);
+    const int bar = 2 + hf;
+    int done = hf;  // next tile of this half
+    for (int i = hf; i < n; i += 2) {
+        const int sl = i % kAttRingSlots, t = T0 + i;
+        if (th == 0) {
+            uint64_t t0 = 0;
+            int ok = 1;
+            for (uint32_t it = 1; !mbar_try_wait(&bars[sl], parity(i)); ++it) {
+                if ((it & 63) == 0) {
+                    if (c.fl->abort) {
+                        ok = 0;
+                        break;
+                    }
+                    const uint64_t now = global_ns();
+                    if (t0 == 0) {
+                        t0 = now;
+                    } else if (now - t0 > p.wait_limit_ns) {
+                        fail(p, c.fl, kErrWaitTimeout, 60u + layer);
+                        ok = 0;
+                        break;
+                    }
+                }
+            }
+            sm.ok[hf] = ok;
+        }
+        named_barrier(bar, 128);
+        if (!sm.ok[hf]) break;
+        done = i + 2;
+        const int nt = min(kAttnTile, ctx - t * kAttnTile);
+        KV* kt = slot_k(sl);
+        KV* vt = slot_v(sl);
+        if (insert_new && pos >= t * kAttnTile && pos < t * kAttnTile + kAttnTile) {
+            // The copy brought the cache's old value at pos; the new token replaces it.
+            const int r = pos - t * kAttnTile;
+            if (th < kHd) {
+                kt[r * kHd + th] = sm.kn[th];
+                vt[r * kHd + th] = sm.vn[th];
+            }
+            named_barrier(bar, 128);
+        }
+#pragma unroll
+        for (int ps = 0; ps < 4; ++ps) {
+            const int j = ps * 16 + (th >> 3);
+            float sc[kGqa] = {0.f, 0.f, 0.f, 0.f};
+            if (j < nt) {
+                const uint4 u = *reinterpret_cast<const uint4*>(kt + j * kHd + 8 * c8);
+                const KV2* k2 = reinterpret_cast<const KV2*>(&u);
+#pragma unroll
+                for (int g = 0; g < kGqa; ++g) {
+                    float2 a = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) a = fma2(kv2_to_float2(k2[e]), q[g][e], a);
+                    sc[g] = a.x + a.y;
+                }
+            }
+            const float r0 = __shfl_xor_sync(0xffffffffu, hi4 ? sc[0] : sc[2], 4);
+            const float r1 = __shfl_xor_sync(0xffffffffu, hi4 ? sc[1] : sc[3], 4);
+            const float a0 = (hi4 ? sc[2] : sc[0]) + r0;
+            const float a1 = (hi4 ? sc[3] : sc[1]) + r1;
+            const float r2 = __shfl_xor_sync(0xffffffffu, hi2 ? a0 : a1, 2);
+            float cc = (hi2 ? a1 : a0) + r2;
+            cc += __shfl_xor_sync(0xffffffffu, cc, 1);
+            if ((lane & 1) == 0) sm.s[hf][j][my_head] = j < nt ? 0.125f * cc : -INFINITY;
+        }
+        named_barrier(bar, 128);
+        if (warp < kGqa) {
+            const float s0 = sm.s[hf][lane][warp], s1 = sm.s[hf][lane + 32][warp];
+            const float m_new = fmaxf(m_run, warp_max(fmaxf(s0, s1)));  // finite: the tile's first token is in the context
+            const float p0 = expf(s0 - m_new), p1 = expf(s1 - m_new);
+            sm.s[hf][lane][warp] = p0;
+            sm.s[hf][lane + 32][warp] = p1;
+            const float alpha = expf(m_run - m_new);
+            l_run = l_run * alpha + warp_sum(p0 + p1);
+            m_run = m_new;
+            if (lane == 0) sm.alpha[hf][warp] = alpha;
+        }
+        named_barrier(bar, 128);
+        {
+            const float4 al = *reinterpret_cast<const float4*>(sm.alpha[hf]);
+            const float alv[kGqa] = {al.x, al.y, al.z, al.w};
+#pragma unroll
+            for (int g = 0; g < kGqa; ++g) {
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[g][e] = make_float2(acc[g][e].x * alv[g], acc[g][e].y * alv[g]);
+            }
+            const int jg = th >> 3;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int j = jg + 16 * k;
+                if (j < nt) {
+                    const uint4 u = *reinterpret_cast<const uint4*>(vt + j * kHd + 8 * c8);
+                    const KV2* v2 = reinterpret_cast<const KV2*>(&u);
+                    const float4 p4 = *reinterpret_cast<const float4*>(&sm.s[hf][j][0]);
+                    const float pv[kGqa] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 vf = kv2_to_float2(v2[e]);
+#pragma unroll
+                        for (int g = 0; g < kGqa; ++g) acc[g][e] = fma2(make_float2(pv[g], pv[g]), vf, acc[g][e]);
+                    }
+                }
+            }
+        }
+        named_barrier(bar, 128);  // the slot and the score buffer are free again
+        if (th == 0 && i + kAttRingSlots < n) issue(i + kAttRingSlots);
+    }
+    if (done < n && th == 0) {
+        // This half gave up: the copies it issued or was due to consume land before it goes on (bounded).
+        for (int i = done; i < min(n, done + kAttRingSlots); i += 2) {  // issued, not consumed: done, done + 2
+            const uint64_t t0 = global_ns();
+            while (!mbar_try_wait(&bars[i % kAttRingSlots], parity(i)) && global_ns() - t0 < p.drain_limit_ns) {
+            }
+        }
+    }
+    // Sum this half's 16 token groups (red[jg][g][d] in the half's first slot, free now), keep (M, L).
+    float* red = reinterpret_cast<float*>(ring + hf * 2 * kTileBytes);
+    {
+        const int jg = th >> 3;
+#pragma unroll
+        for (int g = 0; g < kGqa; ++g) {
+            float4* dst = reinterpret_cast<float4*>(red + (jg * kGqa + g) * kHd + 8 * c8);
+            dst[0] = make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
+            dst[1] = make_float4(acc[g][2].x, acc[g][2].y, acc[g][3].x, acc[g][3].y);
+        }
+    }
+    if (warp < kGqa && lane == 0) {
+        sm.mh[hf][warp] = m_run;
+        sm.lh[hf][warp] = l_run;
+    }
+    csync();
+    {
+        const int g = tid >> 6, d = tid & 63;
+        const float* r0 = reinterpret_cast<const float*>(ring);
+        const float* r1 = reinterpret_cast<const float*>(ring + 2 * kTileBytes);
+        float o0 = 0.f, o1 = 0.f;
+#pragma unroll
+        for (int jg = 0; jg < 16; ++jg) {
+            o0 += r0[(jg * kGqa + g) * kHd + d];
+            o1 += r1[(jg * kGqa + g) * kHd + d];
+        }
+        const float M = fmaxf(sm.mh[0][g], sm.mh[1][g]);
+        const float e0 = expf(sm.mh[0][g] - M), e1 = expf(sm.mh[1][g] - M);  // 0 for a half without tiles
+        emit(h * kGqa + g, d, o0 * e0 + o1 * e1, M, sm.lh[0][g] * e0 + sm.lh[1][g] * e1);
+    }
+    fence_proxy_async_shared();  // this layer's writes to the slots precede the next layer's copies into them
+    csync();
+}
+
 // Merges the S partials of KV head h in range order and writes the 4 query heads' outputs. Threads 0..S-1
 // each acquire one range's flag (bounded polls); one barrier, which also agrees on an abort, then makes the
 // partials visible to every thread. The (M, L) pairs are staged in shared memory by one load per thread;
@@ -652,7 +926,7 @@ __device__ bool load_input(ConsumerCtx& c, const unsigned long long* src, uint32
 // Waits for, accumulates and releases the n_seg tiles of one row group (first global tile `t0`),
 // reduces the N stage rows across the warp and leaves row i's value in my[i]. Not inlined: one copy
 // per (type, N) serves every operation with that tile shape.
-template <WeightType WT, int N, int CPL>
+template <WeightType WT, int N, int CPL, int ST>
 __device__ __forceinline__ bool group_dot(const ConsumerCtx& c, int t0, int r0, const WOp& op, float* my) {
     const StepParams& p = *c.p;
     const TileGeom& g = op.g;
@@ -663,8 +937,8 @@ __device__ __forceinline__ bool group_dot(const ConsumerCtx& c, int t0, int r0, 
     for (int i = 0; i < N; ++i) acc[i] = 0.f;
     for (int sg = 0; sg < g.n_seg; ++sg) {
         const int t = t0 + sg;
-        const int s = t % kStages;
-        if (!wait_tile(p, &c.full[s], (t / kStages) & 1, c.fl, 3000u, &c.stage_tile[s], t)) return false;
+        const int s = t % ST;
+        if (!wait_tile(p, &c.full[s], (t / ST) & 1, c.fl, 3000u, &c.stage_tile[s], t)) return false;
         if (c.lane == 0 && sg == 0) trace_tile(p, t0, 2);
         tile_dot<WT, N, CPL>(c.ring + s * kStageBytes, tr, g.seg_bytes, sg * (g.seg_bytes / 16), c.xp, nc, c.xc, op.s, g.cols,
                              acc, c.lane);
@@ -685,7 +959,7 @@ __device__ __forceinline__ bool group_dot(const ConsumerCtx& c, int t0, int r0, 
 // Consumes this CTA's tiles of weight operation `o` (tile shape N x CPL) and applies the epilogue of
 // `kind` (runtime: one copy of the tile loop serves every operation with this shape). LM tracks the
 // best (value, index) per lane in bv/bi. Returns false if the CTA aborted.
-template <WeightType WT, int N, int CPL>
+template <WeightType WT, int N, int CPL, int ST>
 __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, int layer) {
     const StepParams& p = *c.p;
     const WOp op = weight_op(p, o);
@@ -705,7 +979,7 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
         const int r0 = lo + grp * R;
         const int nr = min(R, hi - r0);
         if (c.lane == 0) trace_tile(p, c.t_base + grp * g.n_seg, 1);
-        ok = group_dot<WT, N, CPL>(c, c.t_base + grp * g.n_seg, r0, op, my);
+        ok = group_dot<WT, N, CPL, ST>(c, c.t_base + grp * g.n_seg, r0, op, my);
         if (!ok) break;
         if (grp == 0 && c.lane == 0) trace_mark(p, trace_op_of_weight_op(o), 5);
         if (c.lane == 0) trace_tile(p, c.t_base + grp * g.n_seg, 3);
@@ -732,6 +1006,102 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
                     bi = r;
                 }
             }
+        }
+        __syncwarp();
+    }
+    if (!ok) c.fl->abort = 1;
+    c.t_base += kr.nt;
+    return !named_barrier_or(1, kCt, !ok || c.fl->abort != 0);
+}
+
+// The epilogue of one output row (value d; SwiGLU: gate d, up u) of operation kind `kind`, row r of an
+// operation whose CTA rows start at lo.
+__device__ __forceinline__ void row_epilogue(const ConsumerCtx& c, int kind, int layer, int r, int lo, float d, float u,
+                                             float& bv, int& bi) {
+    const StepParams& p = *c.p;
+    if (kind == kQkv) {
+        st_tagged(p.t_qkv + r, d, act_tag(p, layer, kTagQkv));
+    } else if (kind == kWo || kind == kDown) {
+        const float v = c.res[r - lo] + d;
+        c.res[r - lo] = v;
+        if (kind == kWo) {
+            st_tagged(p.t_xmid + r, v, act_tag(p, layer, kTagXmid));
+        } else {
+            st_tagged(p.t_xout + r, v, act_tag(p, layer, kTagXout));
+            if (p.debug_res) p.debug_res[static_cast<size_t>(layer + 1) * kH + r] = v;
+        }
+    } else if (kind == kGu) {
+        st_tagged(p.t_act + r, silu_f(d) * u, act_tag(p, layer, kTagAct));
+    } else {
+        __stcg(p.logits + r, d);
+        if (better(d, r, bv, bi)) {
+            bv = d;
+            bi = r;
+        }
+    }
+}
+
+// Consumes this CTA's stages of weight operation `o` when several warps share each stage
+// (StageShape<WT, SHAPE>::kWps > 1): warp group G = warp / kWps takes stages G, G + groups, ...; warp i of the
+// group computes rows i*kHalf .. of each half of the stage, the group agrees (one named barrier, which also
+// ORs a failed wait) and one thread releases the stage; then each warp applies the epilogue to its rows.
+template <WeightType WT, int SHAPE, int ST>
+__device__ bool run_tiles_shared(ConsumerCtx& c, int o, int kind, float& bv, int& bi, int layer) {
+    using SS = StageShape<WT, SHAPE>;
+    constexpr int kGroups = kCw / SS::kWps;
+    constexpr int kRw = SS::kHalf;
+    const StepParams& p = *c.p;
+    const WOp op = weight_op(p, o);
+    const TileGeom& g = op.g;
+    const KindRows kr = kind_table()[kind];
+    const int lo = kr.lo, hi = kr.hi;
+    const int R = g.rows_per_tile;  // rows per half of a stage
+    const int ng = (hi - lo + R - 1) / R;
+    float* my = c.scratch + c.cw * 32;
+    if (R * g.halves != SS::kRows || g.n_seg != 1 || g.seg_bytes != SS::kCpl * 512) {
+        if (c.tid == 0) fail(p, c.fl, kErrWaitTimeout, 4000u + o);  // geometry mismatch: never expected
+        csync();
+        return false;
+    }
+    const int grp0 = c.cw / SS::kWps, wi = c.cw % SS::kWps;
+    const int my0 = wi * kRw;  // this warp's first row (per half) within a stage
+    const int nc = g.cols / Chunk<WT>::kCols;
+    const int up_off = g.halves == 2 ? g.out_rows : 0, last = g.out_rows * g.halves - 1;
+    bool ok = true;
+    for (int grp = grp0; grp < ng; grp += kGroups) {
+        const int r0 = lo + grp * R;
+        const int nr = min(R, hi - r0);
+        const int t = c.t_base + grp;
+        const int s = t % ST;
+        if (c.lane == 0 && wi == 0) trace_tile(p, t, 1);
+        const TileRows tr{r0 + my0, kRw, up_off, last};
+        const bool got = wait_tile(p, &c.full[s], (t / ST) & 1, c.fl, 3000u, &c.stage_tile[s], t);
+        if (c.lane == 0 && wi == 0 && got) trace_tile(p, t, 2);
+        float acc[SS::kNw];
+#pragma unroll
+        for (int i = 0; i < SS::kNw; ++i) acc[i] = 0.f;
+        if (got) {
+            const uint8_t* st = c.ring + s * kStageBytes;
+            tile_dot<WT, SS::kNw, SS::kCpl, kRw>(st + my0 * g.seg_bytes, tr, g.seg_bytes, 0, c.xp, nc, c.xc, op.s, g.cols, acc,
+                                                  c.lane, st + (R + my0) * g.seg_bytes);
+        }
+        const bool failed = SS::kWps == kCw ? named_barrier_or(1, kCt, !got)
+                                            : named_barrier_or(2 + grp0, SS::kWps * 32, !got);
+        if (failed) {
+            ok = false;
+            break;
+        }
+        if (wi == 0 && c.lane == 0) mbar_arrive(&c.empty[s]);
+#pragma unroll
+        for (int i = 0; i < SS::kNw; ++i) {
+            const float v = warp_sum(acc[i]);
+            if (c.lane == 0) my[i] = finish_row<WT>(v, op.s, tr.global_row(i));
+        }
+        __syncwarp();
+        if (grp == 0 && c.lane == 0 && wi == 0) trace_mark(p, trace_op_of_weight_op(o), 5);
+        if (c.lane == 0 && wi == 0) trace_tile(p, t, 3);
+        if (c.lane < kRw && my0 + c.lane < nr) {
+            row_epilogue(c, kind, layer, r0 + my0 + c.lane, lo, my[c.lane], g.halves == 2 ? my[kRw + c.lane] : 0.f, bv, bi);
         }
         __syncwarp();
     }
@@ -862,22 +1232,15 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
                 const int n_slots = p.max_seq / kAttnTile;  // partial slots per query head (>= any S)
                 if (ar.head >= 0) {
                     const int h = ar.head, sp = ar.split;
-                    uint4 hk[4];  // cached keys of the range's first pass: independent of this step's projections
-                    if (ar.p0 * kHeadPassTokens + kHeadWarpTokens * c.cw < ctx) {
-                        head_load_keys<KV>(kc, p.max_seq, h, pos, ar.p0, c.cw, c.lane, hk);
-                    }
-                    HeadPassSmem<KV>& sm = *reinterpret_cast<HeadPassSmem<KV>*>(c.xp);
                     // The range that holds pos inserts the new token. Partials go to slot = range; after a
                     // barrier (all of the CTA's stores done) one release store of the step's tag publishes them.
-                    attend_head_span<KV>(
-                        qkv_src, kNh, kNkv, cs, kc, vc, p.max_seq, h, ctx, ar.p0, ar.p1, ar.p1 == ar.n_pass,
+                    attend_range_stream<KV>(
+                        c, l, h, 2 * ar.p0, min(n_tiles, 2 * ar.p1), ctx, ar.p1 == ar.n_pass, cs, kc, vc, qkv_src,
                         [&](int hq, int d, float O, float M, float L) {
                             const size_t slot = static_cast<size_t>(hq) * n_slots + sp;
                             __stcg(p.part_o + slot * kHd + d, O);
                             if (d == 0) __stcg(reinterpret_cast<float2*>(p.part_ml) + slot, make_float2(M, L));
-                        },
-                        sm, c.tid, hk, [] { csync(); });
-                    csync();
+                        });
                     if (c.tid == 0) st_release_gpu(p.sync + kSyncFlags + 32 * h + sp, act_tag(p, l, kTagPart));
                 } else if (ar.merge >= 0) {
                     combine_splits(c, ar.merge, ar.S, n_slots, act_tag(p, l, kTagPart), att_dst, 50u + l);
@@ -908,9 +1271,17 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
             stage_commit<WT>(v, sK, snorm, p.eps, c.xp, c.xc, c.red, c.tid, kCt, [] { csync(); });
         }
         if (c.tid == 0) trace_mark(p, top, 4);
-        const bool ok = kind == kDown ? run_tiles<WT, kNd, kCpld>(c, o, kind, bv, bi, l)
-                        : (kNg != kN && kind == kGu) ? run_tiles<WT, kNg, kCpl>(c, o, kind, bv, bi, l)
-                                                     : run_tiles<WT, kN, kCpl>(c, o, kind, bv, bi, l);
+        bool ok;
+        constexpr int ST = ring_stages<SPLIT>();
+        if constexpr (StageShape<WT, kQkv>::kWps > 1) {
+            ok = kind == kDown ? run_tiles_shared<WT, kDown, ST>(c, o, kind, bv, bi, l)
+                 : kind == kGu ? run_tiles_shared<WT, kGu, ST>(c, o, kind, bv, bi, l)
+                               : run_tiles_shared<WT, kQkv, ST>(c, o, kind, bv, bi, l);
+        } else {
+            ok = kind == kDown ? run_tiles<WT, kNd, kCpld, ST>(c, o, kind, bv, bi, l)
+                 : (kNg != kN && kind == kGu) ? run_tiles<WT, kNg, kCpl, ST>(c, o, kind, bv, bi, l)
+                                              : run_tiles<WT, kN, kCpl, ST>(c, o, kind, bv, bi, l);
+        }
         if (!ok) return;
         if (kind != kLm && c.tid == 0) trace_mark(p, top, 2);  // run_tiles ended with a block barrier
     }
@@ -985,10 +1356,13 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     volatile int* stage_tile = reinterpret_cast<volatile int*>(smem + kOffTiles);
     uint8_t* ring = smem + kOffRing;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
+        for (int s = 0; s < ring_stages<SPLIT>(); ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
             stage_tile[s] = -1;
+        }
+        if constexpr (SPLIT) {
+            for (int s = 0; s < kAttRingSlots; ++s) mbar_init(reinterpret_cast<uint64_t*>(smem + kOffAttBars) + s, 1);
         }
         fl->abort = 0;
         fl->ok = 0;
@@ -1001,7 +1375,7 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     if (threadIdx.x < 128) {
         asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kProducerRegs));
         if (threadIdx.x < 32) {
-            run_producer(p, ring, full, empty, stage_tile, fl);
+            run_producer<ring_stages<SPLIT>()>(p, ring, full, empty, stage_tile, fl);
         } else if (threadIdx.x >= 32 && threadIdx.x < 64 && p.prefetch_mode >= 2) {
             run_prefetcher(p, fl);
         }

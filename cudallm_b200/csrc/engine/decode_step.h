@@ -22,11 +22,12 @@
 
 namespace cudallm {
 
-// Most weight rows in one tile of the persistent kernel. A tile is one consumer warp's work; int4 tiles
-// stop at 2 rows (a 1 KiB tile of a 2048-column matrix), since dequantising 16 int4 rows (32k weights) per
-// warp leaves most consumer warps idle on the small operations while one warp works through its tile
-// (measured: 16 rows 1277 tok/s, 4 rows 1517, 2 rows 1562; int8 is fastest at the default 16).
-__host__ __device__ constexpr int decode_step_tile_rows(WeightType wt) { return wt == WeightType::INT4 ? 2 : kMaxTileRows; }
+// Most weight rows in one tile (one ring stage) of the persistent kernel. bf16 / int8 tiles are one consumer
+// warp's work. int4 stages are shared: a 16 KiB stage holds 16 rows of a 2048-column matrix and each of the
+// 8 consumer warps takes 2 of them (the down projection: 4 rows of 8192 columns, one per warp, two warp
+// groups alternating stages), so the ring keeps full 16 KiB stages in flight while every warp has work
+// even in the small operations.
+__host__ __device__ constexpr int decode_step_tile_rows(WeightType) { return kMaxTileRows; }
 
 struct StepLayer {
     const float* attn_norm;

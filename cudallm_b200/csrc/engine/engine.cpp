@@ -39,10 +39,8 @@ constexpr unsigned long long kDrainLimitNs = 1000000000ull;  // its final wait f
 // two forms on B200: ~384 tokens for bf16 / int8 weights, ~512 for int4 (whose step is shorter).
 constexpr int kWholeHeadMaxTiles = 6;
 constexpr int kWholeHeadMaxTilesInt4 = 8;
-// L2 prefetch distance of the persistent weight stream, in tiles: 24 tiles of 16 KiB for bf16 / int8; int4
-// tiles hold 2 rows, so the same byte distance is ~8x as many tiles.
+// L2 prefetch distance of the persistent weight stream, in tiles (ring stages of up to 16 KiB).
 constexpr int kPrefetchTiles = 24;
-constexpr int kPrefetchTilesInt4 = 192;
 constexpr int kTraceLmOp = 64;  // weight operation index of the lm_head
 
 int resolve_device(int requested) {
@@ -183,7 +181,7 @@ void Engine::make_step_params() {
     p.group_size = c.group_size;
     p.wait_limit_ns = kWaitLimitNs;
     p.drain_limit_ns = kDrainLimitNs;
-    p.prefetch_tiles = c.wtype == WeightType::INT4 ? kPrefetchTilesInt4 : kPrefetchTiles;
+    p.prefetch_tiles = kPrefetchTiles;
     p.prefetch_mode = 3;  // bulk L2 prefetches from the prefetch warp
     p.whole_head_max_tiles = c.wtype == WeightType::INT4 ? kWholeHeadMaxTilesInt4 : kWholeHeadMaxTiles;
     p.stall_op = -1;

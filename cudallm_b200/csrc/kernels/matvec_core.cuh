@@ -199,11 +199,15 @@ struct TileRows {
 __device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 __device__ __forceinline__ float2 add2(float2 a, float2 b) { return __fadd2_rn(a, b); }
 
-template <WeightType WT, int N, int CPL = 0>
+// Rows i < HALF are read from `stage` (row i at i * seg_bytes), rows i >= HALF from `stage_hi` (row i at
+// (i - HALF) * seg_bytes): a warp that takes some gate rows and the matching up rows of a shared SwiGLU
+// stage reads two blocks. With HALF == N (the default) stage_hi is unused.
+template <WeightType WT, int N, int CPL = 0, int HALF = N>
 __device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& tr, int seg_bytes, int seg_chunk0,
                                          const float* xp, int nc, const float* xc, const void* scales, int K,
-                                         float (&acc)[N], int lane) {
+                                         float (&acc)[N], int lane, const uint8_t* stage_hi = nullptr) {
     const float4* p4 = reinterpret_cast<const float4*>(xp);
+    auto row_at = [&](int i) { return i < HALF ? stage + i * seg_bytes : stage_hi + (i - HALF) * seg_bytes; };
     const int cpl = CPL > 0 ? CPL : (seg_bytes >> 9);  // chunks per lane per row
     if constexpr (CPL > 0) seg_bytes = CPL * 512;
     [[maybe_unused]] const int groups = K >> 7;
@@ -224,7 +228,7 @@ __device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& t
             }
 #pragma unroll
             for (int i = 0; i < N; ++i) {
-                const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                const uint4 w = *reinterpret_cast<const uint4*>(row_at(i) + c * 16);
                 const uint32_t words[4] = {w.x, w.y, w.z, w.w};
                 float2 pp = make_float2(0.f, 0.f);
 #pragma unroll
@@ -254,7 +258,7 @@ __device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& t
                 const float4 x0 = p4[gc], x1 = p4[nc + gc];
 #pragma unroll
                 for (int i = 0; i < N; ++i) {
-                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                    const uint4 w = *reinterpret_cast<const uint4*>(row_at(i) + c * 16);
                     a[i] = fma2(make_float2(bf16lo(w.x), bf16hi(w.x)), make_float2(x0.x, x0.y), a[i]);
                     a[i] = fma2(make_float2(bf16lo(w.y), bf16hi(w.y)), make_float2(x0.z, x0.w), a[i]);
                     a[i] = fma2(make_float2(bf16lo(w.z), bf16hi(w.z)), make_float2(x1.x, x1.y), a[i]);
@@ -265,7 +269,7 @@ __device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& t
                 const float2 bias = make_float2(-8388736.f, -8388736.f);
 #pragma unroll
                 for (int i = 0; i < N; ++i) {
-                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                    const uint4 w = *reinterpret_cast<const uint4*>(row_at(i) + c * 16);
                     const uint32_t b0 = w.x ^ 0x80808080u, b1 = w.y ^ 0x80808080u, b2 = w.z ^ 0x80808080u,
                                    b3 = w.w ^ 0x80808080u;
                     a[i] = fma2(add2(make_float2(i8raw(b0, 0x7540), i8raw(b0, 0x7541)), bias), make_float2(x0.x, x0.y), a[i]);
@@ -289,7 +293,7 @@ __device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& t
                 }
 #pragma unroll
                 for (int i = 0; i < N; ++i) {
-                    const uint4 w = *reinterpret_cast<const uint4*>(stage + i * seg_bytes + c * 16);
+                    const uint4 w = *reinterpret_cast<const uint4*>(row_at(i) + c * 16);
                     const float s = __half2float(__ldg(sc + static_cast<size_t>(tr.global_row(i)) * groups + g));
                     const uint32_t words[4] = {w.x, w.y, w.z, w.w};
                     float2 pp = make_float2(0.f, 0.f);

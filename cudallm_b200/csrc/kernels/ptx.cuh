@@ -16,6 +16,8 @@ __device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
 }
 
 // Makes barrier initialisation visible to the async (TMA) proxy and to the other threads.
+// Orders this thread's generic-proxy accesses to shared memory before later async-proxy (bulk copy) ones.
+__device__ __forceinline__ void fence_proxy_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void fence_barrier_init() {
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }

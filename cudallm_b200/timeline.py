@@ -1,8 +1,10 @@
 """Timeline of one persistent decode step, read from the kernel's own %globaltimer stamps.
 
     python -m cudallm_b200.timeline [--dtype bf16|int8|int4] [--kv bf16|fp16] [--prompt 32] [--tile-op N]
+                                    [--context N]
 
-Runs a seeded prompt through the engine, traces the next step (cudallm_debug_trace) and prints:
+Runs a seeded prompt through the engine (--context N: N seeded tokens through the chunked prefill, on a
+model file with room for 32896 positions), traces the next step (cudallm_debug_trace) and prints:
   * per operation (layers 0, 1, 15 and the lm_head): when the dependency wait begins and ends, when the
     operation ends (median and slowest CTA) and when the copy producer started streaming its weights;
   * per layer, averaged over the 16 layers: the critical duration of each operation (slowest CTA's end
@@ -29,15 +31,27 @@ def op_names() -> list[str]:
     return names + ["lm", "end"]
 
 
-def capture(dtype: str, kv: str, prompt: int, tile_op: int | None) -> tuple[np.ndarray, np.ndarray]:
+LONG_MAX_SEQ = 32896
+
+
+def capture(dtype: str, kv: str, prompt: int, tile_op: int | None,
+            context: int | None = None) -> tuple[np.ndarray, np.ndarray]:
     from . import synth
     from .engine import Engine
-    path, _ = synth.ensure_model(dtype)
-    with Engine(path, kv_dtype=kv) as eng:
+    if context is None:
+        path, _ = synth.ensure_model(dtype)
+        max_seq = 0  # the file's own
+    else:
+        path, _ = synth.ensure_model(dtype, seed=0, max_seq_len=LONG_MAX_SEQ)
+        max_seq = LONG_MAX_SEQ
+    with Engine(path, kv_dtype=kv, max_seq_len=max_seq) as eng:
         if tile_op is not None:
             eng.set_knob("trace_tile_op", tile_op)
-        for t in synth.prompt_ids(prompt):
-            eng.step_async(t)
+        if context is None:
+            for t in synth.prompt_ids(prompt):
+                eng.step_async(t)
+        else:
+            eng.prefill(synth.prompt_ids(context, seed=1))
         for _ in range(4):
             eng.step_async(None)
         eng.synchronize()
@@ -107,8 +121,11 @@ def main(argv: list[str] | None = None) -> int:
     ap.add_argument("--kv", choices=("bf16", "fp16"), default="bf16")
     ap.add_argument("--prompt", type=int, default=32)
     ap.add_argument("--tile-op", type=int, default=None)
+    ap.add_argument("--context", type=int, default=None, help="cached tokens before the traced step (<= 32880)")
     args = ap.parse_args(argv)
-    tr, tt = capture(args.dtype, args.kv, args.prompt, args.tile_op)
+    if args.context is not None and not 1 <= args.context <= LONG_MAX_SEQ - 16:
+        ap.error(f"--context must be in [1, {LONG_MAX_SEQ - 16}]")
+    tr, tt = capture(args.dtype, args.kv, args.prompt, args.tile_op, args.context)
     report(tr, tt, 64 if args.tile_op is None else args.tile_op)
     return 0
 
