@@ -87,16 +87,23 @@ template <WeightType WT>
 constexpr int weight_row_bytes(int k) {
     return WT == WeightType::BF16 ? 2 * k : (WT == WeightType::INT8 ? k : k / 2);
 }
-// Chunks per lane of one row segment (the whole row: every Llama operation has n_seg == 1).
+// Bytes of one tile's row segment: the whole row, except the down projection (K = 8192), whose rows are
+// cut into kDownSegBytes segments (n_seg > 1 for bf16 and int8).
+template <WeightType WT, int KIND>
+constexpr int seg_bytes_of() {
+    constexpr int rb = weight_row_bytes<WT>(KIND == 3 ? 4 * 2048 : 2048);
+    return KIND == 3 && rb > kDownSegBytes ? kDownSegBytes : rb;
+}
+// Chunks per lane of one row segment.
 template <WeightType WT, int KIND>
 constexpr int seg_chunks_per_lane() {
-    return weight_row_bytes<WT>(KIND == 3 ? 4 * 2048 : 2048) / 512;
+    return seg_bytes_of<WT, KIND>() / 512;
 }
 
 template <WeightType WT, int KIND>
 constexpr int stage_rows() {
     constexpr int halves = KIND == 2 ? 2 : 1;  // gate/up
-    constexpr int rb = weight_row_bytes<WT>(KIND == 3 ? 4 * 2048 : 2048);  // down has K = 8192
+    constexpr int rb = seg_bytes_of<WT, KIND>();
     constexpr int fit = kStageBytes / halves / rb;
     constexpr int cap = decode_step_tile_rows(WT);
     return (fit < cap ? fit : cap) * halves;
@@ -106,11 +113,13 @@ constexpr int stage_rows() {
 // gate/up operation), kWps warps per stage (1: one warp consumes a whole stage; >1: the stage's rows are
 // split over kWps warps and kCw / kWps warp groups take stages in turn), kNw rows per warp, kHalf of them
 // per half, kCpl 16-byte chunks per lane of a row. int4 shares stages; bf16 and int8 do not.
+// int4 warps per stage by operation kind (qkv, o-proj, gate/up, down, lm_head).
+constexpr int kInt4WarpsPerStage[5] = {8, 8, 4, 4, 4};
 template <WeightType WT, int KIND>
 struct StageShape {
     static constexpr int kHalves = KIND == 2 ? 2 : 1;
     static constexpr int kRows = stage_rows<WT, KIND>();
-    static constexpr int kWps = WT == WeightType::INT4 ? (KIND == 3 ? 4 : 8) : 1;
+    static constexpr int kWps = WT == WeightType::INT4 ? kInt4WarpsPerStage[KIND] : 1;
     static constexpr int kNw = kRows / kWps;
     static constexpr int kHalf = kNw / kHalves;
     static constexpr int kCpl = seg_chunks_per_lane<WT, KIND>();
@@ -122,6 +131,25 @@ struct WOp {
     const void* s;
     TileGeom g;
 };
+
+// L1 prefetch of the scales of rows [r, r + n) of a quantised operation (int8: one fp32 per row; int4: one
+// fp16 per 128 columns), lines i, i + step, ...: every line lies within the rows' bytes (the first one
+// starts at or before them, inside the same weight arena). Nothing for bf16.
+template <WeightType WT>
+__device__ __forceinline__ void prefetch_scale_rows(const void* scales, int cols, int r, int n, int i, int step) {
+    if constexpr (WT != WeightType::BF16) {
+        const size_t row_bytes = WT == WeightType::INT8 ? 4 : static_cast<size_t>(cols / 128) * 2;
+        const uintptr_t a = reinterpret_cast<uintptr_t>(scales) + static_cast<size_t>(r) * row_bytes;
+        const uintptr_t b = a + static_cast<size_t>(n) * row_bytes;
+        for (uintptr_t line = (a & ~static_cast<uintptr_t>(127)) + static_cast<uintptr_t>(i) * 128; line < b;
+             line += static_cast<uintptr_t>(step) * 128) {
+            prefetch_l1(reinterpret_cast<const void*>(line));
+        }
+    }
+}
+// Rows of scales an operation prefetches before its input wait; past them the tile loop prefetches the
+// rows of the tile this many rows ahead (only the lm_head has more).
+constexpr int kScaleAheadRows = 256;
 
 __device__ __forceinline__ WOp weight_op(const StepParams& p, int o) {
     if (o == kWeightOps - 1) return {static_cast<const uint8_t*>(p.emb_w), p.emb_s, p.g_lm};
@@ -359,18 +387,26 @@ __device__ void run_prefetcher(const StepParams& p, volatile Flags* fl) {
             __nanosleep(128);
         }
         t0 = 0;
-        // Whole-row tiles (every operation of the step): rows r0 .. r0+nr-1 of each half are contiguous.
+        // Tile i of the operation: row group i / n_seg, segment i % n_seg. Whole-row tiles (n_seg == 1) are
+        // one contiguous range per half; segmented tiles one range per row.
         const WOp op = weight_op(p, pf.o);
-        const int r0 = pf.lo + pf.i * op.g.rows_per_tile;
-        const int bytes = min(op.g.rows_per_tile, pf.hi - r0) * op.g.row_bytes;
-        for (int h = 0; h < op.g.halves; ++h) {
-            const size_t row = static_cast<size_t>(r0) + static_cast<size_t>(h) * op.g.out_rows;
-            const uint8_t* a = op.w + row * op.g.row_bytes;
+        const TileGeom& g = op.g;
+        const int grp = pf.i / g.n_seg, sg = pf.i % g.n_seg;
+        const int r0 = pf.lo + grp * g.rows_per_tile;
+        const int nr = min(g.rows_per_tile, pf.hi - r0);
+        for (int h = 0; h < g.halves; ++h) {
+            const size_t row = static_cast<size_t>(r0) + static_cast<size_t>(h) * g.out_rows;
+            const uint8_t* a = op.w + row * g.row_bytes + static_cast<size_t>(sg) * g.seg_bytes;
+            const int pieces = g.n_seg == 1 ? 1 : nr;
+            const int bytes = g.n_seg == 1 ? nr * g.row_bytes : g.seg_bytes;
             if (p.prefetch_mode == 3) {
-                if (lane == 0) bulk_prefetch_l2(a, static_cast<uint32_t>(bytes));  // one request per half (bulk engine)
+                // one bulk request per contiguous range (bulk engine)
+                if (lane < pieces) bulk_prefetch_l2(a + static_cast<size_t>(lane) * g.row_bytes, static_cast<uint32_t>(bytes));
             } else {
-                for (int off = lane * 128; off < bytes; off += 32 * 128) {
-                    asm volatile("prefetch.global.L2 [%0];" ::"l"(a + off) : "memory");
+                for (int q = 0; q < pieces; ++q) {
+                    for (int off = lane * 128; off < bytes; off += 32 * 128) {
+                        asm volatile("prefetch.global.L2 [%0];" ::"l"(a + static_cast<size_t>(q) * g.row_bytes + off) : "memory");
+                    }
                 }
             }
         }
@@ -456,7 +492,8 @@ struct ConsumerCtx {
     float* scratch;
     float* res;  // [kMaxResRows] this CTA's residual rows
     int tid, cw, lane;
-    int t_base;  // global tile index of the current operation's first tile
+    int t_base;      // global tile index of the current operation's first tile
+    float in_scale;  // factor of the current operation's outputs: 1/rms of its input when RMS-normalised, else 1
 };
 
 __device__ __forceinline__ void csync() { named_barrier(1, kCt); }
@@ -948,7 +985,7 @@ __device__ __forceinline__ bool group_dot(const ConsumerCtx& c, int t0, int r0, 
 #pragma unroll
     for (int i = 0; i < N; ++i) {
         const float v = warp_sum(acc[i]);
-        if (c.lane == 0) my[i] = finish_row<WT>(v, op.s, tr.global_row(i));
+        if (c.lane == 0) my[i] = finish_row<WT>(v, op.s, tr.global_row(i)) * c.in_scale;
     }
     __syncwarp();
     return true;
@@ -969,7 +1006,7 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
     const int R = g.rows_per_tile;
     const int ng = (hi - lo + R - 1) / R;
     float* my = c.scratch + c.cw * 32;
-    if (R * g.halves != N || g.n_seg != 1 || g.seg_bytes != CPL * 512) {
+    if (R * g.halves != N || g.n_seg * g.seg_bytes != g.row_bytes || g.seg_bytes != CPL * 512) {
         if (c.tid == 0) fail(p, c.fl, kErrWaitTimeout, 4000u + o);  // geometry mismatch: never expected
         csync();
         return false;
@@ -979,6 +1016,9 @@ __device__ bool run_tiles(ConsumerCtx& c, int o, int kind, float& bv, int& bi, i
         const int r0 = lo + grp * R;
         const int nr = min(R, hi - r0);
         if (c.lane == 0) trace_tile(p, c.t_base + grp * g.n_seg, 1);
+        if (r0 + kScaleAheadRows < hi) {
+            prefetch_scale_rows<WT>(op.s, g.cols, r0 + kScaleAheadRows, min(R, hi - r0 - kScaleAheadRows), c.lane, 32);
+        }
         ok = group_dot<WT, N, CPL, ST>(c, c.t_base + grp * g.n_seg, r0, op, my);
         if (!ok) break;
         if (grp == 0 && c.lane == 0) trace_mark(p, trace_op_of_weight_op(o), 5);
@@ -1075,6 +1115,9 @@ __device__ bool run_tiles_shared(ConsumerCtx& c, int o, int kind, float& bv, int
         const int s = t % ST;
         if (c.lane == 0 && wi == 0) trace_tile(p, t, 1);
         const TileRows tr{r0 + my0, kRw, up_off, last};
+        if (wi == 0 && r0 + kScaleAheadRows < hi) {
+            prefetch_scale_rows<WT>(op.s, g.cols, r0 + kScaleAheadRows, min(R, hi - r0 - kScaleAheadRows), c.lane, 32);
+        }
         const bool got = wait_tile(p, &c.full[s], (t / ST) & 1, c.fl, 3000u, &c.stage_tile[s], t);
         if (c.lane == 0 && wi == 0 && got) trace_tile(p, t, 2);
         float acc[SS::kNw];
@@ -1095,7 +1138,7 @@ __device__ bool run_tiles_shared(ConsumerCtx& c, int o, int kind, float& bv, int
 #pragma unroll
         for (int i = 0; i < SS::kNw; ++i) {
             const float v = warp_sum(acc[i]);
-            if (c.lane == 0) my[i] = finish_row<WT>(v, op.s, tr.global_row(i));
+            if (c.lane == 0) my[i] = finish_row<WT>(v, op.s, tr.global_row(i)) * c.in_scale;
         }
         __syncwarp();
         if (grp == 0 && c.lane == 0 && wi == 0) trace_mark(p, trace_op_of_weight_op(o), 5);
@@ -1125,6 +1168,61 @@ __device__ __forceinline__ void prefetch_split_kv(const ConsumerCtx& c, size_t l
         const uint8_t* base = static_cast<const uint8_t*>((q & 1) ? p.v_cache : p.k_cache);
         bulk_prefetch_l2(base + layer_bytes + off, static_cast<uint32_t>(n * kHd * sizeof(KV)));
     }
+}
+
+// Stages an operation's input vector into the planes of c.xp (int4: and the chunk sums into c.xc) with the
+// RMSNorm's 1/rms deferred: the planes hold x * gain, and the returned factor (1/rms, or 1 without a norm)
+// scales each output row after its dot product (the projection is linear). So the sum of squares needs no
+// barrier of its own: each warp leaves its partial in c.red before the barrier that publishes the planes,
+// and every thread then adds the kCw partials in warp order. A norm is over K == kH columns, whose gain
+// (kGainPre float4s per thread) the caller loaded before it waited for v.
+static_assert(kGainPre * 4 * kCt == kH, "the gain of a norm is kGainPre float4s per consumer thread");
+template <WeightType WT>
+__device__ __forceinline__ float stage_input(ConsumerCtx& c, float4 (&v)[kStagePer], int K, const float* norm_w,
+                                             const float4 (&gain)[kGainPre], float eps) {
+    constexpr int C = Chunk<WT>::kCols;
+    const int nc = K / C, n4 = K / 4;
+    if (norm_w != nullptr) {
+        float ss = 0.f;
+#pragma unroll
+        for (int i = 0; i < kGainPre; ++i) {
+            ss = fmaf(v[i].x, v[i].x, ss);
+            ss = fmaf(v[i].y, v[i].y, ss);
+            ss = fmaf(v[i].z, v[i].z, ss);
+            ss = fmaf(v[i].w, v[i].w, ss);
+            v[i] = make_float4(v[i].x * gain[i].x, v[i].y * gain[i].y, v[i].z * gain[i].z, v[i].w * gain[i].w);
+        }
+        ss = warp_sum(ss);
+        if (c.lane == 0) c.red[c.cw] = ss;
+    }
+    float4* p4 = reinterpret_cast<float4*>(c.xp);
+#pragma unroll
+    for (int i = 0; i < kStagePer; ++i) {
+        const int q = c.tid + i * kCt;
+        if (q >= n4) continue;
+        const int ch = (4 * q) / C, i0 = (4 * q) % C;
+        p4[(i0 >> 2) * nc + ch] = v[i];
+    }
+    csync();
+    if constexpr (WT == WeightType::INT4) {
+        for (int ch = c.tid; ch < nc; ch += kCt) {
+            // Per word k: the even columns 8k, 8k+2, 8k+4, 8k+6, then the odd ones.
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 a = p4[(2 * k) * nc + ch], b = p4[(2 * k + 1) * nc + ch];
+                s += a.x + a.z + b.x + b.z;
+                s += a.y + a.w + b.y + b.w;
+            }
+            c.xc[ch] = s;
+        }
+        csync();
+    }
+    if (norm_w == nullptr) return 1.f;
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCw; ++w) t += c.red[w];
+    return rsqrtf(t / static_cast<float>(K) + eps);
 }
 
 template <WeightType WT, typename KV, bool SPLIT>
@@ -1263,12 +1361,29 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
             tag = act_tag(p, kStepLayers - 1, kTagXout);
             snorm = p.final_norm;
         }
+        // Neither depends on the input, so they are issued before its wait: the RMSNorm gain (into
+        // registers) and the first scale rows of this CTA's tiles (into L1).
+        float4 gain[kGainPre];
+        if (snorm != nullptr) {
+#pragma unroll
+            for (int i = 0; i < kGainPre; ++i) {
+                const int q = c.tid + i * kCt;
+                if (q < sK / 4) gain[i] = __ldg(reinterpret_cast<const float4*>(snorm) + q);
+            }
+        }
+        if constexpr (WT != WeightType::BF16) {
+            const WOp op = weight_op(p, o);
+            const KindRows kr = kind_table()[kind];
+            const int n = min(kr.hi - kr.lo, kScaleAheadRows);
+            prefetch_scale_rows<WT>(op.s, op.g.cols, kr.lo, n, c.tid, kCt);
+            if (op.g.halves == 2) prefetch_scale_rows<WT>(op.s, op.g.cols, kr.lo + op.g.out_rows, n, c.tid, kCt);
+        }
         if (c.tid == 0) trace_mark(p, top, 0);
         if (o == p.stall_op && tsrc != nullptr) tag ^= 1u << 7;  // bit 7 is in no tag a writer produces
         {
             float4 v[kStagePer];
             if (!load_input<WT>(c, tsrc, tag, sK, tok, 10u + o, top, v)) return;
-            stage_commit<WT>(v, sK, snorm, p.eps, c.xp, c.xc, c.red, c.tid, kCt, [] { csync(); });
+            c.in_scale = stage_input<WT>(c, v, sK, snorm, gain, p.eps);
         }
         if (c.tid == 0) trace_mark(p, top, 4);
         bool ok;
@@ -1276,6 +1391,7 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
         if constexpr (StageShape<WT, kQkv>::kWps > 1) {
             ok = kind == kDown ? run_tiles_shared<WT, kDown, ST>(c, o, kind, bv, bi, l)
                  : kind == kGu ? run_tiles_shared<WT, kGu, ST>(c, o, kind, bv, bi, l)
+                 : kind == kLm ? run_tiles_shared<WT, kLm, ST>(c, o, kind, bv, bi, l)
                                : run_tiles_shared<WT, kQkv, ST>(c, o, kind, bv, bi, l);
         } else {
             ok = kind == kDown ? run_tiles<WT, kNd, kCpld, ST>(c, o, kind, bv, bi, l)

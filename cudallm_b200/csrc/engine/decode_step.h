@@ -28,6 +28,11 @@ namespace cudallm {
 // groups alternating stages), so the ring keeps full 16 KiB stages in flight while every warp has work
 // even in the small operations.
 __host__ __device__ constexpr int decode_step_tile_rows(WeightType) { return kMaxTileRows; }
+// Longest row segment of the down projection's tiles (K = 8192). At 16 KiB every type keeps whole rows
+// (bf16: 1 row per stage, int8: 2, int4: 4). Shorter segments (more rows per stage, each input column read
+// from shared memory serving more rows) were measured slower: a warp then walks a row group's segments in
+// sequence and fewer warps share the operation.
+constexpr int kDownSegBytes = 16384;
 
 struct StepLayer {
     const float* attn_norm;

@@ -192,7 +192,7 @@ void Engine::make_step_params() {
     p.g_qkv = make_tile_geom(c.wtype, Epilogue::STORE, qkv_rows, c.hidden, rows);
     p.g_wo = make_tile_geom(c.wtype, Epilogue::ADD, c.hidden, c.hidden, rows);
     p.g_gu = make_tile_geom(c.wtype, Epilogue::SWIGLU, 2 * c.inter, c.hidden, rows);
-    p.g_down = make_tile_geom(c.wtype, Epilogue::ADD, c.hidden, c.inter, rows);
+    p.g_down = make_tile_geom(c.wtype, Epilogue::ADD, c.hidden, c.inter, rows, kDownSegBytes);
     p.g_lm = make_tile_geom(c.wtype, Epilogue::STORE, c.vocab, c.hidden, rows);
     set_knob("trace_tile_op", kTraceLmOp);
 }

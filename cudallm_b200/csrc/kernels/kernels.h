@@ -46,7 +46,9 @@ struct TileGeom {
     int rows_per_tile;
     int halves;     // 2 for SWIGLU (gate rows then up rows in one stage), else 1
 };
-TileGeom make_tile_geom(WeightType wt, Epilogue ep, int rows, int cols, int rpb);
+// seg_cap > 0 caps the row segment of a tile at that many bytes (a multiple of 512), so that a tile holds
+// more rows of a long row.
+TileGeom make_tile_geom(WeightType wt, Epilogue ep, int rows, int cols, int rpb, int seg_cap = 0);
 
 int num_sms();
 int default_rpb(WeightType w);

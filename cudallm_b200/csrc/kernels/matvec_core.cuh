@@ -77,10 +77,14 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.f + expf(-g)); 
 // `sync()` is a barrier over those threads; `red` is 32 floats of scratch.
 constexpr int kMaxStageK = 8192;
 constexpr int kStagePer = kMaxStageK / 4 / 256;  // float4 per thread at the largest K
-// Second half of stage_vector: v[i] holds columns 4q..4q+3 for q = tid + i * nthr (q < K/4).
+// Gain float4s per thread a caller may load ahead of time (gain_pre): all of them at K = 2048, 256 threads.
+constexpr int kGainPre = 2;
+// Second half of stage_vector: v[i] holds columns 4q..4q+3 for q = tid + i * nthr (q < K/4). gain_pre, if
+// given, holds the first kGainPre gain float4s of this thread (the same indices), loaded by the caller.
 template <WeightType WT, typename Sync>
 __device__ __forceinline__ void stage_commit(float4 (&v)[kStagePer], int K, const float* __restrict__ norm_w, float eps,
-                                             float* xp, float* xc, float* red, int tid, int nthr, Sync sync) {
+                                             float* xp, float* xc, float* red, int tid, int nthr, Sync sync,
+                                             const float4* gain_pre = nullptr) {
     constexpr int C = Chunk<WT>::kCols;
     constexpr int kMaxPer = kStagePer;
     const int nc = K / C;
@@ -100,7 +104,7 @@ __device__ __forceinline__ void stage_commit(float4 (&v)[kStagePer], int K, cons
 #pragma unroll
         for (int i = 0; i < kMaxPer; ++i) {
             const int q = tid + i * nthr;
-            if (q < n4) g[i] = __ldg(reinterpret_cast<const float4*>(norm_w) + q);
+            if (q < n4) g[i] = (gain_pre != nullptr && i < kGainPre) ? gain_pre[i] : __ldg(reinterpret_cast<const float4*>(norm_w) + q);
         }
         ss = warp_sum(ss);
         if ((tid & 31) == 0) red[tid >> 5] = ss;

@@ -276,13 +276,14 @@ int num_sms() {
 
 int default_rpb(WeightType) { return kMaxTileRows; }
 
-TileGeom make_tile_geom(WeightType wt, Epilogue ep, int rows, int cols, int rpb) {
+TileGeom make_tile_geom(WeightType wt, Epilogue ep, int rows, int cols, int rpb, int seg_cap) {
     TileGeom g{};
     g.halves = ep == Epilogue::SWIGLU ? 2 : 1;
     g.out_rows = rows / g.halves;
     g.cols = cols;
     g.row_bytes = static_cast<int>(row_bytes(wt, static_cast<uint64_t>(cols)));
-    const int limit = kStageBytes / g.halves;
+    const int stage_limit = kStageBytes / g.halves;
+    const int limit = seg_cap > 0 ? std::min(seg_cap, stage_limit) : stage_limit;
     int seg = g.row_bytes;
     if (seg > limit) {
         const int units = g.row_bytes / 512;
@@ -295,7 +296,7 @@ TileGeom make_tile_geom(WeightType wt, Epilogue ep, int rows, int cols, int rpb)
     g.seg_bytes = seg;
     g.n_seg = g.row_bytes / seg;
     const int cap = rpb > 0 ? std::min(rpb, kMaxTileRows) : kMaxTileRows;
-    g.rows_per_tile = std::max(1, std::min(cap, limit / seg));
+    g.rows_per_tile = std::max(1, std::min(cap, stage_limit / seg));
     return g;
 }
 

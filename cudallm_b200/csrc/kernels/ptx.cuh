@@ -72,6 +72,9 @@ __device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t b
         : "memory");
 }
 
+// Prefetch of the 128-byte line holding `p` into L1 (fire and forget; a later ld.global.nc hits it).
+__device__ __forceinline__ void prefetch_l1(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+
 // Bulk prefetch of global memory into L2 (fire and forget). src 16-B aligned, bytes a multiple of 16.
 __device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
     asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
