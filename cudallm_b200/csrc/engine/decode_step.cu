@@ -30,15 +30,16 @@ constexpr int kProducerRegs = 88;
 constexpr int kConsumerRegs = 208;
 static_assert(kProducerRegs * 128 + kConsumerRegs * kCt == kLaunchRegs * kThreads, "register split must use the launch pool");
 // Weight ring: kStages stages of 16 KiB in the short-context kernel; the split-attention kernel keeps
-// kSplitStages of them and gives the rest to its K/V tile ring (kAttRingSlots slots of one 64-token K tile +
-// V tile each). Barrier and tile-word arrays are laid out for kStages.
+// kStages - kAttSlots of them and gives the rest to its K/V tile ring (one 64-token K tile + V tile,
+// 16 KiB, per slot). Barrier and tile-word arrays are laid out for kStages.
 constexpr int kStages = 12;
-constexpr int kSplitStages = 8;
-constexpr int kAttRingSlots = 4;
+constexpr int kAttSlots = 4;
+// The split attention's tiles are not prefetched into L2: at 16K-32K tokens every prefetch distance
+// tried (the whole range at the layer's start, or 4-32 tiles ahead of the copies) measured slower.
 static_assert(kStages <= 32, "one producer lane per stage");
 template <bool SPLIT>
 constexpr int ring_stages() {
-    return SPLIT ? kSplitStages : kStages;
+    return SPLIT ? kStages - kAttSlots : kStages;
 }
 constexpr int kMaxK = 8192;
 constexpr int kOpsPerLayer = 4;
@@ -59,8 +60,13 @@ constexpr int kOffBars = 0;
 constexpr int kOffTiles = 2 * kStages * 8;  // int per stage: tile the producer last issued into it
 constexpr int kOffFlags = 256;
 constexpr int kOffKinds = 288;  // KindRows[5]: this CTA's rows of each operation kind
-constexpr int kOffRed = 384;
+constexpr int kOffAttFull = 352;  // split kernel: kAttSlots mbarriers of the K/V tile ring (room for 8)
+constexpr int kOffRed = 416;      // kCw floats: one partial sum of squares per consumer warp
+constexpr int kOffAttCnt = 448;   // split kernel: kAttSlots arrival counters, then kAttSlots pending words
 constexpr int kOffCs = 512;
+static_assert(kOffAttFull + kAttSlots * 8 <= kOffRed && kOffRed + 4 * kCw <= kOffAttCnt &&
+                  kOffAttCnt + 2 * kAttSlots * 4 <= kOffCs,
+              "attention ring words overflow");
 constexpr int kOffScratch = 768;
 constexpr int kOffAm = kOffScratch + kCw * 32 * 4;  // 1792
 // The residual rows this CTA owns (the same row range in the O and down projections), kept on chip for
@@ -72,9 +78,6 @@ constexpr int kOffXp = 3072;
 constexpr int kOffRing = kOffXp + kMaxK * 4;  // 35840
 constexpr int kSmemBytes = kOffRing + kStages * kStageBytes;
 static_assert(kOffTiles + kStages * 4 <= kOffFlags, "barriers overflow");
-constexpr int kOffAttBars = 352;  // kAttRingSlots mbarriers of the split kernel's K/V ring
-static_assert(kOffAttBars % 8 == 0 && kOffAttBars + kAttRingSlots * 8 <= kOffRed, "attention barriers overflow");
-static_assert((kStages - kSplitStages) * kStageBytes >= kAttRingSlots * 2 * kAttnTile * 64 * 2, "K/V ring must fit");
 static_assert(kOffAm + kCw * 8 <= kOffRes && kOffRes + kMaxResRows * 4 <= kOffXc, "argmax / residual scratch overflow");
 static_assert(kOffXc + (kMaxK / 32) * 4 <= kOffXp, "chunk sums overflow");
 static_assert(sizeof(AttSmem<__half>) <= kMaxK * 4, "attention scratch must fit in the vector area");
@@ -251,7 +254,7 @@ __device__ __forceinline__ uint8_t* smem_base() {
 struct KindRows {
     int lo, hi, nt;
 };
-static_assert(kOffKinds + 5 * sizeof(KindRows) <= kOffAttBars, "kind table overflow");
+static_assert(kOffKinds + 5 * sizeof(KindRows) <= kOffAttFull, "kind table overflow");
 __device__ __forceinline__ KindRows kind_rows(const TileGeom& g) {
     KindRows r;
     split_rows(g.out_rows, r.lo, r.hi);
@@ -616,63 +619,124 @@ __device__ __forceinline__ AttnRole attn_role(const StepParams& p, int ctx) {
     return r;
 }
 
-// ---- Range attention of the split kernel: K/V tiles through a ring of bulk copies -------------------
-// One CTA computes the 4 query heads of KV head h over the 64-token tiles [T0, T1) of the context. Its two
-// warp halves take alternate tiles (half f: tiles T0 + f, T0 + f + 2, ...); each tile's K and V rows
-// (8 KiB each, contiguous in the cache) arrive in one of kAttRingSlots shared-memory slots by bulk copies
-// completing on the slot's mbarrier, so up to four tiles (64 KiB) stream while one per half is computed.
-// Per tile and half (128 threads, the layout of the batched streaming attention): thread (token j, dims
-// 8c..8c+7) forms partial dots for the 4 heads, a butterfly over the token's 8 lanes completes them; warp g
-// advances head g's running (max, sum); p.V by token groups with per-head rescaling. The halves' states are
-// merged at the end and handed to emit(hq, d, O, M, L). The range that holds pos rotates the new key,
-// rounds k and v to the cache type, writes them to the cache and patches them into its last tile. Every
-// wait is bounded; a CTA that gives up lets its issued copies land before it goes on.
+// ---- Range attention of the split kernel --------------------------------------------------------------
+// One CTA computes the 4 query heads of KV head h over the 64-token tiles [T0, T1) of the context. Each
+// tile's K and V rows (8 KiB each, contiguous in the cache) arrive by bulk copies in one of kAttSlots
+// shared-memory slots, completing on the slot's mbarrier; the copies of the first tiles are issued before
+// the step's q is waited for. Warp w takes tokens 8w .. 8w + 7 of every tile: it copies its rows into
+// registers, releases the slot (the last of the 8 warps to do so issues the copy of the tile kAttSlots
+// ahead into it) and then computes, so no block barrier separates the tiles. Lane l works on token l / 4
+// of the group: its 16-dimension quarter (l % 4) of the key for the 4 heads' scores, completed over the
+// token's 4 lanes by two exchange steps that leave lane l with head hl = 2 (l & 1) + ((l >> 1) & 1); and
+// output dimensions 2l, 2l + 1 of the 4 heads for p.V, the group's probabilities passing through a
+// per-warp shared-memory slot. Each warp keeps its own running softmax; the warps' states are merged in
+// warp order at the end and handed to emit(hq, d, O, M, L). The range that holds pos rotates the new key,
+// rounds k and v to the cache type, writes them to the cache and uses the rounded values for token pos.
+// Every wait is bounded; after a wait gives up, every issued copy lands before the CTA goes on.
 template <typename KV>
 struct RangeAttnSmem {
     float qs[kGqa][kHd];
     alignas(16) KV kn[kHd];
     alignas(16) KV vn[kHd];
-    float s[2][kAttnTile][kGqa];  // per half: scores, then probabilities, of the tile
-    float alpha[2][kGqa];
-    float mh[2][kGqa], lh[2][kGqa];
-    int ok[2];
+    alignas(16) float pw[kCw][8][kGqa];  // per warp: the current group's probabilities [token][head]
+    alignas(16) float aw[kCw][kGqa];     // per warp: the group's rescale factors per head
+    float wo[kCw][kGqa][kHd];
+    float wm[kCw][kGqa], wl[kCw][kGqa];
 };
 static_assert(sizeof(RangeAttnSmem<__half>) <= kMaxK * 4, "range attention scratch must fit in the vector area");
 
-template <typename KV, typename Src, typename Emit>
-__device__ void attend_range_stream(const ConsumerCtx& c, int layer, int h, int T0, int T1, int ctx, bool insert_new,
-                                    const float* cs, KV* k_cache, KV* v_cache, Src qkv, Emit emit) {
-    using KV2 = typename Kv2<KV>::T;
-    constexpr int kTileBytes = kAttnTile * kHd * static_cast<int>(sizeof(KV));
-    const StepParams& p = *c.p;
-    const int pos = ctx - 1;
-    const int tid = c.tid, hf = tid >> 7, th = tid & 127, warp = th >> 5, lane = c.lane, c8 = th & 7;
-    RangeAttnSmem<KV>& sm = *reinterpret_cast<RangeAttnSmem<KV>*>(c.xp);
-    uint8_t* ring = smem_base() + kOffRing + kSplitStages * kStageBytes;
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem_base() + kOffAttBars);
-    const int n = T1 - T0;
-    auto slot_k = [&](int sl) { return reinterpret_cast<KV*>(ring + sl * 2 * kTileBytes); };
-    auto slot_v = [&](int sl) { return reinterpret_cast<KV*>(ring + sl * 2 * kTileBytes + kTileBytes); };
-    // Every layer of a step uses each slot the same number of times, so tile i's phase parity follows.
-    auto parity = [&](int i) {
-        const int sl = i % kAttRingSlots;
-        const int per_layer = sl < n ? (n - sl + kAttRingSlots - 1) / kAttRingSlots : 0;
-        return static_cast<uint32_t>((layer * per_layer + i / kAttRingSlots) & 1);
-    };
-    const uint64_t pol = l2_policy_evict_first();
-    const KV* kg = k_cache + static_cast<size_t>(h) * p.max_seq * kHd;
-    const KV* vg = v_cache + static_cast<size_t>(h) * p.max_seq * kHd;
-    auto issue = [&](int i) {
-        const int t = T0 + i, sl = i % kAttRingSlots;
-        const uint32_t bytes = static_cast<uint32_t>(min(kAttnTile, ctx - t * kAttnTile) * kHd * sizeof(KV));
-        mbar_arrive_expect_tx(&bars[sl], 2 * bytes);
-        bulk_load(slot_k(sl), kg + static_cast<size_t>(t) * kAttnTile * kHd, bytes, &bars[sl], pol);
-        bulk_load(slot_v(sl), vg + static_cast<size_t>(t) * kAttnTile * kHd, bytes, &bars[sl], pol);
-    };
-    // Cached tiles do not depend on this step: their copies start before q is waited for.
-    if (tid == 0) {
-        for (int i = 0; i < min(kAttRingSlots, n); ++i) issue(i);
+// One 8-token group's cached rows as this lane holds them: its key quarter, and dims 2l, 2l + 1 of the 8
+// values.
+struct GroupRows {
+    uint4 k0, k1;
+    uint32_t v[8];
+};
+
+// This lane's part of the group of 8 tokens starting at row jt of a staged 64-token tile: its key quarter of
+// token jt + lane / 4, and dims 2l, 2l + 1 of the 8 values (zero for tokens at or past `nt`, the tile's
+// valid rows, whose staged bytes are stale).
+template <typename KV>
+__device__ __forceinline__ void stage_group(const KV* kt, const KV* vt, int jt, int nt, int lane, GroupRows& r) {
+    const int j = jt + (lane >> 2);
+    if (j < nt) {
+        const uint4* kp = reinterpret_cast<const uint4*>(kt + j * kHd + 16 * (lane & 3));
+        r.k0 = kp[0];
+        r.k1 = kp[1];
+    } else {
+        r.k0 = r.k1 = make_uint4(0u, 0u, 0u, 0u);
     }
+#pragma unroll
+    for (int t = 0; t < 8; ++t) r.v[t] = jt + t < nt ? reinterpret_cast<const uint32_t*>(vt + (jt + t) * kHd)[lane] : 0u;
+}
+
+// Scores, online softmax and p.V of one group (tokens j0 .. j0 + 7, valid below `end`) for this warp.
+template <typename KV>
+__device__ __forceinline__ void attend_group(const GroupRows& r, int j0, int end, int lane, int warp, const float2 (&q)[kGqa][8],
+                                             float& m_run, float& l_run, float2 (&acc)[kGqa], RangeAttnSmem<KV>& sm) {
+    using KV2 = typename Kv2<KV>::T;
+    const KV2* k2a = reinterpret_cast<const KV2*>(&r.k0);
+    const KV2* k2b = reinterpret_cast<const KV2*>(&r.k1);
+    float sc[kGqa];
+#pragma unroll
+    for (int g = 0; g < kGqa; ++g) {
+        float2 a = make_float2(0.f, 0.f);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) a = fma2(kv2_to_float2(k2a[e]), q[g][e], a);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) a = fma2(kv2_to_float2(k2b[e]), q[g][4 + e], a);
+        sc[g] = a.x + a.y;
+    }
+    // Two exchanges over the token's 4 lanes: lane bit 0 picks heads {0,1} or {2,3}, bit 1 one of the pair.
+    const bool b0 = (lane & 1) != 0, b1 = (lane & 2) != 0;
+    const float x0 = __shfl_xor_sync(0xffffffffu, b0 ? sc[0] : sc[2], 1);
+    const float x1 = __shfl_xor_sync(0xffffffffu, b0 ? sc[1] : sc[3], 1);
+    const float t0 = (b0 ? sc[2] : sc[0]) + x0, t1 = (b0 ? sc[3] : sc[1]) + x1;
+    const float y = __shfl_xor_sync(0xffffffffu, b1 ? t0 : t1, 2);
+    const int hl = 2 * (lane & 1) + ((lane >> 1) & 1);
+    const int j = j0 + (lane >> 2);
+    const float s = j < end ? 0.125f * ((b1 ? t1 : t0) + y) : -INFINITY;
+    // Online softmax of head hl over the group's 8 tokens (the lanes with this lane's bits 0-1).
+    float mg = s;
+    mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, 4));
+    mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, 8));
+    mg = fmaxf(mg, __shfl_xor_sync(0xffffffffu, mg, 16));
+    const float m_new = fmaxf(m_run, mg);  // finite: token j0 is valid
+    const float p = expf(s - m_new);
+    float ps = p;
+    ps += __shfl_xor_sync(0xffffffffu, ps, 4);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 8);
+    ps += __shfl_xor_sync(0xffffffffu, ps, 16);
+    const float alpha = expf(m_run - m_new);
+    l_run = l_run * alpha + ps;
+    m_run = m_new;
+    sm.pw[warp][lane >> 2][hl] = p;
+    if (lane < 4) sm.aw[warp][hl] = alpha;
+    __syncwarp();
+    const float4 al = *reinterpret_cast<const float4*>(sm.aw[warp]);
+    acc[0] = make_float2(acc[0].x * al.x, acc[0].y * al.x);
+    acc[1] = make_float2(acc[1].x * al.y, acc[1].y * al.y);
+    acc[2] = make_float2(acc[2].x * al.z, acc[2].y * al.z);
+    acc[3] = make_float2(acc[3].x * al.w, acc[3].y * al.w);
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+        const float4 p4 = *reinterpret_cast<const float4*>(sm.pw[warp][t]);
+        const float2 vf = kv2_to_float2(*reinterpret_cast<const KV2*>(&r.v[t]));
+        acc[0] = fma2(make_float2(p4.x, p4.x), vf, acc[0]);
+        acc[1] = fma2(make_float2(p4.y, p4.y), vf, acc[1]);
+        acc[2] = fma2(make_float2(p4.z, p4.z), vf, acc[2]);
+        acc[3] = fma2(make_float2(p4.w, p4.w), vf, acc[3]);
+    }
+    __syncwarp();  // pw / aw are rewritten by the next group
+}
+
+// Rotates the 4 query heads of KV head h into sm.qs and, for the range that holds pos, rotates the new
+// key, rounds k and v to the cache type, writes them to the cache and keeps the rounded values in sm.kn /
+// sm.vn. Threads 0..127 the queries, 128..159 the key, 160..223 the value; the caller's barrier follows.
+template <typename KV, typename Src>
+__device__ __forceinline__ void load_query_insert_kv(const ConsumerCtx& c, int h, int pos, bool insert_new, const float* cs,
+                                                     KV* k_cache, KV* v_cache, Src qkv, RangeAttnSmem<KV>& sm) {
+    const StepParams& p = *c.p;
+    const int tid = c.tid;
     if (tid < kGqa * kHd / 2) {
         const int g = tid >> 5, i = tid & 31;
         const int q = (h * kGqa + g) * kHd;
@@ -697,168 +761,153 @@ __device__ void attend_range_stream(const ConsumerCtx& c, int layer, int h, int 
         sm.vn[d] = vv;
         v_cache[(static_cast<size_t>(h) * p.max_seq + pos) * kHd + d] = vv;
     }
-    csync();
-    float2 q[kGqa][4];
-#pragma unroll
-    for (int g = 0; g < kGqa; ++g) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) q[g][e] = make_float2(sm.qs[g][8 * c8 + 2 * e], sm.qs[g][8 * c8 + 2 * e + 1]);
+}
+
+// Token `row` of a group is the new token: its key quarter and value pair come from the rounded values in
+// shared memory (the staged copy of its cache row may predate this step's store).
+template <typename KV>
+__device__ __forceinline__ void patch_new_token(GroupRows& r, int row, int lane, const RangeAttnSmem<KV>& sm) {
+    if ((lane >> 2) == row) {
+        const uint4* ks = reinterpret_cast<const uint4*>(sm.kn + 16 * (lane & 3));
+        r.k0 = ks[0];
+        r.k1 = ks[1];
     }
-    float2 acc[kGqa][4];
+    r.v[row] = reinterpret_cast<const uint32_t*>(sm.vn)[lane];
+}
+
+// Merges the 8 warps' softmax states in warp order (a warp that saw no token has M = -inf, L = 0, O = 0)
+// and hands emit(hq, d, O, M, L) to thread 64 (hq - 4h) + d. Ends with a barrier.
+template <typename KV, typename Emit>
+__device__ __forceinline__ void merge_warp_states(const ConsumerCtx& c, int h, float m_run, float l_run,
+                                                  const float2 (&acc)[kGqa], RangeAttnSmem<KV>& sm, Emit emit) {
+    const int warp = c.cw, lane = c.lane, tid = c.tid;
+    const int hl = 2 * (lane & 1) + ((lane >> 1) & 1);
 #pragma unroll
-    for (int g = 0; g < kGqa; ++g) {
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[g][e] = make_float2(0.f, 0.f);
-    }
-    float m_run = -INFINITY, l_run = 0.f;  // head `warp`'s running softmax of this half (warps 0..3)
-    const bool hi4 = (lane & 4) != 0, hi2 = (lane & 2) != 0;
-    const int my_head = (hi4 ? 2 : 0) + (hi2 ? 1 : 0);
-    const int bar = 2 + hf;
-    int done = hf;  // next tile of this half
-    for (int i = hf; i < n; i += 2) {
-        const int sl = i % kAttRingSlots, t = T0 + i;
-        if (th == 0) {
-            uint64_t t0 = 0;
-            int ok = 1;
-            for (uint32_t it = 1; !mbar_try_wait(&bars[sl], parity(i)); ++it) {
-                if ((it & 63) == 0) {
-                    if (c.fl->abort) {
-                        ok = 0;
-                        break;
-                    }
-                    const uint64_t now = global_ns();
-                    if (t0 == 0) {
-                        t0 = now;
-                    } else if (now - t0 > p.wait_limit_ns) {
-                        fail(p, c.fl, kErrWaitTimeout, 60u + layer);
-                        ok = 0;
-                        break;
-                    }
-                }
-            }
-            sm.ok[hf] = ok;
-        }
-        named_barrier(bar, 128);
-        if (!sm.ok[hf]) break;
-        done = i + 2;
-        const int nt = min(kAttnTile, ctx - t * kAttnTile);
-        KV* kt = slot_k(sl);
-        KV* vt = slot_v(sl);
-        if (insert_new && pos >= t * kAttnTile && pos < t * kAttnTile + kAttnTile) {
-            // The copy brought the cache's old value at pos; the new token replaces it.
-            const int r = pos - t * kAttnTile;
-            if (th < kHd) {
-                kt[r * kHd + th] = sm.kn[th];
-                vt[r * kHd + th] = sm.vn[th];
-            }
-            named_barrier(bar, 128);
-        }
-#pragma unroll
-        for (int ps = 0; ps < 4; ++ps) {
-            const int j = ps * 16 + (th >> 3);
-            float sc[kGqa] = {0.f, 0.f, 0.f, 0.f};
-            if (j < nt) {
-                const uint4 u = *reinterpret_cast<const uint4*>(kt + j * kHd + 8 * c8);
-                const KV2* k2 = reinterpret_cast<const KV2*>(&u);
-#pragma unroll
-                for (int g = 0; g < kGqa; ++g) {
-                    float2 a = make_float2(0.f, 0.f);
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) a = fma2(kv2_to_float2(k2[e]), q[g][e], a);
-                    sc[g] = a.x + a.y;
-                }
-            }
-            const float r0 = __shfl_xor_sync(0xffffffffu, hi4 ? sc[0] : sc[2], 4);
-            const float r1 = __shfl_xor_sync(0xffffffffu, hi4 ? sc[1] : sc[3], 4);
-            const float a0 = (hi4 ? sc[2] : sc[0]) + r0;
-            const float a1 = (hi4 ? sc[3] : sc[1]) + r1;
-            const float r2 = __shfl_xor_sync(0xffffffffu, hi2 ? a0 : a1, 2);
-            float cc = (hi2 ? a1 : a0) + r2;
-            cc += __shfl_xor_sync(0xffffffffu, cc, 1);
-            if ((lane & 1) == 0) sm.s[hf][j][my_head] = j < nt ? 0.125f * cc : -INFINITY;
-        }
-        named_barrier(bar, 128);
-        if (warp < kGqa) {
-            const float s0 = sm.s[hf][lane][warp], s1 = sm.s[hf][lane + 32][warp];
-            const float m_new = fmaxf(m_run, warp_max(fmaxf(s0, s1)));  // finite: the tile's first token is in the context
-            const float p0 = expf(s0 - m_new), p1 = expf(s1 - m_new);
-            sm.s[hf][lane][warp] = p0;
-            sm.s[hf][lane + 32][warp] = p1;
-            const float alpha = expf(m_run - m_new);
-            l_run = l_run * alpha + warp_sum(p0 + p1);
-            m_run = m_new;
-            if (lane == 0) sm.alpha[hf][warp] = alpha;
-        }
-        named_barrier(bar, 128);
-        {
-            const float4 al = *reinterpret_cast<const float4*>(sm.alpha[hf]);
-            const float alv[kGqa] = {al.x, al.y, al.z, al.w};
-#pragma unroll
-            for (int g = 0; g < kGqa; ++g) {
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[g][e] = make_float2(acc[g][e].x * alv[g], acc[g][e].y * alv[g]);
-            }
-            const int jg = th >> 3;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int j = jg + 16 * k;
-                if (j < nt) {
-                    const uint4 u = *reinterpret_cast<const uint4*>(vt + j * kHd + 8 * c8);
-                    const KV2* v2 = reinterpret_cast<const KV2*>(&u);
-                    const float4 p4 = *reinterpret_cast<const float4*>(&sm.s[hf][j][0]);
-                    const float pv[kGqa] = {p4.x, p4.y, p4.z, p4.w};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const float2 vf = kv2_to_float2(v2[e]);
-#pragma unroll
-                        for (int g = 0; g < kGqa; ++g) acc[g][e] = fma2(make_float2(pv[g], pv[g]), vf, acc[g][e]);
-                    }
-                }
-            }
-        }
-        named_barrier(bar, 128);  // the slot and the score buffer are free again
-        if (th == 0 && i + kAttRingSlots < n) issue(i + kAttRingSlots);
-    }
-    if (done < n && th == 0) {
-        // This half gave up: the copies it issued or was due to consume land before it goes on (bounded).
-        for (int i = done; i < min(n, done + kAttRingSlots); i += 2) {  // issued, not consumed: done, done + 2
-            const uint64_t t0 = global_ns();
-            while (!mbar_try_wait(&bars[i % kAttRingSlots], parity(i)) && global_ns() - t0 < p.drain_limit_ns) {
-            }
-        }
-    }
-    // Sum this half's 16 token groups (red[jg][g][d] in the half's first slot, free now), keep (M, L).
-    float* red = reinterpret_cast<float*>(ring + hf * 2 * kTileBytes);
-    {
-        const int jg = th >> 3;
-#pragma unroll
-        for (int g = 0; g < kGqa; ++g) {
-            float4* dst = reinterpret_cast<float4*>(red + (jg * kGqa + g) * kHd + 8 * c8);
-            dst[0] = make_float4(acc[g][0].x, acc[g][0].y, acc[g][1].x, acc[g][1].y);
-            dst[1] = make_float4(acc[g][2].x, acc[g][2].y, acc[g][3].x, acc[g][3].y);
-        }
-    }
-    if (warp < kGqa && lane == 0) {
-        sm.mh[hf][warp] = m_run;
-        sm.lh[hf][warp] = l_run;
+    for (int g = 0; g < kGqa; ++g) *reinterpret_cast<float2*>(&sm.wo[warp][g][2 * lane]) = acc[g];
+    if (lane < 4) {
+        sm.wm[warp][hl] = m_run;
+        sm.wl[warp][hl] = l_run;
     }
     csync();
     {
         const int g = tid >> 6, d = tid & 63;
-        const float* r0 = reinterpret_cast<const float*>(ring);
-        const float* r1 = reinterpret_cast<const float*>(ring + 2 * kTileBytes);
-        float o0 = 0.f, o1 = 0.f;
+        float M = -INFINITY;
 #pragma unroll
-        for (int jg = 0; jg < 16; ++jg) {
-            o0 += r0[(jg * kGqa + g) * kHd + d];
-            o1 += r1[(jg * kGqa + g) * kHd + d];
+        for (int w = 0; w < kCw; ++w) M = fmaxf(M, sm.wm[w][g]);
+        float L = 0.f, O = 0.f;
+#pragma unroll
+        for (int w = 0; w < kCw; ++w) {
+            const float e = expf(sm.wm[w][g] - M);
+            L = fmaf(sm.wl[w][g], e, L);
+            O = fmaf(sm.wo[w][g][d], e, O);
         }
-        const float M = fmaxf(sm.mh[0][g], sm.mh[1][g]);
-        const float e0 = expf(sm.mh[0][g] - M), e1 = expf(sm.mh[1][g] - M);  // 0 for a half without tiles
-        emit(h * kGqa + g, d, o0 * e0 + o1 * e1, M, sm.lh[0][g] * e0 + sm.lh[1][g] * e1);
+        emit(h * kGqa + g, d, O, M, L);
     }
-    fence_proxy_async_shared();  // this layer's writes to the slots precede the next layer's copies into them
+    fence_proxy_async_shared();  // this layer's reads of the K/V slots precede the next layer's copies
     csync();
+}
+
+template <typename KV, typename Src, typename Emit>
+__device__ void attend_range_tiles(const ConsumerCtx& c, int layer, int h, int T0, int T1, int ctx, bool insert_new,
+                                   const float* cs, KV* k_cache, KV* v_cache, Src qkv, Emit emit) {
+    constexpr int kTileBytes = kAttnTile * kHd * static_cast<int>(sizeof(KV));
+    const StepParams& p = *c.p;
+    const int pos = ctx - 1;
+    const int tid = c.tid, warp = c.cw, lane = c.lane;
+    RangeAttnSmem<KV>& sm = *reinterpret_cast<RangeAttnSmem<KV>*>(c.xp);
+    uint8_t* ring = smem_base() + kOffRing + ring_stages<true>() * kStageBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem_base() + kOffAttFull);
+    int* cnt = reinterpret_cast<int*>(smem_base() + kOffAttCnt);  // arrivals per slot, then pending parity + 1
+    int* pend = cnt + kAttSlots;
+    const int n = T1 - T0;
+    auto slot_k = [&](int sl) { return reinterpret_cast<KV*>(ring + sl * 2 * kTileBytes); };
+    auto slot_v = [&](int sl) { return reinterpret_cast<KV*>(ring + sl * 2 * kTileBytes + kTileBytes); };
+    // Every layer of a step uses each slot the same number of times, so tile i's phase parity follows.
+    auto parity = [&](int i) {
+        const int sl = i % kAttSlots;
+        const int per_layer = sl < n ? (n - sl + kAttSlots - 1) / kAttSlots : 0;
+        return static_cast<uint32_t>((layer * per_layer + i / kAttSlots) & 1);
+    };
+    const KV* kg = k_cache + static_cast<size_t>(h) * p.max_seq * kHd;
+    const KV* vg = v_cache + static_cast<size_t>(h) * p.max_seq * kHd;
+    auto issue = [&](int i) {
+        const int t = T0 + i, sl = i % kAttSlots;
+        const uint32_t bytes = static_cast<uint32_t>(min(kAttnTile, ctx - t * kAttnTile) * kHd * sizeof(KV));
+        const uint64_t pol = l2_policy_evict_first();
+        pend[sl] = static_cast<int>(parity(i)) + 1;
+        mbar_arrive_expect_tx(&full[sl], 2 * bytes);
+        bulk_load(slot_k(sl), kg + static_cast<size_t>(t) * kAttnTile * kHd, bytes, &full[sl], pol);
+        bulk_load(slot_v(sl), vg + static_cast<size_t>(t) * kAttnTile * kHd, bytes, &full[sl], pol);
+    };
+    // Cached tiles do not depend on this step: their copies start before q is waited for.
+    if (tid == 0) {
+        for (int i = 0; i < min(kAttSlots, n); ++i) issue(i);
+    }
+    load_query_insert_kv<KV>(c, h, pos, insert_new, cs, k_cache, v_cache, qkv, sm);
+    csync();
+    float2 q[kGqa][8];
+#pragma unroll
+    for (int g = 0; g < kGqa; ++g) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) q[g][e] = *reinterpret_cast<const float2*>(&sm.qs[g][16 * (lane & 3) + 2 * e]);
+    }
+    float m_run = -INFINITY, l_run = 0.f;
+    float2 acc[kGqa];
+#pragma unroll
+    for (int g = 0; g < kGqa; ++g) acc[g] = make_float2(0.f, 0.f);
+    bool ok = true;
+    for (int i = 0; i < n && ok; ++i) {
+        const int sl = i % kAttSlots, t = T0 + i;
+        uint64_t t0 = 0;
+        for (uint32_t it = 1; !__all_sync(0xffffffffu, mbar_try_wait(&full[sl], parity(i))); ++it) {
+            if ((it & 63) == 0) {
+                if (__any_sync(0xffffffffu, c.fl->abort != 0)) {
+                    ok = false;
+                    break;
+                }
+                const uint64_t now = __shfl_sync(0xffffffffu, global_ns(), 0);
+                if (t0 == 0) {
+                    t0 = now;
+                } else if (now - t0 > p.wait_limit_ns) {
+                    if (lane == 0) fail(p, c.fl, kErrWaitTimeout, 60u + layer);
+                    ok = false;
+                    break;
+                }
+            }
+        }
+        if (!ok) break;
+        const int nt = min(kAttnTile, ctx - t * kAttnTile);
+        const int jt = 8 * warp;
+        GroupRows r;
+        if (jt < nt) stage_group<KV>(slot_k(sl), slot_v(sl), jt, nt, lane, r);
+        // The warp's rows are in registers: it releases the slot; the last of the 8 warps refills it.
+        __syncwarp();
+        if (lane == 0) {
+            __threadfence_block();
+            if (atomicAdd(&cnt[sl], 1) == kCw - 1) {
+                cnt[sl] = 0;
+                if (i + kAttSlots < n) {
+                    fence_proxy_async_shared();
+                    issue(i + kAttSlots);
+                }
+            }
+        }
+        if (jt < nt) {
+            const int j0 = t * kAttnTile + jt;
+            if (insert_new && pos >= j0 && pos < j0 + 8) patch_new_token<KV>(r, pos - j0, lane, sm);
+            attend_group<KV>(r, j0, t * kAttnTile + nt, lane, warp, q, m_run, l_run, acc, sm);
+        }
+    }
+    if (named_barrier_or(1, kCt, !ok) && tid == 0) {
+        // A wait gave up: every copy issued lands before the CTA goes on (bounded).
+        for (int sl = 0; sl < kAttSlots; ++sl) {
+            const uint64_t t0 = global_ns();
+            while (pend[sl] != 0 && !mbar_try_wait(&full[sl], static_cast<uint32_t>(pend[sl] - 1)) &&
+                   global_ns() - t0 < p.drain_limit_ns) {
+            }
+        }
+    }
+    merge_warp_states<KV>(c, h, m_run, l_run, acc, sm, emit);
 }
 
 // Merges the S partials of KV head h in range order and writes the 4 query heads' outputs. Threads 0..S-1
@@ -1153,23 +1202,6 @@ __device__ bool run_tiles_shared(ConsumerCtx& c, int o, int kind, float& bv, int
     return !named_barrier_or(1, kCt, !ok || c.fl->abort != 0);
 }
 
-// The cached K/V rows of this CTA's range (split contexts) into L2, before the layer's attention needs them.
-template <typename KV>
-__device__ __forceinline__ void prefetch_split_kv(const ConsumerCtx& c, size_t layer_bytes, int ctx) {
-    const StepParams& p = *c.p;
-    const AttnRole ar = attn_role(p, ctx);
-    if (ar.head < 0) return;
-    const int n_tiles = (ctx + kAttnTile - 1) / kAttnTile;
-    const int t0 = 2 * ar.p0, t1 = min(n_tiles, 2 * ar.p1);
-    for (int q = c.tid; q < 2 * (t1 - t0); q += kCt) {
-        const int tile = t0 + (q >> 1);
-        const int n = min(kAttnTile, ctx - tile * kAttnTile);
-        const size_t off = (static_cast<size_t>(ar.head) * p.max_seq + tile * kAttnTile) * kHd * sizeof(KV);
-        const uint8_t* base = static_cast<const uint8_t*>((q & 1) ? p.v_cache : p.k_cache);
-        bulk_prefetch_l2(base + layer_bytes + off, static_cast<uint32_t>(n * kHd * sizeof(KV)));
-    }
-}
-
 // Stages an operation's input vector into the planes of c.xp (int4: and the chunk sums into c.xc) with the
 // RMSNorm's 1/rms deferred: the planes hold x * gain, and the returned factor (1/rms, or 1 without a norm)
 // scales each output row after its dot product (the projection is linear). So the sum of squares needs no
@@ -1291,8 +1323,6 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
                         bulk_prefetch_l2(base + layer_bytes + off, static_cast<uint32_t>(n * kHd * sizeof(KV)));
                     }
                 }
-            } else if constexpr (SPLIT) {
-                prefetch_split_kv<KV>(c, layer_bytes, ctx);
             }
             if (l > 0) {
                 tsrc = p.t_xout;
@@ -1332,7 +1362,7 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
                     const int h = ar.head, sp = ar.split;
                     // The range that holds pos inserts the new token. Partials go to slot = range; after a
                     // barrier (all of the CTA's stores done) one release store of the step's tag publishes them.
-                    attend_range_stream<KV>(
+                    attend_range_tiles<KV>(
                         c, l, h, 2 * ar.p0, min(n_tiles, 2 * ar.p1), ctx, ar.p1 == ar.n_pass, cs, kc, vc, qkv_src,
                         [&](int hq, int d, float O, float M, float L) {
                             const size_t slot = static_cast<size_t>(hq) * n_slots + sp;
@@ -1472,13 +1502,18 @@ __global__ void __launch_bounds__(kThreads, 1) decode_step_kernel(const __grid_c
     volatile int* stage_tile = reinterpret_cast<volatile int*>(smem + kOffTiles);
     uint8_t* ring = smem + kOffRing;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < ring_stages<SPLIT>(); ++s) {
+        for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
             stage_tile[s] = -1;
         }
         if constexpr (SPLIT) {
-            for (int s = 0; s < kAttRingSlots; ++s) mbar_init(reinterpret_cast<uint64_t*>(smem + kOffAttBars) + s, 1);
+            int* att_words = reinterpret_cast<int*>(smem + kOffAttCnt);
+            for (int s = 0; s < kAttSlots; ++s) {
+                mbar_init(reinterpret_cast<uint64_t*>(smem + kOffAttFull) + s, 1);
+                att_words[s] = 0;              // arrivals
+                att_words[kAttSlots + s] = 0;  // pending copy: none
+            }
         }
         fl->abort = 0;
         fl->ok = 0;
