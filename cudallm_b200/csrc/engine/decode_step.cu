@@ -115,14 +115,27 @@ constexpr int stage_rows() {
 // How the consumer warps share the stages of one operation kind: kRows stage rows (both halves for the
 // gate/up operation), kWps warps per stage (1: one warp consumes a whole stage; >1: the stage's rows are
 // split over kWps warps and kCw / kWps warp groups take stages in turn), kNw rows per warp, kHalf of them
-// per half, kCpl 16-byte chunks per lane of a row. int4 shares stages; bf16 and int8 do not.
-// int4 warps per stage by operation kind (qkv, o-proj, gate/up, down, lm_head).
-constexpr int kInt4WarpsPerStage[5] = {8, 8, 4, 4, 4};
+// per half, kCpl 16-byte chunks per lane of a row.
+// Warps per stage by weight type and operation kind (qkv, o-proj, gate/up, down, lm_head).
+constexpr int kBf16WarpsPerStage[5] = {1, 1, 1, 1, 1};
+constexpr int kInt8WarpsPerStage[5] = {1, 1, 1, 1, 1};
+constexpr int kInt4WarpsPerStage[5] = {4, 4, 4, 4, 4};
+template <WeightType WT>
+constexpr int warps_per_stage(int kind) {
+    return WT == WeightType::INT4 ? kInt4WarpsPerStage[kind]
+           : WT == WeightType::INT8 ? kInt8WarpsPerStage[kind] : kBf16WarpsPerStage[kind];
+}
+// Whether any operation of this weight type shares its stages (then every operation runs the shared loop).
+template <WeightType WT>
+constexpr bool shares_stages() {
+    return warps_per_stage<WT>(0) > 1 || warps_per_stage<WT>(1) > 1 || warps_per_stage<WT>(2) > 1 ||
+           warps_per_stage<WT>(3) > 1 || warps_per_stage<WT>(4) > 1;
+}
 template <WeightType WT, int KIND>
 struct StageShape {
     static constexpr int kHalves = KIND == 2 ? 2 : 1;
     static constexpr int kRows = stage_rows<WT, KIND>();
-    static constexpr int kWps = WT == WeightType::INT4 ? kInt4WarpsPerStage[KIND] : 1;
+    static constexpr int kWps = warps_per_stage<WT>(KIND);
     static constexpr int kNw = kRows / kWps;
     static constexpr int kHalf = kNw / kHalves;
     static constexpr int kCpl = seg_chunks_per_lane<WT, KIND>();
@@ -1418,7 +1431,7 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
         if (c.tid == 0) trace_mark(p, top, 4);
         bool ok;
         constexpr int ST = ring_stages<SPLIT>();
-        if constexpr (StageShape<WT, kQkv>::kWps > 1) {
+        if constexpr (shares_stages<WT>()) {
             ok = kind == kDown ? run_tiles_shared<WT, kDown, ST>(c, o, kind, bv, bi, l)
                  : kind == kGu ? run_tiles_shared<WT, kGu, ST>(c, o, kind, bv, bi, l)
                  : kind == kLm ? run_tiles_shared<WT, kLm, ST>(c, o, kind, bv, bi, l)
