@@ -18,6 +18,8 @@ reported under "batched" ({"bf16": ..., "int4": ...}) as the whole-job tok/s ove
 On one GPU (unless --quick) the line also carries the configured workloads whatever --steps is:
   * "gen256": the headline precision over the configured 256 decode steps (positions 32..287);
   * "precisions": bf16 / int8 / int4 over the same 256 steps (BASELINE configs 1-3);
+  * "sampling": the headline precision over those 256 steps with top-k / top-p sampling fused into the
+    step (cudallm_set_sampling with SAMPLING's settings) instead of argmax;
   * "long_context": BASELINE config 4, bf16 weights in a max_seq_len 32896 file: the KV cache is filled by
     the chunked prefill (seeded random tokens, untimed for the decode figures) to 4096 and then 32768 cached
     tokens, and 128 greedy decode steps are timed at each context (bytes per token include the KV read at
@@ -179,6 +181,7 @@ def time_e2e(eng, prompt: list[int], steps: int, torch, barrier) -> dict:
 
 
 CONFIG_GEN = 256                           # greedy decode of 256 tokens
+SAMPLING = {"temperature": 0.8, "top_k": 40, "top_p": 0.95, "seed": 1}  # the "sampling" figure's settings
 LONG_MAX_SEQ, LONG_CTX, LONG_GEN = 32896, (4096, 32768), 128
 
 
@@ -397,7 +400,14 @@ def run_ours(args) -> None:
             reuse = t is not None and args.steps == CONFIG_GEN
             t256 = (t if reuse else time_decode(eng, prompt, CONFIG_GEN, args.warmup, torch, lambda: None)) \
                 if world == 1 else None
-        results[dt] = {"t": t, "e": e, "clocks": clocks, "weight_bytes": weight_bytes, "t256": t256}
+            # The same 256 steps with top-k / top-p sampling fused into the step instead of argmax.
+            t_sample = None
+            if world == 1 and not args.quick and dt == args.dtype:
+                eng.set_sampling(SAMPLING["temperature"], SAMPLING["top_k"], SAMPLING["top_p"], SAMPLING["seed"])
+                t_sample = time_decode(eng, prompt, CONFIG_GEN, args.warmup, torch, lambda: None)
+                eng.set_sampling(0.0)
+        results[dt] = {"t": t, "e": e, "clocks": clocks, "weight_bytes": weight_bytes, "t256": t256,
+                       "t_sample": t_sample}
 
     head = results[args.dtype]
     total_ms = max_over_ranks(head["t"]["total_ms"])
@@ -417,6 +427,12 @@ def run_ours(args) -> None:
 
     extra = {dt: summarise(r["t256"], r["weight_bytes"], CONFIG_GEN) for dt, r in results.items() if r["t256"]}
     gen256 = extra.get(args.dtype)
+    ts = results[args.dtype].get("t_sample")
+    sampling = None
+    if ts:
+        sampling = dict(summarise(ts, results[args.dtype]["weight_bytes"], CONFIG_GEN), **SAMPLING)
+        if gen256:
+            sampling["us_per_token_over_greedy"] = 1e3 * (sampling["ms_per_token"] - gen256["ms_per_token"])
     long_context = time_long_context(args, local_rank, torch, peaks["hbm_gbs"]) if (world == 1 and not args.quick) else None
 
     batched = {}
@@ -469,6 +485,7 @@ def run_ours(args) -> None:
             "gpu_launches": args.steps,
             "clocks": head["clocks"],
             "gen256": gen256,
+            "sampling": sampling,
             "precisions": extra,
             "long_context": long_context,
             "batched": batched,

@@ -321,6 +321,10 @@ int cudallm_debug_set(cudallm_engine* e, const char* knob, long long value) {
     });
 }
 
+int cudallm_set_sampling(cudallm_engine* e, float temperature, int top_k, float top_p, unsigned long long seed) {
+    return invoke([&] { cudallm::engine_of(e, "cudallm_set_sampling").set_sampling(temperature, top_k, top_p, seed); });
+}
+
 // ---- single-kernel test hooks ----
 
 int cudallm_kernel_matvec(int impl, int weight_dtype, int epilogue, int fuse_norm, int rpb, const void* w,

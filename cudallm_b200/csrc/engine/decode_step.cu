@@ -12,6 +12,7 @@
 #include "kernels/attention_core.cuh"
 #include "kernels/matvec_core.cuh"
 #include "kernels/ptx.cuh"
+#include "kernels/sampling.cuh"
 
 namespace cudallm {
 
@@ -76,6 +77,11 @@ constexpr int kMaxResRows = 48;
 constexpr int kOffXc = 2048;
 constexpr int kOffXp = 3072;
 constexpr int kOffRing = kOffXp + kMaxK * 4;  // 35840
+// Sampling scratch in the (idle) ring after the lm_head: the candidate keys of one CTA's rows, or of every
+// CTA's top k in the last CTA, then the selection's scratch and result.
+constexpr int kSampleKeyBytes = kSampleMaxGrid * kMaxTopK * 8;
+static_assert(kSampleKeyBytes + static_cast<int>(sizeof(TopKScratch)) + kMaxTopK * 8 <= kStages * kStageBytes,
+              "sampling scratch must fit in the ring");
 constexpr int kSmemBytes = kOffRing + kStages * kStageBytes;
 static_assert(kOffTiles + kStages * 4 <= kOffFlags, "barriers overflow");
 static_assert(kOffAm + kCw * 8 <= kOffRes && kOffRes + kMaxResRows * 4 <= kOffXc, "argmax / residual scratch overflow");
@@ -1447,6 +1453,22 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
     // ---- lm_head done: CTA argmax, then the last CTA commits the token ----------------------
     float* am_v = reinterpret_cast<float*>(c.scratch);  // scratch is free again after run_tiles
     int* am_i = reinterpret_cast<int*>(c.scratch + kCw);
+    // Sampling: this CTA's top k lm_head rows become candidate keys (its logits, stored above, are read back
+    // through L2; the weight ring is idle now and holds the selection's keys).
+    const bool sampling = p.sample_temperature > 0.f;
+    const int kk = p.sample_top_k;
+    uint64_t* keys = reinterpret_cast<uint64_t*>(smem_base() + kOffRing);
+    TopKScratch& tks = *reinterpret_cast<TopKScratch*>(smem_base() + kOffRing + kSampleKeyBytes);
+    uint64_t* top = reinterpret_cast<uint64_t*>(smem_base() + kOffRing + kSampleKeyBytes + sizeof(TopKScratch));
+    if (sampling) {
+        const KindRows kr = kind_table()[kLm];
+        const int n = kr.hi - kr.lo;
+        csync();  // every row of this CTA stored
+        for (int i = c.tid; i < n; i += kCt) keys[i] = candidate_key(__ldcg(p.logits + kr.lo + i), kr.lo + i);
+        csync();
+        select_top_k(keys, n, kk, top, tks, c.tid, kCt, [] { csync(); });
+        for (int j = c.tid; j < kk; j += kCt) __stcg(p.cand + static_cast<size_t>(blockIdx.x) * kMaxTopK + j, top[j]);
+    }
     warp_argmax(bv, bi);
     if (c.lane == 0) {
         am_v[c.cw] = bv;
@@ -1473,7 +1495,16 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
         trace_mark(p, 81, 2);
     }
     if (c.fl->role == 0) return;
-    // Last CTA: reduce the per-CTA winners, commit the token, advance the position, reset counters.
+    // Last CTA: reduce the per-CTA winners (sampling: select among the CTAs' candidates and draw), commit the
+    // token, advance the position, reset counters.
+    int drawn = -1;
+    if (sampling) {
+        const int n = G * kk;
+        for (int i = c.tid; i < n; i += kCt) keys[i] = __ldcg(p.cand + static_cast<size_t>(i / kk) * kMaxTopK + i % kk);
+        csync();
+        select_top_k(keys, n, kk, top, tks, c.tid, kCt, [] { csync(); });
+        if (c.tid == 0) drawn = draw_from_top_k(top, kk, p.sample_temperature, p.sample_top_p, sample_uniform(p.sample_seed, pos));
+    }
     float v = -INFINITY;
     int i = INT_MAX;
     for (int k = c.tid; k < G; k += kCt) {
@@ -1500,7 +1531,7 @@ __device__ void run_consumers(ConsumerCtx& c, float* cs) {
                 bi2 = am_i[w];
             }
         }
-        *p.d_token = bi2 == INT_MAX ? 0 : bi2;
+        *p.d_token = drawn >= 0 ? drawn : (bi2 == INT_MAX ? 0 : bi2);
         *p.d_pos = pos + 1;
         __threadfence();
     }

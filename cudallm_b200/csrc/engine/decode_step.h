@@ -19,6 +19,7 @@
 
 #include "common/dtype.h"
 #include "kernels/kernels.h"
+#include "kernels/sampling.cuh"
 
 namespace cudallm {
 
@@ -48,6 +49,8 @@ struct StepLayer {
 };
 
 constexpr int kStepLayers = 16;
+// Largest grid whose lm_head candidates the persistent step's last CTA can hold when sampling.
+constexpr int kSampleMaxGrid = 160;
 
 // Trace layout per CTA: operation k (layer l: 5l + {0 qkv, 1 attention, 2 o-proj, 3 gate/up, 4 down};
 // 80 lm_head; 81 step end) has kTraceStamps slots: 0 dependency wait begins, 1 wait ends, 2 operation
@@ -120,6 +123,14 @@ struct StepParams {
     int trace_t0;        // first stamped tile (global index in CTA 0's tile stream)
     int stall_op;        // test only, -1 = off: the consumers of weight operation k (k >= 1) wait for an input
                          // tag that nothing writes, so every CTA's wait runs out after wait_limit_ns
+    // Next-token choice: temperature 0 = greedy (argmax, the reference's rule); > 0 = sampling from the top
+    // sample_top_k (1..64) logits, nucleus sample_top_p, draw sample_seed at the current position. cand:
+    // [grid][64] candidate keys (each CTA's top k), used only when sampling.
+    float sample_temperature;  // (sampling needs grid <= kSampleMaxGrid and <= kSampleMaxGrid * 64 rows per CTA)
+    float sample_top_p;
+    int sample_top_k;
+    unsigned long long sample_seed;
+    unsigned long long* cand;
     TileGeom g_qkv, g_wo, g_gu, g_down, g_lm;
 };
 

@@ -4,6 +4,7 @@
 #include <cuda_fp16.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <string>
 #include <type_traits>
@@ -76,6 +77,7 @@ void Engine::for_each_region(Fn&& fn) {
     fn(logits_, V);
     fn(am_v_, kArgmaxBlocks);
     fn(am_i_, kArgmaxBlocks);
+    fn(cand_, static_cast<size_t>(kArgmaxBlocks) * kMaxTopK);
     fn(part_o_, NH * slots * D);
     fn(part_ml_, NH * slots * 2);
     fn(debug_res_, (c.n_layers + 1) * H);
@@ -185,6 +187,14 @@ void Engine::make_step_params() {
     p.prefetch_mode = 3;  // bulk L2 prefetches from the prefetch warp
     p.whole_head_max_tiles = c.wtype == WeightType::INT4 ? kWholeHeadMaxTilesInt4 : kWholeHeadMaxTiles;
     p.stall_op = -1;
+    p.sample_temperature = 0.f;  // greedy
+    p.sample_top_k = kMaxTopK;
+    p.sample_top_p = 1.f;
+    p.sample_seed = 0;
+    p.cand = cand_;
+    CLLM_CHECK(c.vocab / decode_step_grid() >= kMaxTopK && decode_step_grid() <= kSampleMaxGrid &&
+                   c.vocab / decode_step_grid() + 1 <= kSampleMaxGrid * kMaxTopK,
+               "decode step: lm_head rows per CTA or grid outside the sampling bounds");
     // The persistent kernel has its own compile-time tile shape (matvec_rpb applies to the per-op kernels;
     // results do not depend on either).
     const int rows = decode_step_tile_rows(c.wtype);
@@ -195,6 +205,17 @@ void Engine::make_step_params() {
     p.g_down = make_tile_geom(c.wtype, Epilogue::ADD, c.hidden, c.inter, rows, kDownSegBytes);
     p.g_lm = make_tile_geom(c.wtype, Epilogue::STORE, c.vocab, c.hidden, rows);
     set_knob("trace_tile_op", kTraceLmOp);
+}
+
+void Engine::set_sampling(float temperature, int top_k, float top_p, unsigned long long seed) {
+    CLLM_REQUIRE(std::isfinite(temperature) && temperature >= 0.f, "temperature must be finite and >= 0 (0 = greedy)");
+    CLLM_REQUIRE(top_k >= 0 && top_k <= kMaxTopK, "top_k must be in [0, 64] (0 = 64)");
+    CLLM_REQUIRE(top_p > 0.f && top_p <= 1.f, "top_p must be in (0, 1]");
+    CLLM_REQUIRE(temperature == 0.f || persistent_, "sampling needs the persistent decode path");
+    step_.sample_temperature = temperature;
+    step_.sample_top_k = top_k == 0 ? kMaxTopK : top_k;
+    step_.sample_top_p = top_p;
+    step_.sample_seed = seed;
 }
 
 void Engine::set_knob(const std::string& name, long long value) {

@@ -89,6 +89,9 @@ public:
     // consumers of weight operation k wait for an input that is never written, so the step's waits run out
     // and it fails with StateError; -1 = off, 1 .. 64).
     void set_knob(const std::string& name, long long value);
+    // Next-token rule of the persistent step: temperature 0 = greedy argmax (the default); > 0 = sampling
+    // from the top_k (1..64; 0 = 64) logits with nucleus top_p (0, 1], drawn from (seed, position).
+    void set_sampling(float temperature, int top_k, float top_p, unsigned long long seed);
 
     // Device state read back with every synchronising step: the fed/argmax token, the position and the
     // error words of the bounded in-kernel waits.
@@ -150,6 +153,7 @@ private:
     float* part_ml_ = nullptr;  // [heads][max_seq / 64][2]
     float* am_v_ = nullptr;     // argmax partials
     int* am_i_ = nullptr;
+    unsigned long long* cand_ = nullptr;  // persistent step, sampling: [argmax slots][64] candidate keys
     DevState* state_ = nullptr;
     unsigned* sync_ = nullptr;  // persistent step: split-attention flags and the lm_head ticket
     float* debug_res_ = nullptr;  // persistent step_debug: residuals [(layers + 1) * hidden]

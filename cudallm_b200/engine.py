@@ -160,6 +160,11 @@ class Engine(_Owned):
         """Tuning / test knob of the persistent step (cudallm_debug_set)."""
         check(lib().cudallm_debug_set(self._handle(), name.encode(), int(value)))
 
+    def set_sampling(self, temperature: float = 0.0, top_k: int = 0, top_p: float = 1.0, seed: int = 0) -> None:
+        """Next-token rule (cudallm_set_sampling): temperature 0 = greedy; else top-k / top-p sampling drawn
+        from (seed, position)."""
+        check(lib().cudallm_set_sampling(self._handle(), float(temperature), int(top_k), float(top_p), int(seed)))
+
     def trace(self, enable: bool = True) -> None:
         """Per-CTA timestamps of each following step (persistent path only)."""
         check(lib().cudallm_debug_trace(self._handle(), int(bool(enable))))

@@ -154,6 +154,16 @@ int cudallm_debug_read_trace(cudallm_engine* e, unsigned long long* out, unsigne
  * CUDALLM_ERR_STATE; -1 = off, the default). */
 int cudallm_debug_set(cudallm_engine* e, const char* knob, long long value);
 
+/* Next-token rule of the following steps (no counterpart in the reference, which decodes greedily:
+ * src/kernels/argmax.cu). temperature 0 (the default) = argmax, lowest index on ties. temperature > 0 =
+ * sampling: the top_k largest logits (1 .. 64; 0 = 64; ties to the lower index) are weighted by
+ * exp((logit - max) / temperature); the nucleus is the shortest prefix of them, in descending order, whose
+ * weight reaches top_p (0 < top_p <= 1) of their total; the token is drawn from it with a uniform number
+ * that depends only on (seed, position), so a rerun reproduces the tokens. The `next` output of
+ * cudallm_step and the token fed by cudallm_step(e, -1, ...) are the drawn token; logits are unchanged.
+ * Persistent decode path only (INVALID_ARG on a per-op engine with temperature > 0). */
+int cudallm_set_sampling(cudallm_engine* e, float temperature, int top_k, float top_p, unsigned long long seed);
+
 /* ---- batched decode (no counterpart in the reference, whose engine holds one sequence): up to 64
  * independent sequences decoded together on one GPU, one token each per step; every row runs the
  * reference engine's per-token sequence (src/engine/engine.cpp:181-237) on its own token, position and KV
