@@ -319,6 +319,62 @@ __device__ __forceinline__ void tile_dot(const uint8_t* stage, const TileRows& t
     }
 }
 
+// Register-staged form of tile_dot for bf16 and int8 tiles with a compile-time shape (N rows of CPL chunks per
+// lane, rows contiguous at CPL * 512 bytes): load_tile_regs copies chunks j0 .. j0 + H - 1 of this lane's
+// chunks of every row into registers, so the caller can release the stage before all the arithmetic is done
+// and the ring refills while the warp computes; tile_dot_regs advances the two accumulation chains per row
+// a[i] over those chunks. Called over consecutive chunk ranges from a[i] = 0 and followed by
+// acc[i] += a[i].x + a[i].y, it performs exactly tile_dot's operations in tile_dot's order (bit-identical).
+template <WeightType WT, int N, int H, int CPL>
+__device__ __forceinline__ void load_tile_regs(const uint8_t* stage, uint4 (&w)[N][H], int lane, int j0) {
+    static_assert(WT != WeightType::INT4, "int4 stages are shared between warps");
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) {
+            w[i][j] = *reinterpret_cast<const uint4*>(stage + i * (CPL * 512) + (lane + 32 * (j0 + j)) * 16);
+        }
+    }
+}
+
+template <WeightType WT, int N, int H>
+__device__ __forceinline__ void tile_dot_regs(const uint4 (&w)[N][H], int chunk0, const float* xp, int nc, float2 (&a)[N],
+                                              int lane) {
+    static_assert(WT != WeightType::INT4, "int4 stages are shared between warps");
+    const float4* p4 = reinterpret_cast<const float4*>(xp);
+#pragma unroll
+    for (int j = 0; j < H; ++j) {
+        const int gc = chunk0 + lane + 32 * j;
+        if constexpr (WT == WeightType::BF16) {
+            const float4 x0 = p4[gc], x1 = p4[nc + gc];
+#pragma unroll
+            for (int i = 0; i < N; ++i) {
+                const uint4 v = w[i][j];
+                a[i] = fma2(make_float2(bf16lo(v.x), bf16hi(v.x)), make_float2(x0.x, x0.y), a[i]);
+                a[i] = fma2(make_float2(bf16lo(v.y), bf16hi(v.y)), make_float2(x0.z, x0.w), a[i]);
+                a[i] = fma2(make_float2(bf16lo(v.z), bf16hi(v.z)), make_float2(x1.x, x1.y), a[i]);
+                a[i] = fma2(make_float2(bf16lo(v.w), bf16hi(v.w)), make_float2(x1.z, x1.w), a[i]);
+            }
+        } else {
+            const float4 x0 = p4[gc], x1 = p4[nc + gc], x2 = p4[2 * nc + gc], x3 = p4[3 * nc + gc];
+            const float2 bias = make_float2(-8388736.f, -8388736.f);
+#pragma unroll
+            for (int i = 0; i < N; ++i) {
+                const uint4 v = w[i][j];
+                const uint32_t b0 = v.x ^ 0x80808080u, b1 = v.y ^ 0x80808080u, b2 = v.z ^ 0x80808080u, b3 = v.w ^ 0x80808080u;
+                a[i] = fma2(add2(make_float2(i8raw(b0, 0x7540), i8raw(b0, 0x7541)), bias), make_float2(x0.x, x0.y), a[i]);
+                a[i] = fma2(add2(make_float2(i8raw(b0, 0x7542), i8raw(b0, 0x7543)), bias), make_float2(x0.z, x0.w), a[i]);
+                a[i] = fma2(add2(make_float2(i8raw(b1, 0x7540), i8raw(b1, 0x7541)), bias), make_float2(x1.x, x1.y), a[i]);
+                a[i] = fma2(add2(make_float2(i8raw(b1, 0x7542), i8raw(b1, 0x7543)), bias), make_float2(x1.z, x1.w), a[i]);
+                a[i] = fma2(add2(make_float2(i8raw(b2, 0x7540), i8raw(b2, 0x7541)), bias), make_float2(x2.x, x2.y), a[i]);
+                a[i] = fma2(add2(make_float2(i8raw(b2, 0x7542), i8raw(b2, 0x7543)), bias), make_float2(x2.z, x2.w), a[i]);
+                a[i] = fma2(add2(make_float2(i8raw(b3, 0x7540), i8raw(b3, 0x7541)), bias), make_float2(x3.x, x3.y), a[i]);
+                a[i] = fma2(add2(make_float2(i8raw(b3, 0x7542), i8raw(b3, 0x7543)), bias), make_float2(x3.z, x3.w), a[i]);
+            }
+        }
+    }
+}
+
 // Row result after the warp reduction (all lanes hold it); int8 applies its per-row scale here.
 template <WeightType WT>
 __device__ __forceinline__ float finish_row(float reduced, const void* scales, int global_row) {
