@@ -583,8 +583,9 @@ __device__ __forceinline__ float get_tagged(const StepParams& p, volatile Flags*
                                             unsigned id) {
     unsigned long long w = ld_tagged(src);
     PollClock clk;
+    // No back-off between polls: each poll already waits one L2 round trip, and a sleep only delays seeing
+    // the value (measured: 32-64 ns sleeps here and in load_input cost bf16 2.3 % of its tok/s).
     for (uint32_t it = 1; !tag_is(w, tag); ++it) {
-        __nanosleep(32);
         w = ld_tagged(src);
         if ((it & 15) == 0 && !clk.keep_going(p, fl, id)) break;
     }
@@ -1015,8 +1016,7 @@ __device__ bool load_input(ConsumerCtx& c, const unsigned long long* src, uint32
         }
     }
     PollClock clk;
-    for (uint32_t it = 1; pending != 0; ++it) {
-        __nanosleep(64);
+    for (uint32_t it = 1; pending != 0; ++it) {  // no back-off: see get_tagged
 #pragma unroll
         for (int i = 0; i < kStagePer; ++i) {
             if (pending & (1u << i)) {
