@@ -592,6 +592,20 @@ __device__ __forceinline__ float get_tagged(const StepParams& p, volatile Flags*
     return tag_value(w);
 }
 
+// Two elements of a tagged vector: both loads are in flight together and each is re-polled until current,
+// so the pair costs one memory round trip, not two.
+__device__ __forceinline__ float2 get_tagged_pair(const StepParams& p, volatile Flags* fl, const unsigned long long* a,
+                                                  const unsigned long long* b, uint32_t tag, unsigned id) {
+    unsigned long long wa = ld_tagged(a), wb = ld_tagged(b);
+    PollClock clk;
+    for (uint32_t it = 1; !(tag_is(wa, tag) && tag_is(wb, tag)); ++it) {
+        if (!tag_is(wa, tag)) wa = ld_tagged(a);
+        if (!tag_is(wb, tag)) wb = ld_tagged(b);
+        if ((it & 15) == 0 && !clk.keep_going(p, fl, id)) break;
+    }
+    return make_float2(tag_value(wa), tag_value(wb));
+}
+
 struct TaggedSrc {
     const StepParams* p;
     volatile Flags* fl;
@@ -599,6 +613,7 @@ struct TaggedSrc {
     uint32_t tag;
     unsigned id;
     __device__ __forceinline__ float operator()(int i) const { return get_tagged(*p, fl, v + i, tag, id); }
+    __device__ __forceinline__ float2 pair(int i, int j) const { return get_tagged_pair(*p, fl, v + i, v + j, tag, id); }
 };
 struct TaggedDst {
     unsigned long long* v;
@@ -769,14 +784,16 @@ __device__ __forceinline__ void load_query_insert_kv(const ConsumerCtx& c, int h
     if (tid < kGqa * kHd / 2) {
         const int g = tid >> 5, i = tid & 31;
         const int q = (h * kGqa + g) * kHd;
-        const float x0 = qkv(q + i), x1 = qkv(q + i + kHd / 2);
+        const float2 x = qkv.pair(q + i, q + i + kHd / 2);
+        const float x0 = x.x, x1 = x.y;
         const float cz = cs[i], sz = cs[kHd / 2 + i];
         sm.qs[g][i] = x0 * cz - x1 * sz;
         sm.qs[g][i + kHd / 2] = x1 * cz + x0 * sz;
     } else if (insert_new && tid < kGqa * kHd / 2 + kHd / 2) {
         const int i = tid - kGqa * kHd / 2;
         const int kp = (kNh + h) * kHd;
-        const float x0 = qkv(kp + i), x1 = qkv(kp + i + kHd / 2);
+        const float2 x = qkv.pair(kp + i, kp + i + kHd / 2);
+        const float x0 = x.x, x1 = x.y;
         const float cz = cs[i], sz = cs[kHd / 2 + i];
         const KV k0 = to_kv<KV>(x0 * cz - x1 * sz), k1 = to_kv<KV>(x1 * cz + x0 * sz);
         sm.kn[i] = k0;

@@ -67,6 +67,7 @@ struct AttSmem {
 struct PlainSrc {
     const float* p;
     __device__ __forceinline__ float operator()(int i) const { return __ldcg(p + i); }
+    __device__ __forceinline__ float2 pair(int i, int j) const { return make_float2(__ldcg(p + i), __ldcg(p + j)); }
 };
 struct PlainDst {
     float* p;
@@ -293,14 +294,16 @@ __device__ __forceinline__ void attend_head_span(Src qkv, int nh, int nkv, const
     if (tid < kGqa * kHd / 2) {
         const int g = tid >> 5, i = tid & 31;
         const int q = (h * kGqa + g) * kHd;
-        const float x0 = qkv(q + i), x1 = qkv(q + i + kHd / 2);
+        const float2 x = qkv.pair(q + i, q + i + kHd / 2);  // both loads in flight at once
+        const float x0 = x.x, x1 = x.y;
         const float c = cs[i], s = cs[kHd / 2 + i];
         sm.qs[g][i] = x0 * c - x1 * s;
         sm.qs[g][i + kHd / 2] = x1 * c + x0 * s;
     } else if (insert_new && tid < kGqa * kHd / 2 + kHd / 2) {
         const int i = tid - kGqa * kHd / 2;
         const int kp = (nh + h) * kHd;
-        const float x0 = qkv(kp + i), x1 = qkv(kp + i + kHd / 2);
+        const float2 x = qkv.pair(kp + i, kp + i + kHd / 2);
+        const float x0 = x.x, x1 = x.y;
         const float c = cs[i], s = cs[kHd / 2 + i];
         const KV k0 = to_kv<KV>(x0 * c - x1 * s), k1 = to_kv<KV>(x1 * c + x0 * s);
         sm.kn[i] = k0;
@@ -421,14 +424,16 @@ __device__ __forceinline__ void attend_head_pass(Src qkv, int nh, int nkv, const
     if (tid < kGqa * kHd / 2) {
         const int g = tid >> 5, i = tid & 31;
         const int q = (h * kGqa + g) * kHd;
-        const float x0 = qkv(q + i), x1 = qkv(q + i + kHd / 2);
+        const float2 x = qkv.pair(q + i, q + i + kHd / 2);  // both loads in flight at once
+        const float x0 = x.x, x1 = x.y;
         const float c = cs[i], s = cs[kHd / 2 + i];
         sm.qs[g][i] = x0 * c - x1 * s;
         sm.qs[g][i + kHd / 2] = x1 * c + x0 * s;
     } else if (tid < kGqa * kHd / 2 + kHd / 2) {
         const int i = tid - kGqa * kHd / 2;
         const int kp = (nh + h) * kHd;
-        const float x0 = qkv(kp + i), x1 = qkv(kp + i + kHd / 2);
+        const float2 x = qkv.pair(kp + i, kp + i + kHd / 2);
+        const float x0 = x.x, x1 = x.y;
         const float c = cs[i], s = cs[kHd / 2 + i];
         const KV k0 = to_kv<KV>(x0 * c - x1 * s), k1 = to_kv<KV>(x1 * c + x0 * s);
         sm.kn[i] = k0;
