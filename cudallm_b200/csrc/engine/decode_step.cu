@@ -561,9 +561,12 @@ __device__ __forceinline__ float tag_value(unsigned long long w) { return __uint
 // reported an error.
 struct PollClock {
     uint64_t t0 = 0;
+    uint32_t n = 0;
     __device__ __forceinline__ bool keep_going(const StepParams& p, volatile Flags* fl, unsigned id) {
         if (fl->abort) return false;
-        if (*reinterpret_cast<volatile unsigned*>(p.err) != 0) {
+        // Another CTA's failure (the global error word, one memory round trip during which the poll does not
+        // advance) is looked at on every 8th call only; the wall-clock limit on every call.
+        if ((++n & 7) == 0 && *reinterpret_cast<volatile unsigned*>(p.err) != 0) {
             fl->abort = 1;
             return false;
         }
