@@ -25,7 +25,8 @@ On one GPU (unless --quick) the line also carries the configured workloads whate
     tokens, and 128 greedy decode steps are timed at each context (bytes per token include the KV read at
     the step's context).
 
-Reported (one JSON line on rank 0): value = tok/s with weights resident; e2e = tok/s through the C ABI
+Reported (one JSON line on rank 0): value = tok/s with weights resident; load = wall time of creating the
+engine for each precision (reading and uploading the weights); e2e = tok/s through the C ABI
 when every step takes its token from the host and returns the next token to the host; roofline of the
 persistent decode-step kernel (algorithmic bytes = weight bytes + KV bytes read at the step's context,
 the reference's bytes-per-token count, cudallm_bench.cpp:82-87); cpu_baseline = the oracle's restatement
@@ -385,7 +386,9 @@ def run_ours(args) -> None:
     for dt in dtypes:
         path, digest = synth.ensure_model(dt, seed=0, max_seq_len=4096)
         barrier()
+        t_create = time.perf_counter()
         with Engine(path, kv_dtype=args.kv, device=local_rank) as eng:
+            load_s = time.perf_counter() - t_create  # cudallm_create: parse, read and upload every weight
             assert eng.decode_path == "persistent"
             weight_bytes = eng.config["weight_bytes"]
             if dt == args.dtype:
@@ -407,7 +410,7 @@ def run_ours(args) -> None:
                 t_sample = time_decode(eng, prompt, CONFIG_GEN, args.warmup, torch, lambda: None)
                 eng.set_sampling(0.0)
         results[dt] = {"t": t, "e": e, "clocks": clocks, "weight_bytes": weight_bytes, "t256": t256,
-                       "t_sample": t_sample}
+                       "t_sample": t_sample, "load_s": load_s}
 
     head = results[args.dtype]
     total_ms = max_over_ranks(head["t"]["total_ms"])
@@ -489,6 +492,10 @@ def run_ours(args) -> None:
             "precisions": extra,
             "long_context": long_context,
             "batched": batched,
+            "load": {dt: {"seconds": r["load_s"], "gb_per_s": r["weight_bytes"] / r["load_s"] / 1e9,
+                          "note": "cudallm_create wall time: header and table checks, the data region read into two "
+                                  "alternating pinned buffers while the other uploads; file in the host page cache"}
+                     for dt, r in results.items()},
         }
         print(json.dumps(line), flush=True)
     if world > 1:
