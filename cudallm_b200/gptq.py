@@ -279,6 +279,35 @@ def evaluate(ref: Path | str, candidates: list[Path | str], n_tokens: int = 64, 
     return {"tokens": n_tokens, "seed": seed, "results": res}
 
 
+def layer_errors(ref: Path | str, candidates: list[Path | str], layers: list[int], n_tokens: int = 256,
+                 seed: int = 11) -> dict:
+    """Relative output error ||(W - Wq) X|| / ||W X|| of every linear of the given layers, for each candidate
+    file's weights Wq, on inputs X that the reference (bf16) model produces for a seeded held-out sequence. A
+    local measure of quantisation quality that does not depend on how the whole network amplifies errors."""
+    torch.set_num_threads(os.cpu_count() or 1)
+    f = _File(ref)
+    hdr = f.hdr
+    tokens = np.random.default_rng(seed).integers(0, hdr["vocab_size"], n_tokens).tolist()
+    cos, sin = _rope_tables(f, n_tokens)
+    cands = [_File(c) for c in candidates]
+    res = {str(c): {} for c in candidates}
+    with torch.no_grad():
+        x = _embed(f, tokens)
+        for li in range(max(layers) + 1):
+            L = _Layer(f, li)
+            cap: dict = {}
+            x_next = _layer_forward(L, x, hdr, cos, sin, cap)
+            if li in layers:
+                for n in LINEARS:
+                    ref_out = cap[n] @ L.w[n].T
+                    for c, cf in zip(candidates, cands):
+                        wq = cf.mat(f"layers.{li}.{n}")
+                        res[str(c)][f"layers.{li}.{n}"] = float(torch.linalg.norm(cap[n] @ (L.w[n] - wq).T) /
+                                                                torch.linalg.norm(ref_out))
+            x = x_next
+    return {"tokens": n_tokens, "seed": seed, "results": res}
+
+
 def evaluate_engine(ref: Path | str, candidates: list[Path | str], n_tokens: int = 64, seed: int = 11) -> dict:
     """As evaluate, with every file run by this library's decode engine on the GPU (persistent step, fp16 KV):
     the quality the engine actually serves."""
