@@ -93,5 +93,8 @@ void launch_bw_write(uint4* dst, size_t n_uint4, int grid, cudaStream_t);
 void launch_bw_copy(const uint4* src, uint4* dst, size_t n_uint4, int grid, cudaStream_t);
 size_t bulk_probe_chunk_bytes();
 void launch_bw_bulk_read(const void* src, size_t bytes, unsigned* sink, unsigned* err, cudaStream_t);
+// Bulk copies of `bytes` (re-read `reps` times) through a 12-stage ring per SM with per-stage producer lanes
+// and 8 consumer warps; returns the bytes one launch moves. sink: num_sms() * 256 words.
+size_t launch_bw_bulk_ring(const void* src, size_t bytes, int reps, unsigned* sink, unsigned* err, cudaStream_t);
 
 }  // namespace cudallm

@@ -4,8 +4,9 @@
 //
 // Buffers of 1 GiB (8x the L2) are read, written and copied by the probes in kernels/hbm_probe.cu, 3
 // untimed and 20 timed launches each, with CUDA events; GB/s counts the bytes moved (a copy counts its read
-// and its write). Added key: bulk_read_gbps_best / _median, the read rate of 1-D bulk (TMA) copies into
-// shared memory, which is how the decode step streams its weights.
+// and its write). Added keys: bulk_read_gbps_best / _median, the read rate of 1-D bulk (TMA) copies into
+// shared memory, which is how the decode step streams its weights; bulk_read_l2_gbps_best / _median, the same
+// copies from a 48 MiB buffer resident in L2 (how fast the ring can refill from L2-prefetched weights).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -25,6 +26,7 @@ using cudallm::tools::Options;
 namespace {
 
 constexpr size_t kBytes = size_t{1} << 30;
+constexpr size_t kL2Bytes = size_t{48} << 20;
 constexpr int kUntimed = 3;
 constexpr int kTimed = 20;
 
@@ -83,6 +85,12 @@ int main(int argc, char** argv) {
         const Rate cp = time_rate([&] { launch_bw_copy(src, dst, n, grid, 0); }, 2.0 * kBytes);
         const Rate mc = time_rate([&] { CLLM_CUDA(cudaMemcpyAsync(dst, src, kBytes, cudaMemcpyDeviceToDevice, 0)); }, 2.0 * kBytes);
         const Rate bk = time_rate([&] { launch_bw_bulk_read(src, kBytes, sink, err, 0); }, kBytes);
+        // Bulk copies through a decode-step-like ring (12 stages per SM, per-stage producer lanes, consumers
+        // releasing stages at once) from a 48 MiB buffer that stays resident in L2, re-read 16 times per launch:
+        // the rate at which the weight ring can refill from L2-prefetched data.
+        const double l2_moved = static_cast<double>(16 * (kL2Bytes / bulk_probe_chunk_bytes()) / num_sms()) * num_sms() *
+                                bulk_probe_chunk_bytes();  // what launch_bw_bulk_ring reports it moves
+        const Rate bl2 = time_rate([&] { launch_bw_bulk_ring(src, kL2Bytes, 16, sink, err, 0); }, l2_moved);
         unsigned gave_up = 0;
         CLLM_CUDA(cudaMemcpy(&gave_up, err, sizeof(unsigned), cudaMemcpyDeviceToHost));
         if (gave_up) throw StateError("bulk read probe: a bounded wait gave up");
@@ -92,6 +100,7 @@ int main(int argc, char** argv) {
         std::printf("copy   best %.1f GB/s  median %.1f GB/s (read+write)\n", cp.best, cp.median);
         std::printf("memcpy best %.1f GB/s (read+write)\n", mc.best);
         std::printf("bulk   best %.1f GB/s  median %.1f GB/s (1-D bulk copies to shared memory)\n", bk.best, bk.median);
+        std::printf("bulk from L2 best %.1f GB/s  median %.1f GB/s (48 MiB buffer resident in L2)\n", bl2.best, bl2.median);
         if (opt.given("json")) {
             JsonValue j = JsonValue::object();
             j["tool"] = "cudallm_bandwidth";
@@ -104,6 +113,8 @@ int main(int argc, char** argv) {
             j["memcpy_d2d_gbps_best"] = mc.best;
             j["bulk_read_gbps_best"] = bk.best;
             j["bulk_read_gbps_median"] = bk.median;
+            j["bulk_read_l2_gbps_best"] = bl2.best;
+            j["bulk_read_l2_gbps_median"] = bl2.median;
             j["bytes"] = static_cast<unsigned long long>(kBytes);
             j["gpu_name"] = prop.name;
             if (!j.write_file(opt.str("json"))) throw std::runtime_error("cannot write " + opt.str("json"));

@@ -104,6 +104,8 @@ def test_bandwidth_as_bench_bandwidth_runs_it(tmp_path):
     assert res.returncode == 0, res.stderr
     d = json.loads(out.read_text())
     for k in ("read_gbps_best", "read_gbps_median", "write_gbps_best", "copy_gbps_best", "memcpy_d2d_gbps_best",
-              "bulk_read_gbps_best", "gpu_name"):
+              "bulk_read_gbps_best", "bulk_read_l2_gbps_best", "gpu_name"):
         assert k in d, k
     assert 3000 < d["read_gbps_best"] < 9000
+    # bulk copies from an L2-resident buffer outrun HBM (the weight ring's refill after a hand-off relies on it)
+    assert d["bulk_read_l2_gbps_best"] > d["bulk_read_gbps_best"]
